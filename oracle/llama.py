@@ -1,0 +1,118 @@
+"""Llama-family packed prefill, restated in fp32 on the CPU (test infrastructure only).
+
+Follows dan/models/llama.py of the reference:
+- RoPE inverse frequencies incl. "linear" and "llama3" scaling (llama.py:18-40),
+  angles in fp32 from integer positions, rotate-half (llama.py:43-45, 155-158);
+- pre-norm layer: x + attn(rms_norm(x)), then x + mlp(rms_norm(x)) (llama.py:115-117);
+- RMSNorm: normalise in fp32, then scale by the weight (fused.py:35-40);
+- attention: q/k/v projections, optional per-head q/k RMSNorm for qwen3
+  (llama.py:75-87), tree attention (oracle.attention), o projection;
+- MLP: down(silu(gate(x)) * up(x)) (llama.py:100-103, fused.py:59-61);
+- final norm, then label logits ``W_lm[label_ids] @ h`` in fp32 (llama.py:161-165).
+
+``state`` is a Hugging Face style fp32 state dict (oracle.weights).
+"""
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import attention
+
+
+def inv_frequencies(config, head_dim):
+    """llama.py:18-40: default / linear / llama3 scaled inverse frequencies (fp32)."""
+    params = config.get("rope_parameters") or config.get("rope_scaling") or {}
+    theta = float(params.get("rope_theta") or config.get("rope_theta") or 10000.0)
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    kind = params.get("rope_type") or params.get("type") or "default"
+    if kind == "default":
+        return inv.float()
+    if kind == "linear":
+        return (inv / params["factor"]).float()
+    if kind == "llama3":
+        factor, lo, hi = params["factor"], params["low_freq_factor"], params["high_freq_factor"]
+        old = params["original_max_position_embeddings"]
+        wavelen = 2 * math.pi / inv
+        smooth = (old / wavelen - lo) / (hi - lo)
+        scaled = torch.where(wavelen > old / lo, inv / factor, inv)
+        mid = (wavelen <= old / lo) & (wavelen >= old / hi)
+        return torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled).float()
+    raise NotImplementedError(kind)
+
+
+def rms_norm(x, w, eps):
+    """fused.py:35-40 in fp32."""
+    x = x.float()
+    return w.float() * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
+
+
+def rotate(x, cos, sin):
+    """Rotate-half RoPE (llama.py:43-45); x [..., D], cos/sin broadcastable [.., D]."""
+    a, b = x.chunk(2, dim=-1)
+    return x * cos + torch.cat((-b, a), dim=-1) * sin
+
+
+def rope_tables(positions, inv_freq):
+    """cos/sin [N, D] from integer positions (llama.py:155-158)."""
+    ang = positions.float()[:, None] * inv_freq[None, :]
+    ang = torch.cat((ang, ang), dim=-1)
+    return ang.cos(), ang.sin()
+
+
+def head_dim(config):
+    return config.get("head_dim") or config["hidden_size"] // config["num_attention_heads"]
+
+
+def hidden(state, config, ids, positions, segments):
+    """Final-normed hidden states [N, hidden] of a packed batch.
+
+    ``segments``: list of dicts ``{"start", "end", "branch", "past": {layer: (k, v)} or None,
+    "save": int}``; for segments with ``save`` the first ``save`` new tokens' (k, v) per
+    layer are stored into ``s["saved"]`` (attention.py:202-204)."""
+    c = config
+    eps = c["rms_norm_eps"]
+    d = head_dim(c)
+    nh, nkv = c["num_attention_heads"], c["num_key_value_heads"]
+    inv = inv_frequencies(c, d)
+    cos, sin = rope_tables(torch.as_tensor(positions), inv)
+    x = state["model.embed_tokens.weight"][torch.as_tensor(ids)].float()
+    n = x.shape[0]
+    for s in segments:
+        s["saved"] = {}
+    for i in range(c["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        h = rms_norm(x, state[p + "input_layernorm.weight"], eps)
+        q = (h @ state[p + "self_attn.q_proj.weight"].T).reshape(n, nh, d)
+        k = (h @ state[p + "self_attn.k_proj.weight"].T).reshape(n, nkv, d)
+        v = (h @ state[p + "self_attn.v_proj.weight"].T).reshape(n, nkv, d)
+        if c["model_type"] == "qwen3":
+            q = rms_norm(q, state[p + "self_attn.q_norm.weight"], eps)
+            k = rms_norm(k, state[p + "self_attn.k_norm.weight"], eps)
+        q = rotate(q, cos[:, None], sin[:, None]).transpose(0, 1)
+        k = rotate(k, cos[:, None], sin[:, None]).transpose(0, 1)
+        v = v.transpose(0, 1)
+        segs = []
+        for s in segments:
+            past = s["past"][i] if s.get("past") else None
+            if s.get("save"):
+                a = s["start"]
+                s["saved"][i] = (k[:, a:a + s["save"]].clone(), v[:, a:a + s["save"]].clone())
+            segs.append({"start": s["start"], "end": s["end"], "branch": s["branch"], "past": past})
+        o = attention.attend(q, k, v, segs)
+        o = o.transpose(0, 1).reshape(n, nh * d)
+        x = x + o @ state[p + "self_attn.o_proj.weight"].T
+        h = rms_norm(x, state[p + "post_attention_layernorm.weight"], eps)
+        g = h @ state[p + "mlp.gate_proj.weight"].T
+        u = h @ state[p + "mlp.up_proj.weight"].T
+        x = x + (F.silu(g) * u) @ state[p + "mlp.down_proj.weight"].T
+    return rms_norm(x, state["model.norm.weight"], eps)
+
+
+def lm_head(state):
+    return state.get("lm_head.weight", state["model.embed_tokens.weight"])
+
+
+def label_logits(state, h_row, label_ids):
+    """llama.py:163-165: fp32 logits of ``label_ids`` for one hidden row."""
+    return lm_head(state)[torch.as_tensor(label_ids)].float() @ h_row.float()
