@@ -1,0 +1,193 @@
+"""Tree attention for packed, prefill-only reads (host side of the CUDA kernel).
+
+Same model as the reference (dan/attention.py:1-30): requests are packed into
+one flat token sequence; each request is a *segment* whose new tokens are a
+trunk followed by one branch per question; a query sees a key when the key
+comes first and is trunk (cached past included) or in the same branch.
+
+The reference runs three flash varlen calls, gathers and an LSE merge per
+layer (attention.py:210-241). Here one kernel (``dan_tree_attention``) reads
+the packed q/k/v rows and the cached prefix pages in place, driven by a tile
+table built once per batch (``TreeLayout``) and shared by every layer.
+"""
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+
+BLOCK = 128  # query rows per tile, keys per block, tokens per pool page
+TILE_FIELDS = ("row0", "nrows", "seg_start", "past", "ppad", "split", "nblk_a", "blk_b0", "blk_b1", "page0", "q0v",
+               "pad")
+
+
+def tree_mask(branch):
+    """[N, N] boolean mask (True = attend) from per-token branch ids (0 = trunk) (attention.py:54-59)."""
+    n = branch.shape[0]
+    idx = torch.arange(n, device=branch.device)
+    causal = idx[None, :] <= idx[:, None]
+    return causal & ((branch[None, :] == 0) | (branch[None, :] == branch[:, None]))
+
+
+def branch_rows_mask(branch, trunk):
+    """The tree mask's rows for branch tokens only (== tree_mask(branch)[trunk:]) (attention.py:62-69)."""
+    n = branch.shape[0]
+    cols = torch.arange(n, device=branch.device)
+    rows = cols[trunk:]
+    own = (branch[None, :] == branch[trunk:, None]) & (cols[None, :] <= rows[:, None])
+    return (cols[None, :] < trunk) | own
+
+
+@dataclass
+class Segment:
+    """One request of a packed batch (attention.py:72-95). ``past`` is a prefix-pool
+    entry (its pages hold the cached keys/values of every layer) or None."""
+    start: int
+    end: int
+    trunk: int = 0
+    branches: list = field(default_factory=list)
+    past: object = None
+    save: int = 0
+    saved: dict = field(default_factory=dict)
+    past_len: int = 0
+    branch_ids: list = field(default_factory=list, repr=False)
+    device: str = "cpu"
+
+
+class Batch(list):
+    """The segments of one packed forward; caches the tile layout every attention
+    layer shares (``layout``) and the recurrent-layer layout (``recurrent``)."""
+
+    layout = None
+    recurrent = None
+
+
+def segment(start, branch, past=None, save=0, past_len=0, device="cpu"):
+    """A segment over new tokens with ``branch`` ids (trunk first, then each branch
+    contiguous), after ``past_len`` cached tokens (attention.py:114-126)."""
+    trunk = next((i for i, b in enumerate(branch) if b), len(branch))
+    spans, i = [], trunk
+    while i < len(branch):
+        j = i
+        while j < len(branch) and branch[j] == branch[i]:
+            j += 1
+        spans.append((start + i, start + j))
+        i = j
+    return Segment(start, start + len(branch), trunk, spans, past, save, past_len=past_len if past else 0,
+                   branch_ids=branch, device=device)
+
+
+def useful_pairs(segments):
+    """Visible (query, key) pairs: t(t+1)/2 + P t + sum_b (l_b (P + t) + l_b (l_b + 1) / 2) per segment."""
+    total = 0
+    for s in segments:
+        t, p = s.trunk, s.past_len
+        total += t * (t + 1) // 2 + p * t
+        for a, b in s.branches:
+            n = b - a
+            total += n * (p + t) + n * (n + 1) // 2
+    return total
+
+
+@dataclass
+class TreeLayout:
+    """Device tables of one packed batch for ``dan_tree_attention``."""
+    tiles: torch.Tensor  # int32 [n_tiles, 12], longest tiles first
+    row_own: torch.Tensor  # int32 [N]: packed row where each row's own run starts
+    pages: torch.Tensor  # int32: pool page of each cached 128-token block, per segment
+    n_tiles: int
+    n_rows: int
+    pairs: int  # visible (query, key) pairs (the useful work)
+    blocks: int  # key blocks the tiles visit (per head)
+
+    @classmethod
+    def build(cls, segments, n_rows, device):
+        own = np.zeros(max(n_rows, 1), dtype=np.int32)
+        pages, recs = [], []
+        for s in segments:
+            n = s.end - s.start
+            p = s.past_len
+            ppad = -(-p // BLOCK) * BLOCK
+            split = ppad + s.trunk
+            page0 = len(pages)
+            if p:
+                pg = list(s.past.pages)
+                if len(pg) * BLOCK < p:
+                    raise ValueError(f"segment at {s.start}: {len(pg)} pages cannot hold {p} cached tokens")
+                pages += pg[:ppad // BLOCK]
+            own[s.start:s.start + s.trunk] = s.start
+            for a, b in s.branches:
+                own[a:b] = a
+            for t0 in range(0, n, BLOCK):
+                nr = min(BLOCK, n - t0)
+                q0v, q1v = ppad + t0, ppad + t0 + nr - 1
+                nblk_a = -(-min(split, q1v + 1) // BLOCK)
+                if q1v >= split:  # the tile holds branch rows
+                    rb = max(t0, s.trunk)
+                    own_v = ppad + (int(own[s.start + rb]) - s.start)
+                    b0, b1 = max(own_v // BLOCK, nblk_a), q1v // BLOCK + 1
+                    if b0 >= b1:
+                        b0 = b1 = nblk_a
+                else:
+                    b0 = b1 = nblk_a
+                recs.append((s.start + t0, nr, s.start, p, ppad, split, nblk_a, b0, b1, page0, q0v, 0))
+        recs.sort(key=lambda r: -(r[6] + r[8] - r[7]))
+        tiles = np.asarray(recs, dtype=np.int32).reshape(-1, len(TILE_FIELDS))
+        blocks = int((tiles[:, 6] + tiles[:, 8] - tiles[:, 7]).sum()) if len(recs) else 0
+        pg = np.asarray(pages or [0], dtype=np.int32)
+        dev = torch.device(device)
+
+        def up(a):
+            t = torch.from_numpy(np.ascontiguousarray(a))
+            return t.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else t
+
+        return cls(up(tiles), up(own[:n_rows] if n_rows else own), up(pg), len(recs), n_rows,
+                   useful_pairs(segments), blocks)
+
+
+def layout_of(segments, n_rows, device):
+    lay = getattr(segments, "layout", None)
+    if lay is None or lay.n_rows != n_rows:
+        lay = TreeLayout.build(segments, n_rows, device)
+        if isinstance(segments, Batch):
+            segments.layout = lay
+    return lay
+
+
+def tree_attention(q, k, v, layout, out=None, pool=None, layer=0, scale=None):
+    """q: [N, H, D], k/v: [N, Hkv, D] (any row/head strides, unit stride in D) -> out [N, H, D] bf16.
+
+    ``pool``: the prefix pool holding cached keys/values (needed when any segment has a past)."""
+    n, h, d = q.shape
+    hkv = k.shape[1]
+    if out is None:
+        out = torch.empty(n, h, d, dtype=q.dtype, device=q.device)
+    if layout.n_tiles == 0:
+        return out
+    scale = d ** -0.5 if scale is None else scale
+    if pool is not None:
+        pk, pv = pool.k[layer], pool.v[layer]
+        pool_args = (_lib.ptr(pk), _lib.ptr(pv), pk.stride(0), pk.stride(1), pk.shape[0])
+    else:
+        pool_args = (None, None, 0, 0, 0)
+    _lib.call("dan_tree_attention", _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(k), k.stride(0), k.stride(1),
+              _lib.ptr(v), v.stride(0), v.stride(1), *pool_args, _lib.ptr(out), out.stride(0), out.stride(1), n, h,
+              hkv, d, _lib.ptr(layout.tiles), layout.n_tiles, _lib.ptr(layout.row_own), _lib.ptr(layout.pages),
+              float(scale), _lib.ptr(_lib.status_word(q.device)), _lib.stream(), work=4 * h * d * layout.pairs)
+    return out
+
+
+def attend(q, k, v, segments, layer, scale=None, pool=None):
+    """q: [H, N, D]; k, v: [Hkv, N, D] (rotary applied) -> [H, N, D] (attention.py:200-207).
+
+    Views of the packed [N, heads, D] projections are used in place (no copies).
+    Segments with ``save`` record their first ``save`` new tokens' k/v into
+    ``s.saved[layer]`` (as views; the pool stores them in pages)."""
+    for s in segments:
+        if s.save:
+            s.saved[layer] = (k[:, s.start:s.start + s.save], v[:, s.start:s.start + s.save])
+    lay = layout_of(segments, q.shape[1], q.device)
+    out = tree_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), lay, pool=pool, layer=layer,
+                         scale=scale)
+    return out.transpose(0, 1)

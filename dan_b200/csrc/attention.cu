@@ -1,0 +1,423 @@
+// Tree-masked attention for packed prefill reads, one kernel for the whole batch.
+//
+// Replaces the reference's three flash varlen calls + log-sum-exp merge + row
+// gathers (dan/attention.py:210-241; dense semantics 244-270). A query may see
+// a key when the key comes first and is trunk (cached past included) or in the
+// query's own branch (attention.py:6-13).
+//
+// Virtual key index space of a segment: [0, P) cached past keys (pool pages of
+// 128 tokens), [P, Ppad) padding (never visible, Ppad = P rounded up to 128),
+// then the segment's new tokens in packed order: trunk [Ppad, split), branches
+// [split, Ppad + len). A query row with virtual index qv whose own run starts
+// at ``own`` sees key v iff
+//     v <= qv  and  (v < split or v >= own)  and  (v < P or v >= Ppad).
+// Trunk rows have qv < split, so the middle clause is true for them; branch
+// rows see every trunk key and their own branch causally.
+//
+// Work unit: one 128-row query tile of one segment x one query head (CTA).
+// The host lists, per tile, the key blocks it needs: blocks [0, nblk_a) over
+// past + trunk, then [blk_b0, blk_b1) over the tile's own branch region;
+// every other block is fully masked and skipped. A block that is fully
+// visible to every row of the tile skips the mask arithmetic.
+//
+// Pipeline (warp-specialised, 192 threads):
+//   warp 0   TMA producer: Q once, then K_j / V_j into an NS-deep ring
+//            (packed rows of the current batch, or pool pages for past keys);
+//   warp 1   MMA issuer: S_j = Q K_j^T into TMEM buffer j&1 (SS MMA); after the
+//            softmax has written P_j (bf16) over S_j, O += P_j V_j with P read
+//            from TMEM (TS MMA) and V as an MN-major shared-memory operand;
+//   warps 2-5 softmax (one thread per query row): online softmax in the log2
+//            domain; O is rescaled lazily, only when a row max grows by more
+//            than 2^8 (exact: the same stale max is used for P and for l);
+//            then the epilogue O / l -> bf16.
+// TMEM: S0 [0,128), S1 [128,256), O [256, 256 + D).
+#include "common.cuh"
+
+namespace dan {
+namespace attn {
+
+constexpr int BM = 128, BN = 128;
+constexpr int THREADS = 192;
+constexpr int CHUNK = 128 * 128;  // bytes of one 64-column x 128-row bf16 box
+
+struct Tile {
+  int row0, nrows, seg_start, past, ppad, split, nblk_a, blk_b0, blk_b1, page0, q0v, pad;
+};
+
+struct Params {
+  __nv_bfloat16* out;
+  int64_t out_row, out_head;
+  const int* tiles;
+  const int* row_own;
+  const int* pages;
+  int n_rows, n_heads, n_kv_heads;
+  float scale_log2;
+  int32_t* status;
+};
+
+template <int D>
+struct Cfg {
+  static constexpr int NS = D <= 64 ? 3 : (D <= 128 ? 2 : 1);
+  static constexpr int CHUNKS = D / 64;
+  static constexpr int Q_BYTES = CHUNKS * CHUNK;
+  static constexpr int KV_BYTES = CHUNKS * CHUNK;
+  // At least 120 KB so two CTAs never share an SM: each allocates all 512 TMEM columns.
+  static constexpr int SMEM_USED = Q_BYTES + 2 * NS * KV_BYTES + 1024 + 512;
+  static constexpr int SMEM = SMEM_USED < 120 * 1024 ? 120 * 1024 : SMEM_USED;
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
+__global__ void __launch_bounds__(THREADS, 1)
+    tree_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tpk,
+                          const __grid_constant__ CUtensorMap tpv, Params p) {
+  using C = Cfg<D>;
+  constexpr int NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* sk = sq + C::Q_BYTES;
+  uint8_t* sv = sk + NS * C::KV_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + NS * C::KV_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* v_full = k_full + NS;
+  uint64_t* k_empty = v_full + NS;
+  uint64_t* v_empty = k_empty + NS;
+  uint64_t* s_full = v_empty + NS;   // [2]
+  uint64_t* p_full = s_full + 2;     // [2]
+  uint64_t* pv_done = p_full + 2;    // [2] indexed by block parity
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+
+  const int head = blockIdx.x;
+  const int kvh = head / (p.n_heads / p.n_kv_heads);
+  const Tile tile = reinterpret_cast<const Tile*>(p.tiles)[blockIdx.y];
+  const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+  const int warp = warp_id(), lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&pv_done[b], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem + 256;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < C::CHUNKS; ++c) tma_load_3d(sq + c * CHUNK, &tq, q_full, c * 64, head, tile.row0);
+      for (int j = 0; j < nblk; ++j) {
+        const int stage = j % NS;
+        const uint32_t ph = (j / NS) & 1;
+        const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
+        const int kb = b * BN;
+        const bool pool = kb < tile.ppad;
+        const int row = pool ? p.pages[tile.page0 + b] * BN : tile.seg_start + (kb - tile.ppad);
+        const CUtensorMap* mk = pool ? &tpk : &tk;
+        const CUtensorMap* mv = pool ? &tpv : &tv;
+        if (!mbar_wait(&k_empty[stage], ph ^ 1)) {
+          report(p.status, kTimeoutEmpty);
+          break;
+        }
+        mbar_expect_tx(&k_full[stage], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_3d(sk + stage * C::KV_BYTES + c * CHUNK, mk, &k_full[stage], c * 64, kvh, row);
+        if (!mbar_wait(&v_empty[stage], ph ^ 1)) {
+          report(p.status, kTimeoutEmpty);
+          break;
+        }
+        mbar_expect_tx(&v_full[stage], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_3d(sv + stage * C::KV_BYTES + c * CHUNK, mv, &v_full[stage], c * 64, kvh, row);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16(BM, D, false, true);
+      bool ok = mbar_wait(q_full, 0);
+      if (!ok) report(p.status, kTimeoutFull);
+      tc_fence_after();
+      const uint32_t q0 = smem_u32(sq);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i % NS;
+        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1)) {
+          report(p.status, kTimeoutSoftmax);
+          return false;
+        }
+        if (!mbar_wait(&v_full[st], (i / NS) & 1)) {
+          report(p.status, kTimeoutFull);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t v0 = smem_u32(sv + st * C::KV_BYTES);
+        const uint32_t pa = tmem + (i & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t db = desc_sw128(v0 + kk * 2048, CHUNK, 1024);
+          mma_f16_ts(tmem_o, pa + kk * 8, db, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&v_empty[st]);
+        mma_commit(&pv_done[i & 1]);
+        return true;
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int stage = j % NS;
+        if (j >= 2 && !mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1)) {
+          report(p.status, kTimeoutMma);
+          break;
+        }
+        if (!mbar_wait(&k_full[stage], (j / NS) & 1)) {
+          report(p.status, kTimeoutFull);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sk + stage * C::KV_BYTES);
+        const uint32_t sd = tmem + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_f16_ss(sd, desc_sw128(q0 + off, 16, 1024), desc_sw128(k0 + off, 16, 1024), idesc_qk, kk > 0);
+        }
+        mma_commit(&s_full[j & 1]);
+        mma_commit(&k_empty[stage]);
+        if (j >= 1 && !issue_pv(j - 1)) break;
+        if (j == nblk - 1) issue_pv(j);
+      }
+    }
+  } else {
+    // softmax + epilogue: thread <-> query row
+    const int sub = warp & 3;
+    const int r_in = sub * 32 + lane;
+    const int row = tile.row0 + r_in;
+    const bool valid = r_in < tile.nrows;
+    const int qv = tile.q0v + r_in;
+    const int own = valid ? tile.ppad + (p.row_own[row] - tile.seg_start) : 0;
+    const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
+      const int kb = b * BN;
+      const bool full = (kb + BN <= tile.past) ||
+                        (kb >= tile.ppad && kb + BN <= tile.split && kb + BN - 1 <= tile.q0v);
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
+        report(p.status, kTimeoutMma);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = tmem + lane_base + (j & 1) * 128;
+      uint32_t s[128];
+      tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+      tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+      tmem_wait_ld();
+      float mx = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const float x = __uint_as_float(s[c]) * p.scale_log2;
+          s[c] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const int v = kb + c;
+          const bool vis = v <= qv && (v < tile.split || v >= own) && (v < tile.past || v >= tile.ppad);
+          const float x = vis ? __uint_as_float(s[c]) * p.scale_log2 : -INFINITY;
+          s[c] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      bool rescale = false;
+      float alpha = 1.f;
+      if (m_new != -INFINITY) {
+        if (m == -INFINITY) {
+          m = m_new;  // nothing accumulated yet for this row: O row and l are zero
+        } else if (m_new > m + 8.f) {
+          alpha = fast_exp2(m - m_new);
+          m = m_new;
+          rescale = true;
+        }
+      }
+      const float mu = m == -INFINITY ? 0.f : m;
+      float sum = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = fast_exp2(__uint_as_float(s[2 * c]) - mu);
+        const float p1 = fast_exp2(__uint_as_float(s[2 * c + 1]) - mu);
+        sum += p0 + p1;
+        pk[c] = pack_bf16(p0, p1);
+      }
+      l = l * alpha + sum;
+      tmem_st32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_st32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      if (__any_sync(0xffffffffu, rescale) && j > 0) {
+        // O holds sum_{i<j} P_i V_i once PV_{j-1} completes; scale this warp's rows.
+        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          report(p.status, kTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem_o + lane_base + c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem_o + lane_base + c, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+    }
+    if (ok && nblk > 0) {
+      const int last = nblk - 1;
+      if (!mbar_wait(&pv_done[last & 1], (last >> 1) & 1)) {
+        report(p.status, kTimeoutMma);
+      } else {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem_o + lane_base + c, o);
+          tmem_wait_ld();
+          if (valid) {
+            uint32_t pkd[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tpk,
+           const CUtensorMap& tpv, const Params& p, int n_tiles, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    DAN_CUDA(cudaFuncSetAttribute(tree_attention_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
+    configured = true;
+  }
+  dim3 grid(p.n_heads, n_tiles);
+  tree_attention_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, p);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+static int rows_map(CUtensorMap* m, const void* base, int64_t row_stride, int64_t head_stride, int heads, int rows,
+                    int d) {
+  uint64_t dims[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(heads), static_cast<uint64_t>(rows)};
+  uint64_t strides[2] = {static_cast<uint64_t>(head_stride) * 2, static_cast<uint64_t>(row_stride) * 2};
+  uint32_t box[3] = {64, 1, 128};
+  return make_tmap(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace attn
+}  // namespace dan
+
+using namespace dan;
+
+DAN_API int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, const void* k, int64_t k_row,
+                               int64_t k_head, const void* v, int64_t v_row, int64_t v_head, const void* k_pool,
+                               const void* v_pool, int64_t pool_row, int64_t pool_head, int pool_rows, void* out,
+                               int64_t out_row, int64_t out_head, int n_rows, int n_heads, int n_kv_heads,
+                               int head_dim, const int* tiles, int n_tiles, const int* row_own, const int* pages,
+                               float scale, int32_t* status, void* stream) {
+  DAN_REQUIRE(n_rows > 0 && n_tiles >= 0, "tree_attention: n_rows=%d n_tiles=%d", n_rows, n_tiles);
+  DAN_REQUIRE(n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0,
+              "tree_attention: %d query heads are not a multiple of %d kv heads", n_heads, n_kv_heads);
+  DAN_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, "tree_attention: head_dim %d unsupported",
+              head_dim);
+  DAN_REQUIRE(n_tiles < 65536, "tree_attention: %d tiles exceed the grid limit", n_tiles);
+  DAN_REQUIRE(out_head % 8 == 0 && out_row % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0,
+              "tree_attention: output must be 16-byte aligned with strides that are multiples of 8");
+  if (n_tiles == 0) return 0;
+  CUtensorMap tq, tk, tv, tpk, tpv;
+  int rc;
+  if ((rc = attn::rows_map(&tq, q, q_row, q_head, n_heads, n_rows, head_dim))) return rc;
+  if ((rc = attn::rows_map(&tk, k, k_row, k_head, n_kv_heads, n_rows, head_dim))) return rc;
+  if ((rc = attn::rows_map(&tv, v, v_row, v_head, n_kv_heads, n_rows, head_dim))) return rc;
+  if (k_pool && v_pool && pool_rows > 0) {
+    if ((rc = attn::rows_map(&tpk, k_pool, pool_row, pool_head, n_kv_heads, pool_rows, head_dim))) return rc;
+    if ((rc = attn::rows_map(&tpv, v_pool, pool_row, pool_head, n_kv_heads, pool_rows, head_dim))) return rc;
+  } else {
+    tpk = tk;
+    tpv = tv;
+  }
+  attn::Params p{};
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_row = out_row;
+  p.out_head = out_head;
+  p.tiles = tiles;
+  p.row_own = row_own;
+  p.pages = pages;
+  p.n_rows = n_rows;
+  p.n_heads = n_heads;
+  p.n_kv_heads = n_kv_heads;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (head_dim) {
+    case 64:
+      return attn::launch<64>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
+    case 128:
+      return attn::launch<128>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
+    default:
+      return attn::launch<256>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
+  }
+}

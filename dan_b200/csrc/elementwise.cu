@@ -1,0 +1,389 @@
+// Memory-bound kernels of the read path: embedding gather, RMSNorm (Llama and
+// zero-centred, optionally fused with per-row e4m3 quantisation), RoPE, per-row
+// e4m3 quantisation, sigmoid output gate, prefix K/V page stores, and the fused
+// final-norm + label gather-GEMV + per-question softmax readout.
+//
+// All use 128-bit vector loads where rows allow it, one warp per row for the
+// row reductions, and compute in fp32 with the reference's rounding points.
+#include "common.cuh"
+
+namespace dan {
+namespace ew {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------- embedding
+__global__ void embed_kernel(const int64_t* ids, const __nv_bfloat16* table, int64_t ldt, int64_t vocab,
+                             __nv_bfloat16* out, int64_t ldo, int rows, int cols, int32_t* status) {
+  const int row = blockIdx.x;
+  int64_t id = ids[row];
+  if (id < 0 || id >= vocab) {
+    report(status, kBadIndex);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * ldt);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * ldo);
+  for (int i = threadIdx.x; i < cols / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// ---------------------------------------------------------------- RMSNorm
+// Rows are addressed as (outer, inner): element (r, c) of the logical [rows, cols]
+// matrix is at base + (r / inner) * ld_outer + (r % inner) * ld_inner + c, so
+// per-head norms run in place on a packed q/k/v buffer.
+// mode 0 (Llama, fused.py:35-40):  y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps)))
+// mode 1 (zero-centred, fused.py:43-48): y = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))
+// With ``q8`` set, y is also quantised per row to e4m3 (fused.py:85-91):
+//   scale = max(amax |y|, 1e-12) / 448, q = e4m3(y / scale).
+template <int VEC>  // bf16 elements per lane per step (8 = one 16-byte load)
+__global__ void rms_norm_kernel(const __nv_bfloat16* x, int64_t x_outer, int64_t x_inner, int inner,
+                                const __nv_bfloat16* w, float eps, int mode, __nv_bfloat16* y, int64_t y_outer,
+                                int64_t y_inner, uint8_t* q8, int64_t ldq, float* q8_scale, int rows, int cols) {
+  constexpr int MAXV = 8192 / (32 * 8);  // supports cols <= 8192
+  const int warps = blockDim.x / 32;
+  const int r = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(r / inner) * x_outer + static_cast<int64_t>(r % inner) * x_inner;
+  __nv_bfloat16* yr = y + static_cast<int64_t>(r / inner) * y_outer + static_cast<int64_t>(r % inner) * y_inner;
+  const int nvec = cols / 8;
+  uint4 buf[MAXV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nvec) {
+      buf[i] = reinterpret_cast<const uint4*>(xr)[v];
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&buf[i]);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float f = __bfloat162float(e[t]);
+        ss += f * f;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / cols + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nvec) {
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&buf[i]);
+      const uint4 wv = reinterpret_cast<const uint4*>(w)[v];
+      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float f = __bfloat162float(e[t]) * inv;
+        float o;
+        if (mode == 0)
+          o = __bfloat162float(we[t]) * bf16_round(f);
+        else
+          o = f * (1.f + __bfloat162float(we[t]));
+        e[t] = __float2bfloat16_rn(o);
+        amax = fmaxf(amax, fabsf(__bfloat162float(e[t])));
+      }
+      if (y) reinterpret_cast<uint4*>(yr)[v] = buf[i];
+    }
+  }
+  if (q8) {
+    amax = warp_max(amax);
+    const float scale = fmaxf(amax, 1e-12f) / 448.f;
+    uint8_t* qr = q8 + static_cast<int64_t>(r) * ldq;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int v = lane + 32 * i;
+      if (v < nvec) {
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&buf[i]);
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const __nv_fp8_e4m3 c(__bfloat162float(e[t]) / scale);
+          const uint32_t b = *reinterpret_cast<const uint8_t*>(&c);
+          if (t < 4)
+            lo |= b << (8 * t);
+          else
+            hi |= b << (8 * (t - 4));
+        }
+        reinterpret_cast<uint2*>(qr)[v] = make_uint2(lo, hi);
+      }
+    }
+    if (lane == 0) q8_scale[r] = scale;
+  }
+}
+
+// ---------------------------------------------------------------- per-row e4m3
+// scale = max(amax |x|, 1e-12) / 448 ; q = e4m3(x / scale)   (fused.py:85-91, quant.py:26-33)
+__global__ void quant_rows_kernel(const __nv_bfloat16* x, int64_t ldx, uint8_t* q, int64_t ldq, float* scale,
+                                  int rows, int cols) {
+  const int r = blockIdx.x;
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(r) * ldx;
+  __shared__ float red[32];
+  float amax = 0.f;
+  for (int c = threadIdx.x * 8; c < cols; c += blockDim.x * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) amax = fmaxf(amax, fabsf(__bfloat162float(e[t])));
+  }
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float a = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    a = warp_max(a);
+    if (threadIdx.x == 0) red[0] = fmaxf(a, 1e-12f) / 448.f;
+  }
+  __syncthreads();
+  const float s = red[0];
+  if (threadIdx.x == 0) scale[r] = s;
+  uint8_t* qr = q + static_cast<int64_t>(r) * ldq;
+  for (int c = threadIdx.x * 8; c < cols; c += blockDim.x * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const __nv_fp8_e4m3 cv(__bfloat162float(e[t]) / s);
+      const uint32_t b = *reinterpret_cast<const uint8_t*>(&cv);
+      if (t < 4)
+        lo |= b << (8 * t);
+      else
+        hi |= b << (8 * (t - 4));
+    }
+    *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
+  }
+}
+
+// ---------------------------------------------------------------- RoPE
+// Rotate-half on the first ``rot`` dims of each of ``heads`` heads of each row, in place
+// (llama.py:43-45, fused.py:69-76). cos/sin are computed in fp32 from integer positions
+// and rounded to bf16 as the reference does (llama.py:155-158); the products and the sum
+// are rounded to bf16 at the reference's points.
+__global__ void rope_kernel(__nv_bfloat16* x, int64_t ld_row, int64_t ld_head, int heads, int rot,
+                            const int64_t* pos, const float* inv_freq, int rows) {
+  const int half = rot / 2;
+  const int per_row = heads * half;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(rows) * per_row) return;
+  const int r = static_cast<int>(idx / per_row);
+  const int rem = static_cast<int>(idx % per_row);
+  const int h = rem / half, i = rem % half;
+  const float ang = static_cast<float>(pos[r]) * inv_freq[i];
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  const float c = bf16_round(cs), s = bf16_round(sn);
+  __nv_bfloat16* p = x + static_cast<int64_t>(r) * ld_row + static_cast<int64_t>(h) * ld_head;
+  const float a = __bfloat162float(p[i]), b = __bfloat162float(p[i + half]);
+  p[i] = __float2bfloat16_rn(bf16_round(a * c) + bf16_round(-b * s));
+  p[i + half] = __float2bfloat16_rn(bf16_round(b * c) + bf16_round(a * s));
+}
+
+// ---------------------------------------------------------------- sigmoid gate
+// o[r, j] = bf16(o[r, j] * sigmoid(g[r, j]))  (fused.py:64-66); g row stride may differ.
+__global__ void sigmoid_gate_kernel(__nv_bfloat16* o, int64_t ldo, const __nv_bfloat16* g, int64_t ldg,
+                                    int64_t g_head_stride, int head_dim, int rows, int cols) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(rows) * cols) return;
+  const int r = static_cast<int>(idx / cols), c = static_cast<int>(idx % cols);
+  const float gv = __bfloat162float(g[static_cast<int64_t>(r) * ldg + (c / head_dim) * g_head_stride + c % head_dim]);
+  const float ov = __bfloat162float(o[static_cast<int64_t>(r) * ldo + c]);
+  o[static_cast<int64_t>(r) * ldo + c] = __float2bfloat16_rn(ov * (1.f / (1.f + __expf(-gv))));
+}
+
+// ---------------------------------------------------------------- prefix K/V page store
+// Copies rows src_rows[i] of k/v ([rows, heads, d] strided) to pool rows dst_rows[i].
+__global__ void kv_store_kernel(const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t ld_row, int64_t ld_head,
+                                __nv_bfloat16* pk, __nv_bfloat16* pv, int64_t pld_row, int64_t pld_head,
+                                const int* src_rows, const int* dst_rows, int count, int heads, int d) {
+  const int i = blockIdx.x;
+  if (i >= count) return;
+  const int64_t s = src_rows[i], t = dst_rows[i];
+  const int vec = d / 8;
+  for (int e = threadIdx.x; e < heads * vec; e += blockDim.x) {
+    const int h = e / vec, c = (e % vec) * 8;
+    *reinterpret_cast<uint4*>(pk + t * pld_row + h * pld_head + c) =
+        *reinterpret_cast<const uint4*>(k + s * ld_row + h * ld_head + c);
+    *reinterpret_cast<uint4*>(pv + t * pld_row + h * pld_head + c) =
+        *reinterpret_cast<const uint4*>(v + s * ld_row + h * ld_head + c);
+  }
+}
+
+// ---------------------------------------------------------------- label readout
+// One CTA per question: final norm of its read row (the norm is row-wise, so
+// norming only the read rows equals norming all rows then gathering,
+// llama.py:161 + runner.py:73), logits = W_lm[label_ids] @ h in fp32
+// (llama.py:163-165), then the question's softmax (readout.py:13-17).
+__global__ void readout_kernel(const __nv_bfloat16* h, int64_t ldh, const int* read_rows, const __nv_bfloat16* nw,
+                               float eps, int mode, const __nv_bfloat16* wlm, int64_t ldw, int64_t vocab,
+                               const int* label_ids, const int* offsets, int hidden, float* logits, float* probs,
+                               int32_t* status) {
+  extern __shared__ float sh[];  // [hidden] normed row, then [labels] logits
+  __shared__ float red[32];
+  const int q = blockIdx.x;
+  const int nwarps = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __nv_bfloat16* x = h + static_cast<int64_t>(read_rows[q]) * ldh;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    const float f = __bfloat162float(x[c]);
+    sh[c] = f;
+    ss += f * f;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < nwarps ? red[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) red[0] = rsqrtf(t / hidden + eps);
+  }
+  __syncthreads();
+  const float inv = red[0];
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    const float f = sh[c] * inv;
+    const float w = __bfloat162float(nw[c]);
+    sh[c] = bf16_round(mode == 0 ? w * bf16_round(f) : f * (1.f + w));
+  }
+  __syncthreads();
+  const int a = offsets[q], b = offsets[q + 1];
+  float* lg = sh + hidden;
+  for (int j = a + warp; j < b; j += nwarps) {
+    int64_t id = label_ids[j];
+    if (id < 0 || id >= vocab) {
+      report(status, kBadIndex);
+      id = 0;
+    }
+    const __nv_bfloat16* wr = wlm + id * ldw;
+    float acc = 0.f;
+    for (int c = lane * 8; c < hidden; c += 256) {
+      const uint4 v = *reinterpret_cast<const uint4*>(wr + c);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc += __bfloat162float(e[t]) * sh[c + t];
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) lg[j - a] = acc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float mx = -INFINITY;
+    for (int j = lane; j < b - a; j += 32) mx = fmaxf(mx, lg[j]);
+    mx = warp_max(mx);
+    float z = 0.f;
+    for (int j = lane; j < b - a; j += 32) z += expf(lg[j] - mx);
+    z = warp_sum(z);
+    for (int j = lane; j < b - a; j += 32) {
+      logits[a + j] = lg[j];
+      probs[a + j] = expf(lg[j] - mx) / z;
+    }
+  }
+}
+
+}  // namespace ew
+}  // namespace dan
+
+using namespace dan;
+
+DAN_API int dan_embed(const int64_t* ids, const void* table, int64_t ldt, int64_t vocab, void* out, int64_t ldo,
+                      int rows, int cols, int32_t* status, void* stream) {
+  DAN_REQUIRE(rows >= 0 && cols > 0 && cols % 8 == 0 && ldt % 8 == 0 && ldo % 8 == 0,
+              "embed: cols/ld must be multiples of 8");
+  if (!rows) return 0;
+  ew::embed_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<const __nv_bfloat16*>(table), ldt, vocab, static_cast<__nv_bfloat16*>(out), ldo, rows, cols,
+      status);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+DAN_API int dan_rms_norm(const void* x, int64_t x_outer, int64_t x_inner, int inner, const void* w, float eps,
+                         int mode, void* y, int64_t y_outer, int64_t y_inner, void* q8, int64_t ldq, float* q8_scale,
+                         int rows, int cols, void* stream) {
+  DAN_REQUIRE(cols > 0 && cols % 8 == 0 && cols <= 8192, "rms_norm: cols=%d must be a multiple of 8 <= 8192", cols);
+  DAN_REQUIRE(inner > 0 && (mode == 0 || mode == 1), "rms_norm: bad inner=%d or mode=%d", inner, mode);
+  DAN_REQUIRE(x_outer % 8 == 0 && x_inner % 8 == 0 && y_outer % 8 == 0 && y_inner % 8 == 0,
+              "rms_norm: strides must be multiples of 8");
+  DAN_REQUIRE(y || q8, "rms_norm: no output");
+  if (!rows) return 0;
+  const int warps = 4;
+  ew::rms_norm_kernel<8><<<(rows + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), x_outer, x_inner, inner, static_cast<const __nv_bfloat16*>(w), eps, mode,
+      static_cast<__nv_bfloat16*>(y), y_outer, y_inner, static_cast<uint8_t*>(q8), ldq, q8_scale, rows, cols);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+DAN_API int dan_quantize_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, float* scale, int rows, int cols,
+                              void* stream) {
+  DAN_REQUIRE(cols > 0 && cols % 8 == 0 && ldx % 8 == 0 && ldq % 16 == 0, "quantize_e4m3: bad cols/ld");
+  if (!rows) return 0;
+  ew::quant_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<uint8_t*>(q), ldq, scale, rows, cols);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+DAN_API int dan_rope(void* x, int64_t ld_row, int64_t ld_head, int heads, int head_dim, int rot, const int64_t* pos,
+                     const float* inv_freq, int rows, void* stream) {
+  DAN_REQUIRE(rot > 0 && rot % 2 == 0 && rot <= head_dim, "rope: rot=%d head_dim=%d", rot, head_dim);
+  if (!rows || !heads) return 0;
+  const int64_t n = static_cast<int64_t>(rows) * heads * (rot / 2);
+  ew::rope_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(x), ld_row, ld_head, heads, rot, pos, inv_freq, rows);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+DAN_API int dan_sigmoid_gate(void* o, int64_t ldo, const void* g, int64_t ldg, int64_t g_head_stride, int head_dim,
+                             int rows, int cols, void* stream) {
+  if (!rows) return 0;
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  ew::sigmoid_gate_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(g), ldg, g_head_stride, head_dim, rows,
+      cols);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+DAN_API int dan_kv_store(const void* k, const void* v, int64_t ld_row, int64_t ld_head, void* pool_k, void* pool_v,
+                         int64_t pool_row, int64_t pool_head, const int* src_rows, const int* dst_rows, int count,
+                         int heads, int head_dim, void* stream) {
+  DAN_REQUIRE(head_dim % 8 == 0 && ld_row % 8 == 0 && ld_head % 8 == 0 && pool_row % 8 == 0 && pool_head % 8 == 0,
+              "kv_store: strides must be multiples of 8");
+  if (!count) return 0;
+  ew::kv_store_kernel<<<count, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), ld_row, ld_head,
+      static_cast<__nv_bfloat16*>(pool_k), static_cast<__nv_bfloat16*>(pool_v), pool_row, pool_head, src_rows,
+      dst_rows, count, heads, head_dim);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+DAN_API int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, const void* norm_w, float eps,
+                              int mode, const void* w_lm, int64_t ldw, int64_t vocab, const int* label_ids,
+                              const int* offsets, int n_questions, int hidden, int max_labels, float* logits,
+                              float* probs, int32_t* status, void* stream) {
+  DAN_REQUIRE(hidden > 0 && hidden % 8 == 0 && ldw % 8 == 0, "label_readout: hidden/ldw must be multiples of 8");
+  DAN_REQUIRE(max_labels >= 0 && max_labels <= 4096, "label_readout: at most 4096 labels per question");
+  if (!n_questions) return 0;
+  const size_t smem = (static_cast<size_t>(hidden) + max_labels) * sizeof(float);
+  DAN_REQUIRE(smem <= 200 * 1024, "label_readout: hidden %d too large", hidden);
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    DAN_CUDA(cudaFuncSetAttribute(ew::readout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured = smem;
+  }
+  ew::readout_kernel<<<n_questions, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(h), ldh, read_rows, static_cast<const __nv_bfloat16*>(norm_w), eps, mode,
+      static_cast<const __nv_bfloat16*>(w_lm), ldw, vocab, label_ids, offsets, hidden, logits, probs, status);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}

@@ -1,0 +1,339 @@
+// Dense projections on the 5th-generation tensor cores: C = A * W^T.
+//
+// A [M, K] (activations, K-major) and W [N, K] (nn.Linear weight, K-major) are
+// staged by TMA into a 4-deep ring of 128-byte-swizzled shared-memory tiles;
+// one elected thread issues tcgen05.mma (128 x 256 x 16 bf16, or 128 x 256 x 32
+// e4m3) accumulating in TMEM; four epilogue warps read the fp32 accumulator
+// back with tcgen05.ld and apply the fused epilogue. The kernel is persistent
+// (one CTA per SM, tiles strided by the grid) and double-buffers the TMEM
+// accumulator (2 x 256 columns) so the epilogue of tile i overlaps the main
+// loop of tile i+1.
+//
+// Epilogues (replacing separate passes of the reference):
+//   store     C = bf16(acc [+ bias])                          (nn.Linear, llama.py:78,102)
+//   residual  C = bf16(R + bf16(acc [+ bias]))                (x + o_proj(...), llama.py:116-117)
+//   swiglu    W rows interleaved in 128-row blocks [gate | up]; C[:, j] = bf16(silu(g) * u)
+//             with g, u the bf16-rounded projections          (fused.py:59-61, llama.py:100-103)
+// The e4m3 variant multiplies acc by a_scale[row] * w_scale[col] first
+// (torch._scaled_mm with row-wise scales, quant.py:37-42).
+#include "common.cuh"
+
+namespace dan {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256;
+constexpr int KBYTES = 128;  // bytes of K per stage (one 128 B swizzle row)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * KBYTES;
+constexpr int B_BYTES = BN * KBYTES;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+enum Epilogue { kStore = 0, kResidual = 1, kSwiglu = 2 };
+
+struct Params {
+  __nv_bfloat16* c;
+  int64_t ldc;
+  const __nv_bfloat16* resid;
+  int64_t ldr;
+  const __nv_bfloat16* bias;
+  const float* a_scale;  // e4m3 only: per row of A
+  const float* w_scale;  // e4m3 only: per row of W (output channel)
+  int m, n, k;
+  int tiles_m, tiles_n;
+  int epilogue;
+  int32_t* status;
+};
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+template <bool FP8>
+__device__ __forceinline__ void store_chunk(const Params& p, int row, int col, int cols_out, const float* v) {
+  // v: 32 consecutive output values of ``row`` starting at ``col``.
+  if (row >= p.m) return;
+  __nv_bfloat16* dst = p.c + static_cast<int64_t>(row) * p.ldc + col;
+  uint32_t packed[16];
+  if (p.epilogue == kResidual) {
+    const __nv_bfloat16* r = p.resid + static_cast<int64_t>(row) * p.ldr + col;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float a = 0.f, b = 0.f;
+      if (col + 2 * i < cols_out) a = __bfloat162float(r[2 * i]);
+      if (col + 2 * i + 1 < cols_out) b = __bfloat162float(r[2 * i + 1]);
+      packed[i] = pack_bf16(a + bf16_round(v[2 * i]), b + bf16_round(v[2 * i + 1]));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) packed[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+  }
+  const bool full = col + 32 <= cols_out && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+  if (full) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+  } else {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(packed);
+    for (int i = 0; i < 32 && col + i < cols_out; ++i) dst[i] = h[i];
+  }
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int k_iters = (p.k * (FP8 ? 1 : 2) + KBYTES - 1) / KBYTES;
+  constexpr int KELEM = FP8 ? KBYTES : KBYTES / 2;  // elements of K per stage
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&ta);
+      tma_prefetch_desc(&tb);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int tm = t % p.tiles_m, tn = t / p.tiles_m;
+        for (int ki = 0; ki < k_iters; ++ki) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            report(p.status, kTimeoutEmpty);
+            goto done;
+          }
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(sa + stage * A_BYTES, &ta, &full[stage], ki * KELEM, tm * BM);
+          tma_load_2d(sb + stage * B_BYTES, &tb, &full[stage], ki * KELEM, tn * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = FP8 ? idesc_e4m3(BM, BN) : idesc_bf16(BM, BN, false, false);
+      int stage = 0, buf = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty[buf], acc_phase ^ 1)) {
+          report(p.status, kTimeoutEmpty);
+          goto done;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int ki = 0; ki < k_iters; ++ki) {
+          if (!mbar_wait(&full[stage], phase)) {
+            report(p.status, kTimeoutFull);
+            goto done;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + stage * A_BYTES), b0 = smem_u32(sb + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t da = desc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t db = desc_sw128(b0 + kk * 32, 16, 1024);
+            if (FP8)
+              mma_f8_ss(d, da, db, idesc, (ki | kk) != 0);
+            else
+              mma_f16_ss(d, da, db, idesc, (ki | kk) != 0);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit(&tfull[buf]);
+        buf ^= 1;
+        if (buf == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    const int sub = warp & 3;  // TMEM sub-partition this warp may read
+    const int r_in = sub * 32 + lane;
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    const int cols_out = p.epilogue == kSwiglu ? p.n / 2 : p.n;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const int tm = t % p.tiles_m, tn = t / p.tiles_m;
+      if (!mbar_wait(&tfull[buf], acc_phase)) {
+        report(p.status, kTimeoutMma);
+        break;
+      }
+      tc_fence_after();
+      const int row = tm * BM + r_in;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
+      const float as = (FP8 && row < p.m) ? p.a_scale[row] : 1.f;
+      if (p.epilogue == kSwiglu) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(taddr + c, g);
+          tmem_ld32(taddr + BN / 2 + c, u);
+          tmem_wait_ld();
+          float v[32];
+          const int gcol = tn * BN + c, ucol = tn * BN + BN / 2 + c;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+            if (FP8) {
+              gv *= as * (gcol + i < p.n ? p.w_scale[gcol + i] : 0.f);
+              uv *= as * (ucol + i < p.n ? p.w_scale[ucol + i] : 0.f);
+            }
+            if (p.bias) {
+              gv += gcol + i < p.n ? __bfloat162float(p.bias[gcol + i]) : 0.f;
+              uv += ucol + i < p.n ? __bfloat162float(p.bias[ucol + i]) : 0.f;
+            }
+            gv = bf16_round(gv);
+            uv = bf16_round(uv);
+            v[i] = silu(gv) * uv;
+          }
+          store_chunk<FP8>(p, row, tn * (BN / 2) + c, cols_out, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          const int col = tn * BN + c;
+          if (col >= p.n) break;
+          uint32_t r[32];
+          tmem_ld32(taddr + c, r);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float x = __uint_as_float(r[i]);
+            if (FP8) x *= as * (col + i < p.n ? p.w_scale[col + i] : 0.f);
+            if (p.bias && col + i < p.n) x += __bfloat162float(p.bias[col + i]);
+            v[i] = x;
+          }
+          store_chunk<FP8>(p, row, col, cols_out, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      buf ^= 1;
+      if (buf == 0) acc_phase ^= 1;
+    }
+  }
+done:
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool FP8>
+int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cudaStream_t stream) {
+  const int esize = FP8 ? 1 : 2;
+  DAN_REQUIRE(p.m > 0 && p.n > 0 && p.k > 0, "gemm: empty problem m=%d n=%d k=%d", p.m, p.n, p.k);
+  DAN_REQUIRE((p.k * esize) % 16 == 0, "gemm: k=%d must make 16-byte rows", p.k);
+  DAN_REQUIRE((lda * esize) % 16 == 0 && (ldw * esize) % 16 == 0, "gemm: lda/ldw must be 16-byte multiples");
+  DAN_REQUIRE(lda >= p.k && ldw >= p.k, "gemm: leading dimensions smaller than k");
+  DAN_REQUIRE(p.epilogue >= 0 && p.epilogue <= 2, "gemm: unknown epilogue %d", p.epilogue);
+  DAN_REQUIRE(p.epilogue != kSwiglu || p.n % BN == 0, "gemm: swiglu needs n %% 256 == 0 (got %d)", p.n);
+  DAN_REQUIRE(p.epilogue != kResidual || p.resid != nullptr, "gemm: residual epilogue without a residual");
+  DAN_REQUIRE(!FP8 || (p.a_scale && p.w_scale), "gemm: e4m3 needs a_scale and w_scale");
+  CUtensorMap ta, tb;
+  const CUtensorMapDataType dt = FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint32_t kbox = KBYTES / esize;
+  {
+    uint64_t dims[2] = {static_cast<uint64_t>(p.k), static_cast<uint64_t>(p.m)};
+    uint64_t strides[1] = {static_cast<uint64_t>(lda) * esize};
+    uint32_t box[2] = {kbox, BM};
+    int rc = make_tmap(&ta, a, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    uint64_t dims[2] = {static_cast<uint64_t>(p.k), static_cast<uint64_t>(p.n)};
+    uint64_t strides[1] = {static_cast<uint64_t>(ldw) * esize};
+    uint32_t box[2] = {kbox, BN};
+    int rc = make_tmap(&tb, w, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  p.tiles_m = (p.m + BM - 1) / BM;
+  p.tiles_n = (p.n + BN - 1) / BN;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  static bool configured[2] = {false, false};
+  if (!configured[FP8]) {
+    DAN_CUDA(cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    configured[FP8] = true;
+  }
+  gemm_kernel<FP8><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // namespace gemm
+}  // namespace dan
+
+using namespace dan;
+
+DAN_API int dan_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
+                          const void* resid, int64_t ldr, const void* bias, int m, int n, int k, int epilogue,
+                          int32_t* status, void* stream) {
+  gemm::Params p{};
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  p.resid = static_cast<const __nv_bfloat16*>(resid);
+  p.ldr = ldr;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.epilogue = epilogue;
+  p.status = status;
+  return gemm::launch<false>(a, lda, w, ldw, p, static_cast<cudaStream_t>(stream));
+}
+
+DAN_API int dan_gemm_e4m3(const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,
+                          const float* w_scale, void* c, int64_t ldc, const void* resid, int64_t ldr,
+                          const void* bias, int m, int n, int k, int epilogue, int32_t* status, void* stream) {
+  gemm::Params p{};
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  p.resid = static_cast<const __nv_bfloat16*>(resid);
+  p.ldr = ldr;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.a_scale = a_scale;
+  p.w_scale = w_scale;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.epilogue = epilogue;
+  p.status = status;
+  return gemm::launch<true>(a, lda, w, ldw, p, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,103 @@
+/* dan_b200: C ABI of the B200 (sm_100a) kernels for dan's packed prefill read path.
+ *
+ * Conventions for every entry point:
+ *   - pointers are device pointers unless named *_host; strides are in elements;
+ *   - bf16 tensors are raw uint16 bf16 bit patterns; e4m3 tensors are bytes;
+ *   - ``stream`` is a cudaStream_t (NULL = legacy default stream);
+ *   - ``status`` is a device int32 word: kernels write the first error they detect
+ *     (a bounded wait that ran out, an out-of-range index) instead of hanging or
+ *     faulting; read it with dan_read_status once per batch;
+ *   - the return value is 0, or a negative code with the text in dan_last_error();
+ *   - nothing allocates or frees device memory: callers own every buffer.
+ *
+ * Each function names the reference (quangliz/dan) interface it replaces.
+ */
+#ifndef DAN_B200_H
+#define DAN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+const char* dan_version(void);
+/* Text of the last error on the calling thread. */
+const char* dan_last_error(void);
+/* Copy *status_dev to *status_host, synchronise ``stream``, clear the device word if set. */
+int dan_read_status(int32_t* status_dev, int32_t* status_host, void* stream);
+
+/* Tree-masked attention over a packed batch, one launch for all segments and heads.
+ * Replaces attend / _attend_varlen (dan/attention.py:200-241: three varlen flash calls,
+ * row gathers, past concatenation and lse_merge, fused.py:94-101); semantics of
+ * _attend_dense (attention.py:244-270).
+ * q [n_rows, n_heads, head_dim], k/v [n_rows, n_kv_heads, head_dim] (row/head strides given,
+ * unit stride in head_dim, 16-byte aligned); k_pool/v_pool [pool_rows, n_kv_heads, head_dim]
+ * hold cached prefix pages of 128 tokens (may be NULL when no segment has a past).
+ * tiles: int32 [n_tiles, 12] {row0, nrows, seg_start, past, ppad, split, nblk_a, blk_b0,
+ * blk_b1, page0, q0v, 0}; row_own: int32 [n_rows] packed row where each row's run starts;
+ * pages: int32 pool page per cached 128-token block. head_dim in {64, 128, 256}. */
+int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, const void* k, int64_t k_row, int64_t k_head,
+                       const void* v, int64_t v_row, int64_t v_head, const void* k_pool, const void* v_pool,
+                       int64_t pool_row, int64_t pool_head, int pool_rows, void* out, int64_t out_row,
+                       int64_t out_head, int n_rows, int n_heads, int n_kv_heads, int head_dim, const int* tiles,
+                       int n_tiles, const int* row_own, const int* pages, float scale, int32_t* status,
+                       void* stream);
+
+/* C[m, n] = A[m, k] * W[n, k]^T in bf16 with fp32 accumulation on tcgen05 tensor cores.
+ * Replaces nn.Linear in the decoder (dan/models/llama.py:78,87,102; qwen3_5.py:185,212,319,329,344)
+ * and fuses: epilogue 0 store (+bias), 1 C = R + bf16(acc) (the residual adds, llama.py:116-117),
+ * 2 SwiGLU over W rows interleaved in 128-row [gate | up] blocks, C has n/2 columns
+ * (swiglu, dan/fused.py:59-61). C may alias R (in-place residual). */
+int dan_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, const void* resid,
+                  int64_t ldr, const void* bias, int m, int n, int k, int epilogue, int32_t* status, void* stream);
+
+/* e4m3 x e4m3 GEMM with per-row (token) and per-column (output channel) fp32 scales, bf16 out.
+ * Replaces FP8Linear.forward (dan/quant.py:37-42, torch._scaled_mm row-wise); epilogues as above. */
+int dan_gemm_e4m3(const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw, const float* w_scale,
+                  void* c, int64_t ldc, const void* resid, int64_t ldr, const void* bias, int m, int n, int k,
+                  int epilogue, int32_t* status, void* stream);
+
+/* out[r] = table[ids[r]] (nn.Embedding, dan/models/llama.py:157). */
+int dan_embed(const int64_t* ids, const void* table, int64_t ldt, int64_t vocab, void* out, int64_t ldo, int rows,
+              int cols, int32_t* status, void* stream);
+
+/* RMSNorm over rows (r / inner, r % inner) of x; mode 0 Llama (dan/fused.py:35-40), 1 zero-centred
+ * (fused.py:43-48). Optional fused per-row e4m3 quantisation of the result (fused.py:85-91). */
+int dan_rms_norm(const void* x, int64_t x_outer, int64_t x_inner, int inner, const void* w, float eps, int mode,
+                 void* y, int64_t y_outer, int64_t y_inner, void* q8, int64_t ldq, float* q8_scale, int rows,
+                 int cols, void* stream);
+
+/* Per-row e4m3 quantisation, scale = max(amax, 1e-12) / 448 (fp8_quantize, dan/fused.py:85-91;
+ * weight quantisation, dan/quant.py:26-33). */
+int dan_quantize_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, float* scale, int rows, int cols,
+                      void* stream);
+
+/* In-place rotate-half RoPE on the first ``rot`` dims of each head (dan/models/llama.py:43-45,
+ * 155-158; rotate_partial, dan/fused.py:69-76). */
+int dan_rope(void* x, int64_t ld_row, int64_t ld_head, int heads, int head_dim, int rot, const int64_t* pos,
+             const float* inv_freq, int rows, void* stream);
+
+/* o *= sigmoid(gate), gate read per head (sigmoid_gate, dan/fused.py:64-66; qwen3_5.py:328). */
+int dan_sigmoid_gate(void* o, int64_t ldo, const void* g, int64_t ldg, int64_t g_head_stride, int head_dim, int rows,
+                     int cols, void* stream);
+
+/* Store packed k/v rows into prefix-pool rows (the prefix saves of dan/attention.py:202-204
+ * and PrefixCache.put, dan/cache.py:30-39). */
+int dan_kv_store(const void* k, const void* v, int64_t ld_row, int64_t ld_head, void* pool_k, void* pool_v,
+                 int64_t pool_row, int64_t pool_head, const int* src_rows, const int* dst_rows, int count, int heads,
+                 int head_dim, void* stream);
+
+/* Per question q: final RMSNorm of h[read_rows[q]], logits = W_lm[label_ids[off[q]:off[q+1]]] @ h
+ * in fp32, and their softmax. Replaces the read-row gather + per-branch label_logits loop
+ * (dan/runner.py:73-74, dan/models/llama.py:161-165) and readout.softmax (dan/readout.py:13-17). */
+int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, const void* norm_w, float eps, int mode,
+                      const void* w_lm, int64_t ldw, int64_t vocab, const int* label_ids, const int* offsets,
+                      int n_questions, int hidden, int max_labels, float* logits, float* probs, int32_t* status,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

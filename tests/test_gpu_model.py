@@ -1,0 +1,50 @@
+"""End-to-end reads on the GPU vs the reference's own outputs (golden fixtures).
+
+Configuration 1's model (SmolLM2-135M shaped, seeded weights) runs through
+``Runner.read_many`` in bf16 on the dan_b200 kernels over a cold -> warm ->
+mixed prefix-cache sequence. Bars: answer probabilities within 5e-3 of the
+reference's fp32 path (north-star bf16 bound) and the same cache hits."""
+import pytest
+import torch
+from conftest import golden, plans_from_json
+
+from dan_b200.runner import Runner
+from oracle import weights
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tiny_dir(tmp_path_factory):
+    g = golden("tiny_llama.json")
+    path = tmp_path_factory.mktemp("tiny_llama")
+    weights.save_checkpoint(str(path), g["config"], weights.random_state(g["config"], g["seed"]))
+    return str(path), g
+
+
+def test_tiny_llama_matches_reference(cuda, tiny_dir):
+    path, g = tiny_dir
+    runner = Runner(path, cuda)
+    worst_p = worst_l = 0.0
+    for b in g["batches"]:
+        plans = plans_from_json(b["plans"])
+        got, probs = runner.read_many(plans, probabilities=True)
+        for per, pp, want in zip(got, probs, b["runner"]):
+            assert len(per) == len(want)
+            for lg, p, w in zip(per, pp, want):
+                w = torch.tensor(w)
+                worst_l = max(worst_l, (lg - w).abs().max().item())
+                worst_p = max(worst_p, (p - torch.softmax(w.double(), 0).float()).abs().max().item())
+        assert runner.cache.hits == b["hits"], b["name"]
+    assert worst_p < 5e-3, worst_p
+    assert worst_l < 5e-2, worst_l
+
+
+def test_without_cache_same_answers(cuda, tiny_dir):
+    path, g = tiny_dir
+    runner = Runner(path, cuda, cache_bytes=0)
+    b = g["batches"][-1]
+    got, probs = runner.read_many(plans_from_json(b["plans"]), probabilities=True)
+    for pp, want in zip(probs, b["runner"]):
+        for p, w in zip(pp, want):
+            assert (p - torch.softmax(torch.tensor(w).double(), 0).float()).abs().max() < 5e-3

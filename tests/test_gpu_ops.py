@@ -1,0 +1,149 @@
+"""GEMM, norm, RoPE, embedding, quantisation and readout kernels vs fp32 references.
+
+Tolerances: bf16 outputs are compared at a relative error of 1e-2 of the output
+scale (one bf16 rounding is 2^-8); e4m3 GEMMs against the FP8 restatement
+(oracle.fp8) at the same bound after identical quantisation."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from dan_b200 import ops
+from oracle import fp8 as OF
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).abs().max() / b.abs().max().clamp(min=1e-6)).item()
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (200, 960, 576), (1000, 6144, 512), (77, 512, 1536),
+                                   (1, 256, 128), (300, 1000, 200)])
+def test_gemm_bf16(cuda, m, n, k):
+    g = torch.Generator(device=cuda).manual_seed(m + n + k)
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = torch.randn(n, k, device=cuda, generator=g).bfloat16()
+    y = ops.linear(x, w)
+    assert rel_err(y, x.float() @ w.float().T) < 1e-2
+
+
+def test_gemm_bias_residual(cuda):
+    g = torch.Generator(device=cuda).manual_seed(1)
+    m, n, k = 513, 768, 320
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = torch.randn(n, k, device=cuda, generator=g).bfloat16()
+    b = torch.randn(n, device=cuda, generator=g).bfloat16()
+    r = torch.randn(m, n, device=cuda, generator=g).bfloat16()
+    want = r.float() + (x.float() @ w.float().T + b.float())
+    ops.linear(x, w, bias=b, residual=r)  # in place into r
+    assert rel_err(r, want) < 1e-2
+
+
+def test_gemm_swiglu(cuda):
+    g = torch.Generator(device=cuda).manual_seed(2)
+    m, i, k = 333, 512, 256
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    wg = torch.randn(i, k, device=cuda, generator=g).bfloat16()
+    wu = torch.randn(i, k, device=cuda, generator=g).bfloat16()
+    y = ops.linear_swiglu(x, ops.interleave_gate_up(wg, wu))
+    want = F.silu(x.float() @ wg.float().T) * (x.float() @ wu.float().T)
+    assert rel_err(y, want) < 1e-2
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 512, 256), (130, 1280, 640)])
+def test_gemm_e4m3(cuda, m, n, k):
+    g = torch.Generator(device=cuda).manual_seed(3)
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=cuda, generator=g) * 0.05).bfloat16()
+    xq, xs = ops.quantize_e4m3(x)
+    wq, ws = ops.quantize_e4m3(w)
+    y = ops.linear_e4m3(xq, xs, wq, ws)
+    # the same quantisation on the CPU (oracle), then an exact product
+    oxq, oxs = OF.quantize_rows(x.cpu())
+    owq, ows = OF.quantize_rows(w.cpu())
+    assert torch.equal(xq.float().cpu(), oxq) and torch.allclose(xs.cpu(), oxs.flatten())
+    assert torch.equal(wq.float().cpu(), owq)
+    want = OF.linear(x.cpu(), owq, ows.flatten())
+    assert rel_err(y, want) < 1e-2
+
+
+def test_rms_norm_modes(cuda):
+    g = torch.Generator(device=cuda).manual_seed(4)
+    x = torch.randn(37, 4096, device=cuda, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(4096, device=cuda, generator=g)).bfloat16()
+    xf = x.float()
+    xh = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)
+    assert rel_err(ops.rms_norm(x, w, 1e-5), w.float() * xh.bfloat16().float()) < 1e-2
+    assert rel_err(ops.rms_norm(x, w, 1e-5, zero_centered=True), xh * (1 + w.float())) < 1e-2
+    # per-head, in place on a strided view
+    buf = torch.randn(10, 6 * 128, device=cuda, generator=g).bfloat16()
+    view = buf[:, 128:5 * 128].view(10, 4, 128)
+    ref = view.float()
+    hw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).bfloat16()
+    want = hw.float() * (ref * torch.rsqrt(ref.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16().float()
+    before = buf.clone()
+    ops.rms_norm(view, hw, 1e-6, out=view)
+    assert rel_err(view, want) < 1e-2
+    assert torch.equal(buf[:, :128], before[:, :128]) and torch.equal(buf[:, 5 * 128:], before[:, 5 * 128:])
+
+
+def test_rms_norm_fp8_fused(cuda):
+    g = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn(64, 2560, device=cuda, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(2560, device=cuda, generator=g)).bfloat16()
+    y = ops.rms_norm(x, w, 1e-6)
+    _, q8, sc = ops.rms_norm(x, w, 1e-6, fp8=True)
+    oq, osc = OF.quantize_rows(y.cpu())
+    assert torch.equal(q8.float().cpu(), oq) and torch.allclose(sc.cpu(), osc.flatten())
+
+
+@pytest.mark.parametrize("rot", [128, 64])
+def test_rope(cuda, rot):
+    from oracle.llama import rotate
+
+    g = torch.Generator(device=cuda).manual_seed(6)
+    n, heads, d = 50, 6, 128
+    x = torch.randn(n, heads, d, device=cuda, generator=g).bfloat16()
+    pos = torch.randint(0, 5000, (n,), device=cuda, generator=g)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, rot, 2, dtype=torch.float32, device=cuda) / rot))
+    ang = pos.float()[:, None] * inv[None]
+    ang = torch.cat([ang, ang], -1)
+    cos, sin = ang.cos().bfloat16().float(), ang.sin().bfloat16().float()
+    want = torch.cat([rotate(x.float()[..., :rot], cos[:, None], sin[:, None]), x.float()[..., rot:]], -1)
+    ops.rope_(x, pos, inv, rot)
+    assert rel_err(x, want) < 1e-2
+
+
+def test_embed_and_readout(cuda):
+    g = torch.Generator(device=cuda).manual_seed(7)
+    vocab, hidden = 1000, 576
+    table = torch.randn(vocab, hidden, device=cuda, generator=g).bfloat16()
+    ids = torch.randint(0, vocab, (40,), device=cuda, generator=g)
+    x = ops.embed(ids, table)
+    assert torch.equal(x, table[ids])
+    nw = (1 + 0.1 * torch.randn(hidden, device=cuda, generator=g)).bfloat16()
+    rows = torch.tensor([3, 17, 39], dtype=torch.int32, device=cuda)
+    labels = [[5, 9], [1, 2, 3, 4, 999], list(range(100, 355))]
+    flat = torch.tensor([i for l in labels for i in l], dtype=torch.int32, device=cuda)
+    off = torch.tensor([0, 2, 7, 7 + 255], dtype=torch.int32, device=cuda)
+    lg, pr = ops.label_readout(x, rows, nw, 1e-5, False, table, flat, off, 255)
+    xf = x.float()[rows.long()]
+    hn = nw.float() * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).bfloat16().float()
+    hn = hn.bfloat16().float()
+    for q, l in enumerate(labels):
+        want = table.float()[torch.tensor(l, device=cuda)] @ hn[q]
+        got = lg[off[q]:off[q + 1]]
+        torch.testing.assert_close(got, want, atol=1e-3, rtol=1e-3)
+        torch.testing.assert_close(pr[off[q]:off[q + 1]], torch.softmax(want, 0), atol=1e-5, rtol=1e-4)
+
+
+def test_kv_store(cuda):
+    k = torch.randn(20, 2, 64, device=cuda).bfloat16()
+    v = torch.randn(20, 2, 64, device=cuda).bfloat16()
+    pk = torch.zeros(256, 2, 64, device=cuda).bfloat16()
+    pv = torch.zeros_like(pk)
+    src = torch.tensor([3, 4, 5], dtype=torch.int32, device=cuda)
+    dst = torch.tensor([130, 131, 132], dtype=torch.int32, device=cuda)
+    ops.kv_store(k, v, pk, pv, src, dst)
+    assert torch.equal(pk[130:133], k[3:6]) and torch.equal(pv[130:133], v[3:6])

@@ -1,0 +1,155 @@
+"""Host-side logic on the CPU: the C-ABI library, packing, the tree-attention tile
+table and the prefix pool policy. No GPU calls."""
+import os
+import random
+
+import pytest
+import torch
+from conftest import ROOT, golden, plans_from_json
+from helpers import build_segments, expected_visible, header_symbols, kernel_visible
+
+from dan_b200 import synthetic
+from dan_b200.attention import TreeLayout, useful_pairs
+from dan_b200.cache import PrefixPool
+from dan_b200.runner import Runner
+
+
+@pytest.fixture(scope="session")
+def built_lib():
+    from dan_b200 import _lib, build
+
+    build.build()
+    return _lib
+
+
+def test_library_exports_every_header_symbol(built_lib):
+    lib = built_lib.lib()
+    syms = header_symbols(os.path.join(ROOT, "include", "dan_b200.h"))
+    assert len(syms) >= 12
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    assert b"sm_100a" in lib.dan_version()
+
+
+def cpu_runner(cache_bytes=1 << 30):
+    r = Runner.__new__(Runner)
+    r.device = torch.device("cpu")
+    r.cache = PrefixPool(cache_bytes, 1, 1, 8, "cpu") if cache_bytes else None
+    return r
+
+
+def test_pack_matches_reference_bit_exact():
+    runner = cpu_runner()
+    for rec in golden("pack.json"):
+        plans = plans_from_json(rec["plans"])
+        ids, pos, segs, reads, stores = runner.pack(plans)
+        assert ids == rec["ids"] and pos == rec["pos"]
+        assert [[r, list(l)] for r, l in reads] == rec["reads"]
+        assert len(segs) == len(rec["segments"])
+        for s, r in zip(segs, rec["segments"]):
+            assert (s.start, s.end, s.trunk, s.past_len, s.save, bool(s.past)) == \
+                (r["start"], r["end"], r["trunk"], r["past_len"], r["save"], r["has_past"])
+            assert [list(x) for x in s.branches] == r["branches"]
+            assert list(s.branch_ids) == r["branch_ids"]
+        assert [[len(st), segs.index(sg)] for st, sg in stores] == rec["stores"]
+        held, _, _ = runner._reserve(segs, stores)
+        for static, seg, entry in held:
+            runner.cache.commit(static, entry)
+
+
+def test_read_layout_rows_match_reference():
+    """The reference's varlen row sets and cumulative lengths (attention.py:155-172) follow
+    from our segments exactly."""
+    runner = cpu_runner()
+    for rec in golden("pack.json"):
+        plans = plans_from_json(rec["plans"])
+        ids, pos, segs, reads, stores = runner.pack(plans)
+        want = rec["read_layout"]
+        trunk_rows = [r for s in segs for r in range(s.start, s.start + s.trunk)]
+        branch_rows = [r for s in segs for r in range(s.start + s.trunk, s.end)]
+        assert trunk_rows == want["trunk_rows"] and branch_rows == want["branch_rows"]
+        cu = lambda xs: [0] + list(__import__("itertools").accumulate(xs))
+        assert cu([s.trunk for s in segs]) == want["cu_trunk_q"]
+        assert cu([s.past_len + s.trunk for s in segs]) == want["cu_trunk_k"]
+        assert cu([s.end - s.start - s.trunk for s in segs]) == want["cu_branch_q"]
+        bl = [b - a for s in segs for a, b in s.branches]
+        assert (cu(bl) if bl else None) == want["cu_branch"]
+        held, _, _ = runner._reserve(segs, stores)
+        for static, seg, entry in held:
+            runner.cache.commit(static, entry)
+
+
+EDGE = [(40, [5, 9, 1], 0), (7, [30], 12), (1, [3, 3, 3, 3, 3, 3], 0), (64, [], 0), (13, [17, 2], 20)]
+
+
+@pytest.mark.parametrize("shapes", [
+    EDGE,
+    [(300, [17, 200, 1], 0), (129, [128, 128], 250), (0, [5, 7], 130), (128, [1], 128), (1000, [96] * 12, 0)],
+    [(0, [3], 1), (5, [], 300), (256, [0 + 64] * 5, 1024)],
+])
+def test_tree_layout_visits_exactly_the_tree_mask(shapes):
+    segs, n, _ = build_segments(shapes)
+    lay = TreeLayout.build(segs, n, "cpu")
+    got = kernel_visible(lay, n)
+    want = expected_visible(segs)
+    assert got.keys() == want.keys()
+    for r in want:
+        assert sorted(got[r]) == want[r], r
+    assert lay.pairs == sum(len(v) for v in want.values()) == useful_pairs(segs)
+
+
+def test_tree_layout_random_batches():
+    rng = random.Random(7)
+    for trial in range(20):
+        shapes = [(rng.randint(0, 400), [rng.randint(1, 150) for _ in range(rng.randint(0, 6))],
+                   rng.choice([0, 0, rng.randint(1, 700)])) for _ in range(rng.randint(1, 5))]
+        shapes = [s for s in shapes if s[0] + sum(s[1]) > 0]
+        if not shapes:
+            continue
+        segs, n, _ = build_segments(shapes, seed=trial)
+        lay = TreeLayout.build(segs, n, "cpu")
+        got, want = kernel_visible(lay, n), expected_visible(segs)
+        for r in want:
+            assert sorted(got[r]) == want[r]
+
+
+def test_tiles_are_longest_first_and_cover_all_rows():
+    plans = synthetic.batch(2, seed=3)
+    runner = cpu_runner(0)
+    ids, pos, segs, reads, stores = runner.pack(plans)
+    lay = TreeLayout.build(segs, len(ids), "cpu")
+    t = lay.tiles.numpy()
+    cost = t[:, 6] + t[:, 8] - t[:, 7]
+    assert (cost[:-1] >= cost[1:]).all()
+    assert t[:, 1].sum() == len(ids)
+
+
+def test_synthetic_batches_follow_the_engine_rule():
+    for seed in range(5):
+        plans = synthetic.batch(2, seed=seed)
+        used = sum(synthetic.cost(p) for p in plans)
+        assert used <= 8192 and len(plans) <= 16
+        for p in plans:
+            assert 128 <= len(p.prefix) <= 2048 and 1 <= len(p.branches) <= 16
+            assert all(16 <= len(b.suffix) <= 96 and 2 <= len(b.label_ids) <= 26 for b in p.branches)
+    b = synthetic.batches(3, 3, seed=1)
+    assert len(b) == 3 and all(sum(synthetic.cost(p) for p in x) <= 8192 for x in b)
+
+
+def test_prefix_pool_lru_and_budget():
+    page_bytes = 128 * 1 * 8 * 2 * 2
+    pool = PrefixPool(page_bytes * 4, 1, 1, 8, "cpu")
+    assert pool.n_pages == 4
+    a = pool.reserve([1, 2], 200)  # 2 pages
+    pool.commit([1, 2], a)
+    b = pool.reserve([3], 130)  # 2 pages
+    pool.commit([3], b)
+    assert pool.get([1, 2]) is a and pool.hits == 1
+    c = pool.reserve([4], 100)  # evicts the LRU entry ([3]); [1, 2] was just used
+    pool.commit([4], c)
+    assert pool.get([3]) is None and pool.misses == 1
+    assert pool.get([1, 2]) is a
+    assert pool.reserve([5], 10 ** 6) is None  # larger than the budget: not cached
+    d = pool.reserve([6], 300, pinned=[a, c])  # needs 3 pages, only pinned entries left
+    assert d is None
+    assert pool.used == a.nbytes + c.nbytes
