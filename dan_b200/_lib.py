@@ -23,18 +23,22 @@ SIGNATURES = {
     "dan_read_status": ([P, P, P], I32),
     "dan_gemm_bf16": ([P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
     "dan_gemm_e4m3": ([P, I64, P, P, I64, P, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
+    "dan_gemm_bf16_rope": ([P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, I32, I32, P, P, P, P], I32),
+    "dan_gemm_e4m3_rope": ([P, I64, P, P, I64, P, P, I64, P, I64, P, I32, I32, I32, I32, I32, I32, P, P, P, P],
+                           I32),
+    "dan_rope_table": ([P, P, I32, I32, P, P, P], I32),
     "dan_tree_attention": ([P, I64, I64, P, I64, I64, P, I64, I64, P, P, I64, I64, I32, P, I64, I64, I32, I32, I32,
                             I32, P, I32, P, P, F32, P, P], I32),
     "dan_embed": ([P, P, I64, I64, P, I64, I32, I32, P, P], I32),
     "dan_rms_norm": ([P, I64, I64, I32, P, F32, I32, P, I64, I64, P, I64, P, I32, I32, P], I32),
     "dan_quantize_e4m3": ([P, I64, P, I64, P, I32, I32, P], I32),
-    "dan_rope": ([P, I64, I64, I32, I32, I32, P, P, I32, P], I32),
+    "dan_rope": ([P, I64, I64, I32, I32, I32, P, P, I32, P], I32),  # x, ld_row, ld_head, heads, d, rot, cos, sin
     "dan_sigmoid_gate": ([P, I64, P, I64, I64, I32, I32, I32, P], I32),
     "dan_kv_store": ([P, P, I64, I64, P, P, I64, I64, P, P, I32, I32, I32, P], I32),
     "dan_label_readout": ([P, I64, P, P, F32, I32, P, I64, I64, P, P, I32, I32, I32, P, P, P, P], I32),
-    "dan_causal_conv": ([P, I64, P, I64, P, P, P, P, I32, I32, I32, I32, P, I64, P], I32),
-    "dan_delta_gates": ([P, I64, P, I64, P, P, P, P, I32, I32, P], I32),
-    "dan_gated_delta_scan": ([P, I64, P, I64, P, I64, P, P, P, P, P, I32, I32, I32, I32, I32, I32, P, I64, P, P, P],
+    "dan_causal_conv": ([P, I64, P, I64, P, P, P, I64, I32, I32, P], I32),
+    "dan_gather_rows": ([P, I64, P, I64, P, I32, P, I64, I32, P], I32),
+    "dan_gated_delta_scan": ([P, P, P, I64, P, P, I64, P, P, P, I32, P, P, I64, P, I64, I32, I32, I32, I32, F32, P],
                              I32),
     "dan_gated_rms_norm": ([P, I64, P, I64, P, F32, P, I64, I32, I32, I32, P], I32),
 }
@@ -65,8 +69,9 @@ def exported():
     return [n for n in SIGNATURES if hasattr(lb, n)]
 
 
-def call(name, *args, work=0):
-    """Launch entry point ``name``; ``work`` is its algorithmic FLOPs or bytes (for timing)."""
+def call(name, *args, work=0, key=None):
+    """Launch entry point ``name``; ``work`` is its algorithmic FLOPs or bytes, ``key`` the
+    group its timing is reported under (default: the entry point)."""
     fn = getattr(lib(), name)
     timer = profiling.active()
     if timer is not None and timer.wants(name):
@@ -74,7 +79,7 @@ def call(name, *args, work=0):
         s.record()
         rc = fn(*args)
         e.record()
-        timer.records[name].append((s, e, work))
+        timer.records[key or name].append((s, e, work))
     else:
         rc = fn(*args)
     if rc != 0:

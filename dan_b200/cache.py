@@ -10,7 +10,8 @@ them (attention.py:217-226), keys and values live in fixed 128-token pages of
 one preallocated pool per model, ``k`` / ``v`` [layers, pages * 128, Hkv, D]
 bf16. An entry is a list of pages; the attention kernel reads them in place
 through a page table. Recurrent (DeltaNet) layers keep, per entry, one state
-slot: the conv tail [layers, k - 1, conv_dim] and the state [layers, Hv, Dk, Dv]
+slot: the conv tail and the state of every DeltaNet layer, held as ``conv``
+[layers, slots, k - 1, conv_dim] bf16 and ``state`` [layers, slots, Hv, Dk, Dv]
 fp32 (qwen3_5.py:207-209).
 
 Pages are reserved when a batch is packed (the reference stores after the
@@ -56,10 +57,10 @@ class PrefixPool:
         dev = torch.device(device)
         self.k = torch.empty(layers, self.n_pages * PAGE, kv_heads, head_dim, dtype=torch.bfloat16, device=dev)
         self.v = torch.empty_like(self.k)
-        if recurrent:
+        if recurrent:  # layer-major, so one layer's slots are one contiguous block
             nl, kr, cd, hv, dk, dv = recurrent
-            self.conv = torch.zeros(self.n_slots, nl, kr, cd, dtype=torch.bfloat16, device=dev)
-            self.state = torch.zeros(self.n_slots, nl, hv, dk, dv, dtype=torch.float32, device=dev)
+            self.conv = torch.zeros(nl, self.n_slots, kr, cd, dtype=torch.bfloat16, device=dev)
+            self.state = torch.zeros(nl, self.n_slots, hv, dk, dv, dtype=torch.float32, device=dev)
         self.free_pages = list(range(self.n_pages))
         self.free_slots = list(range(self.n_slots))
         self.recurrent = bool(recurrent)

@@ -164,27 +164,46 @@ __global__ void quant_rows_kernel(const __nv_bfloat16* x, int64_t ldx, uint8_t* 
 }
 
 // ---------------------------------------------------------------- RoPE
-// Rotate-half on the first ``rot`` dims of each of ``heads`` heads of each row, in place
-// (llama.py:43-45, fused.py:69-76). cos/sin are computed in fp32 from integer positions
-// and rounded to bf16 as the reference does (llama.py:155-158); the products and the sum
-// are rounded to bf16 at the reference's points.
-__global__ void rope_kernel(__nv_bfloat16* x, int64_t ld_row, int64_t ld_head, int heads, int rot,
-                            const int64_t* pos, const float* inv_freq, int rows) {
-  const int half = rot / 2;
-  const int per_row = heads * half;
+// cos/sin table, once per forward: angle = float(pos) * inv_freq[i] in fp32, then cos and
+// sin rounded to bf16 as the reference does (llama.py:155-158, qwen3_5.py:411-414).
+__global__ void rope_table_kernel(const int64_t* pos, const float* inv_freq, int rows, int half, float* cos_t,
+                                  float* sin_t) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<int64_t>(rows) * per_row) return;
-  const int r = static_cast<int>(idx / per_row);
-  const int rem = static_cast<int>(idx % per_row);
-  const int h = rem / half, i = rem % half;
+  if (idx >= static_cast<int64_t>(rows) * half) return;
+  const int r = static_cast<int>(idx / half), i = static_cast<int>(idx % half);
   const float ang = static_cast<float>(pos[r]) * inv_freq[i];
   float sn, cs;
   sincosf(ang, &sn, &cs);
-  const float c = bf16_round(cs), s = bf16_round(sn);
+  cos_t[idx] = bf16_round(cs);
+  sin_t[idx] = bf16_round(sn);
+}
+
+// Rotate-half on the first ``rot`` dims of each head, in place, 8 pairs per thread with
+// 16-byte accesses (llama.py:43-45, fused.py:69-76); products and sum rounded to bf16 at
+// the reference's points.
+__global__ void rope_kernel(__nv_bfloat16* x, int64_t ld_row, int64_t ld_head, int heads, int rot,
+                            const float* cos_t, const float* sin_t, int rows) {
+  const int half = rot / 2, groups = half / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(rows) * heads * groups) return;
+  const int r = static_cast<int>(idx / (heads * groups));
+  const int rem = static_cast<int>(idx % (heads * groups));
+  const int h = rem / groups, i0 = (rem % groups) * 8;
   __nv_bfloat16* p = x + static_cast<int64_t>(r) * ld_row + static_cast<int64_t>(h) * ld_head;
-  const float a = __bfloat162float(p[i]), b = __bfloat162float(p[i + half]);
-  p[i] = __float2bfloat16_rn(bf16_round(a * c) + bf16_round(-b * s));
-  p[i + half] = __float2bfloat16_rn(bf16_round(b * c) + bf16_round(a * s));
+  uint4 va = *reinterpret_cast<const uint4*>(p + i0), vb = *reinterpret_cast<const uint4*>(p + half + i0);
+  __nv_bfloat16* ea = reinterpret_cast<__nv_bfloat16*>(&va);
+  __nv_bfloat16* eb = reinterpret_cast<__nv_bfloat16*>(&vb);
+  const float* ct = cos_t + static_cast<int64_t>(r) * half + i0;
+  const float* st = sin_t + static_cast<int64_t>(r) * half + i0;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float a = __bfloat162float(ea[t]), b = __bfloat162float(eb[t]);
+    const float c = ct[t], s = st[t];
+    ea[t] = __float2bfloat16_rn(bf16_round(a * c) + bf16_round(-b * s));
+    eb[t] = __float2bfloat16_rn(bf16_round(b * c) + bf16_round(a * s));
+  }
+  *reinterpret_cast<uint4*>(p + i0) = va;
+  *reinterpret_cast<uint4*>(p + half + i0) = vb;
 }
 
 // ---------------------------------------------------------------- sigmoid gate
@@ -331,13 +350,27 @@ DAN_API int dan_quantize_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, 
   return 0;
 }
 
-DAN_API int dan_rope(void* x, int64_t ld_row, int64_t ld_head, int heads, int head_dim, int rot, const int64_t* pos,
-                     const float* inv_freq, int rows, void* stream) {
-  DAN_REQUIRE(rot > 0 && rot % 2 == 0 && rot <= head_dim, "rope: rot=%d head_dim=%d", rot, head_dim);
+DAN_API int dan_rope_table(const int64_t* pos, const float* inv_freq, int rows, int half, float* cos_t,
+                           float* sin_t, void* stream) {
+  DAN_REQUIRE(half > 0, "rope_table: half=%d", half);
+  if (!rows) return 0;
+  const int64_t n = static_cast<int64_t>(rows) * half;
+  ew::rope_table_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      pos, inv_freq, rows, half, cos_t, sin_t);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+DAN_API int dan_rope(void* x, int64_t ld_row, int64_t ld_head, int heads, int head_dim, int rot, const float* cos_t,
+                     const float* sin_t, int rows, void* stream) {
+  DAN_REQUIRE(rot > 0 && rot % 16 == 0 && rot <= head_dim, "rope: rot=%d must be a multiple of 16 <= head_dim=%d",
+              rot, head_dim);
+  DAN_REQUIRE(ld_row % 8 == 0 && ld_head % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0,
+              "rope: x must be 16-byte aligned with strides that are multiples of 8");
   if (!rows || !heads) return 0;
-  const int64_t n = static_cast<int64_t>(rows) * heads * (rot / 2);
+  const int64_t n = static_cast<int64_t>(rows) * heads * (rot / 16);
   ew::rope_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(x), ld_row, ld_head, heads, rot, pos, inv_freq, rows);
+      static_cast<__nv_bfloat16*>(x), ld_row, ld_head, heads, rot, cos_t, sin_t, rows);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }

@@ -30,7 +30,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 
-enum Epilogue { kStore = 0, kResidual = 1, kSwiglu = 2 };
+enum Epilogue { kStore = 0, kResidual = 1, kSwiglu = 2, kRope = 3 };
 
 struct Params {
   __nv_bfloat16* c;
@@ -43,6 +43,10 @@ struct Params {
   int m, n, k;
   int tiles_m, tiles_n;
   int epilogue;
+  int rope_cols;        // kRope: leading output columns holding rotary heads
+  int rope_hd;          // kRope: head size (64, 128 or 256); pairs (i, i + hd/2) rotate
+  const float* cos_t;   // kRope: [m, hd/2] bf16-rounded cos of each row's angles
+  const float* sin_t;
   int32_t* status;
 };
 
@@ -54,20 +58,32 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, i
   if (row >= p.m) return;
   __nv_bfloat16* dst = p.c + static_cast<int64_t>(row) * p.ldc + col;
   uint32_t packed[16];
+  const bool full = col + 32 <= cols_out && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
   if (p.epilogue == kResidual) {
     const __nv_bfloat16* r = p.resid + static_cast<int64_t>(row) * p.ldr + col;
+    if (full && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+      uint4 rv[4];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float a = 0.f, b = 0.f;
-      if (col + 2 * i < cols_out) a = __bfloat162float(r[2 * i]);
-      if (col + 2 * i + 1 < cols_out) b = __bfloat162float(r[2 * i + 1]);
-      packed[i] = pack_bf16(a + bf16_round(v[2 * i]), b + bf16_round(v[2 * i + 1]));
+      for (int i = 0; i < 4; ++i) rv[i] = reinterpret_cast<const uint4*>(r)[i];
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(rv);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 rf = __bfloat1622float2(r2[i]);
+        packed[i] = pack_bf16(rf.x + bf16_round(v[2 * i]), rf.y + bf16_round(v[2 * i + 1]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float a = 0.f, b = 0.f;
+        if (col + 2 * i < cols_out) a = __bfloat162float(r[2 * i]);
+        if (col + 2 * i + 1 < cols_out) b = __bfloat162float(r[2 * i + 1]);
+        packed[i] = pack_bf16(a + bf16_round(v[2 * i]), b + bf16_round(v[2 * i + 1]));
+      }
     }
   } else {
 #pragma unroll
     for (int i = 0; i < 16; ++i) packed[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
   }
-  const bool full = col + 32 <= cols_out && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
   if (full) {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -220,6 +236,60 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           store_chunk<FP8>(p, row, tn * (BN / 2) + c, cols_out, v);
         }
+      } else if (p.epilogue == kRope) {
+        // q/k heads: rotate-half RoPE on the bf16-rounded projection with the reference's
+        // rounding points, bf16(bf16(a cos) + bf16(-b sin)) (llama.py:43-45); v heads: plain.
+        const int hd = p.rope_hd, half = hd / 2;
+        const int trow = row < p.m ? row : 0;
+#pragma unroll 1
+        for (int h0 = 0; h0 < BN; h0 += hd) {
+          const int hc = tn * BN + h0;
+          if (hc >= p.n) break;
+#pragma unroll 1
+          for (int c = 0; c < half; c += 32) {
+            uint32_t ra[32], rb[32];
+            tmem_ld32(taddr + h0 + c, ra);
+            tmem_ld32(taddr + h0 + half + c, rb);
+            tmem_wait_ld();
+            float va[32], vb[32];
+            const bool rot = hc + hd <= p.rope_cols;
+            float ct[32], st[32];
+            if (rot) {  // 32 consecutive cos / sin of this row: 8 + 8 16-byte loads
+              const float4* c4 = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(trow) * half + c);
+              const float4* s4 = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(trow) * half + c);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 cv = c4[i], sv = s4[i];
+                ct[4 * i] = cv.x, ct[4 * i + 1] = cv.y, ct[4 * i + 2] = cv.z, ct[4 * i + 3] = cv.w;
+                st[4 * i] = sv.x, st[4 * i + 1] = sv.y, st[4 * i + 2] = sv.z, st[4 * i + 3] = sv.w;
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float a = __uint_as_float(ra[i]), b = __uint_as_float(rb[i]);
+              if (FP8) {
+                a *= as * p.w_scale[hc + c + i];
+                b *= as * p.w_scale[hc + half + c + i];
+              }
+              if (p.bias) {
+                a += __bfloat162float(p.bias[hc + c + i]);
+                b += __bfloat162float(p.bias[hc + half + c + i]);
+              }
+              if (rot) {
+                a = bf16_round(a);
+                b = bf16_round(b);
+                const float cs = ct[i], sn = st[i];
+                va[i] = bf16_round(a * cs) + bf16_round(-b * sn);
+                vb[i] = bf16_round(b * cs) + bf16_round(a * sn);
+              } else {
+                va[i] = a;
+                vb[i] = b;
+              }
+            }
+            store_chunk<FP8>(p, row, hc + c, cols_out, va);
+            store_chunk<FP8>(p, row, hc + half + c, cols_out, vb);
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -262,7 +332,10 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
   DAN_REQUIRE((p.k * esize) % 16 == 0, "gemm: k=%d must make 16-byte rows", p.k);
   DAN_REQUIRE((lda * esize) % 16 == 0 && (ldw * esize) % 16 == 0, "gemm: lda/ldw must be 16-byte multiples");
   DAN_REQUIRE(lda >= p.k && ldw >= p.k, "gemm: leading dimensions smaller than k");
-  DAN_REQUIRE(p.epilogue >= 0 && p.epilogue <= 2, "gemm: unknown epilogue %d", p.epilogue);
+  DAN_REQUIRE(p.epilogue >= 0 && p.epilogue <= 3, "gemm: unknown epilogue %d", p.epilogue);
+  DAN_REQUIRE(p.epilogue != kRope || ((p.rope_hd == 64 || p.rope_hd == 128 || p.rope_hd == 256) &&
+                                      p.rope_cols % p.rope_hd == 0 && p.n % p.rope_hd == 0 && p.cos_t && p.sin_t),
+              "gemm: rope epilogue needs head size 64/128/256 dividing n and rope_cols, and cos/sin tables");
   DAN_REQUIRE(p.epilogue != kSwiglu || p.n % BN == 0, "gemm: swiglu needs n %% 256 == 0 (got %d)", p.n);
   DAN_REQUIRE(p.epilogue != kResidual || p.resid != nullptr, "gemm: residual epilogue without a residual");
   DAN_REQUIRE(!FP8 || (p.a_scale && p.w_scale), "gemm: e4m3 needs a_scale and w_scale");
@@ -302,10 +375,31 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
 
 using namespace dan;
 
+DAN_API int dan_gemm_bf16_rope(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
+                               const void* resid, int64_t ldr, const void* bias, int m, int n, int k, int epilogue,
+                               int rope_cols, int rope_hd, const float* cos_t, const float* sin_t, int32_t* status,
+                               void* stream);
+DAN_API int dan_gemm_e4m3_rope(const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,
+                               const float* w_scale, void* c, int64_t ldc, const void* resid, int64_t ldr,
+                               const void* bias, int m, int n, int k, int epilogue, int rope_cols, int rope_hd,
+                               const float* cos_t, const float* sin_t, int32_t* status, void* stream);
+
 DAN_API int dan_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
                           const void* resid, int64_t ldr, const void* bias, int m, int n, int k, int epilogue,
                           int32_t* status, void* stream) {
+  return dan_gemm_bf16_rope(a, lda, w, ldw, c, ldc, resid, ldr, bias, m, n, k, epilogue, 0, 0, nullptr, nullptr,
+                            status, stream);
+}
+
+DAN_API int dan_gemm_bf16_rope(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
+                               const void* resid, int64_t ldr, const void* bias, int m, int n, int k, int epilogue,
+                               int rope_cols, int rope_hd, const float* cos_t, const float* sin_t, int32_t* status,
+                               void* stream) {
   gemm::Params p{};
+  p.rope_cols = rope_cols;
+  p.rope_hd = rope_hd;
+  p.cos_t = cos_t;
+  p.sin_t = sin_t;
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
   p.resid = static_cast<const __nv_bfloat16*>(resid);
@@ -322,7 +416,19 @@ DAN_API int dan_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw
 DAN_API int dan_gemm_e4m3(const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,
                           const float* w_scale, void* c, int64_t ldc, const void* resid, int64_t ldr,
                           const void* bias, int m, int n, int k, int epilogue, int32_t* status, void* stream) {
+  return dan_gemm_e4m3_rope(a, lda, a_scale, w, ldw, w_scale, c, ldc, resid, ldr, bias, m, n, k, epilogue, 0, 0,
+                            nullptr, nullptr, status, stream);
+}
+
+DAN_API int dan_gemm_e4m3_rope(const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,
+                               const float* w_scale, void* c, int64_t ldc, const void* resid, int64_t ldr,
+                               const void* bias, int m, int n, int k, int epilogue, int rope_cols, int rope_hd,
+                               const float* cos_t, const float* sin_t, int32_t* status, void* stream) {
   gemm::Params p{};
+  p.rope_cols = rope_cols;
+  p.rope_hd = rope_hd;
+  p.cos_t = cos_t;
+  p.sin_t = sin_t;
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
   p.resid = static_cast<const __nv_bfloat16*>(resid);

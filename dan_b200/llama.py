@@ -139,6 +139,11 @@ class LlamaForReads:
             return ops.linear_swiglu(x, lin.w, lin.bias)
         return ops.linear(x, lin.w, lin.bias, residual=residual)
 
+    def _proj_rope(self, lin, x, x8, table, rope_cols):
+        if lin.fp8:
+            return ops.linear_e4m3_rope(x8[0], x8[1], lin.wq, lin.ws, table, rope_cols, self.d, lin.bias)
+        return ops.linear_rope(x, lin.w, table, rope_cols, self.d, lin.bias)
+
     def _norm(self, x, w):
         if self.fp8:
             _, q8, sc = ops.rms_norm(x, w, self.eps, fp8=True)
@@ -155,16 +160,20 @@ class LlamaForReads:
         x = ops.embed(ids, self.embed_tokens)
         lay = layout_of(segments, n, self.device)
         h, hkv, d = self.h, self.hkv, self.d
+        table = ops.rope_table(positions, self.inv_freq)
         for i, L in enumerate(self.layers):
             hn, h8 = self._norm(x, L["in_norm"])
-            qkv = self._proj(L["qkv"], hn, h8)
+            if self.qk_norm:  # RoPE after the per-head q/k norms (llama.py:82-85)
+                qkv = self._proj(L["qkv"], hn, h8)
+            else:  # RoPE fused into the projection's epilogue
+                qkv = self._proj_rope(L["qkv"], hn, h8, table, (h + hkv) * d)
             q = qkv[:, :h * d].view(n, h, d)
             k = qkv[:, h * d:(h + hkv) * d].view(n, hkv, d)
             v = qkv[:, (h + hkv) * d:].view(n, hkv, d)
             if self.qk_norm:
                 ops.rms_norm(q, L["q_norm"], self.eps, out=q)
                 ops.rms_norm(k, L["k_norm"], self.eps, out=k)
-            ops.rope_(qkv[:, :(h + hkv) * d].view(n, h + hkv, d), positions, self.inv_freq)
+                ops.rope_(qkv[:, :(h + hkv) * d].view(n, h + hkv, d), table)
             if saves is not None and self.pool is not None:
                 ops.kv_store(k, v, self.pool.k[i], self.pool.v[i], saves[0], saves[1])
             ao = torch.empty(n, h * d, dtype=torch.bfloat16, device=self.device)
@@ -189,9 +198,9 @@ class LlamaForReads:
         return self.n_layers, self.hkv, self.d
 
     def launches_per_forward(self):
-        """Kernels one forward launches (embed + per layer + readout), excluding prefix saves."""
-        per = 9 + (2 if self.qk_norm else 0) + (2 if self.fp8 else 0)
-        return 1 + per * self.n_layers + 1
+        """Kernels one forward launches (embed, rope table, per layer, readout), excluding prefix saves."""
+        per = 7 + (3 if self.qk_norm else 0) + (2 if self.fp8 else 0)
+        return 2 + per * self.n_layers + 1
 
     def linear_params(self):
         """Parameters of the decoder linears (for FLOP accounting: 2 per token each)."""

@@ -8,7 +8,7 @@ import torch
 
 from . import _lib
 
-STORE, RESIDUAL, SWIGLU = 0, 1, 2
+STORE, RESIDUAL, SWIGLU, ROPE = 0, 1, 2, 3
 
 
 def _st(t):
@@ -24,7 +24,7 @@ def linear(x, w, bias=None, residual=None, out=None):
     ep = RESIDUAL if residual is not None else STORE
     _lib.call("dan_gemm_bf16", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(out), out.stride(0),
               _lib.ptr(residual), residual.stride(0) if residual is not None else 0, _lib.ptr(bias), m, n, k, ep,
-              _st(x), _lib.stream(), work=2 * m * n * k)
+              _st(x), _lib.stream(), work=2 * m * n * k, key=f"gemm_bf16 n={n} k={k} ep={ep}")
     return out
 
 
@@ -36,7 +36,8 @@ def linear_swiglu(x, w_gate_up, bias=None, out=None):
     if out is None:
         out = torch.empty(m, n // 2, dtype=torch.bfloat16, device=x.device)
     _lib.call("dan_gemm_bf16", _lib.ptr(x), x.stride(0), _lib.ptr(w_gate_up), w_gate_up.stride(0), _lib.ptr(out),
-              out.stride(0), None, 0, _lib.ptr(bias), m, n, k, SWIGLU, _st(x), _lib.stream(), work=2 * m * n * k)
+              out.stride(0), None, 0, _lib.ptr(bias), m, n, k, SWIGLU, _st(x), _lib.stream(), work=2 * m * n * k,
+              key=f"gemm_bf16 n={n} k={k} ep=swiglu")
     return out
 
 
@@ -102,14 +103,53 @@ def rms_norm(x, weight, eps, zero_centered=False, out=None, fp8=False):
     return out
 
 
-def rope_(x, positions, inv_freq, rot=None):
+def rope_table(positions, inv_freq):
+    """(cos, sin) fp32 [N, R/2]: angles from integer positions in fp32, rounded to bf16 as the
+    reference casts them to the model dtype (llama.py:155-158). Built once per forward."""
+    n, half = positions.shape[0], inv_freq.shape[0]
+    cos = torch.empty(n, half, dtype=torch.float32, device=positions.device)
+    sin = torch.empty_like(cos)
+    _lib.call("dan_rope_table", _lib.ptr(positions), _lib.ptr(inv_freq), n, half, _lib.ptr(cos), _lib.ptr(sin),
+              _lib.stream())
+    return cos, sin
+
+
+def rope_(x, table, rot=None):
     """In-place rotate-half RoPE on the first ``rot`` dims of each head; x: [N, heads, D]
-    view (llama.py:43-45 / fused.py:69-76)."""
+    view, ``table`` from ``rope_table`` (llama.py:43-45 / fused.py:69-76)."""
     n, heads, d = x.shape
     rot = d if rot is None else rot
-    _lib.call("dan_rope", _lib.ptr(x), x.stride(0), x.stride(1), heads, d, rot, _lib.ptr(positions),
-              _lib.ptr(inv_freq), n, _lib.stream())
+    cos, sin = table
+    _lib.call("dan_rope", _lib.ptr(x), x.stride(0), x.stride(1), heads, d, rot, _lib.ptr(cos), _lib.ptr(sin), n,
+              _lib.stream(), work=n * heads * rot * 4)
     return x
+
+
+def linear_rope(x, w, table, rope_cols, head_dim, bias=None, out=None):
+    """bf16 ``x @ w.T`` (+ bias) with RoPE applied in the epilogue to every ``head_dim`` head
+    of the first ``rope_cols`` output columns (the fused q/k/v projection + rotary)."""
+    m, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    cos, sin = table
+    _lib.call("dan_gemm_bf16_rope", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(out), out.stride(0),
+              None, 0, _lib.ptr(bias), m, n, k, ROPE, rope_cols, head_dim, _lib.ptr(cos), _lib.ptr(sin), _st(x),
+              _lib.stream(), work=2 * m * n * k, key=f"gemm_bf16 n={n} k={k} ep=rope")
+    return out
+
+
+def linear_e4m3_rope(xq, x_scale, wq, w_scale, table, rope_cols, head_dim, bias=None, out=None):
+    """FP8 ``linear_rope``: per-token / per-channel scaled e4m3 GEMM with RoPE in the epilogue."""
+    m, k = xq.shape
+    n = wq.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=xq.device)
+    cos, sin = table
+    _lib.call("dan_gemm_e4m3_rope", _lib.ptr(xq), xq.stride(0), _lib.ptr(x_scale), _lib.ptr(wq), wq.stride(0),
+              _lib.ptr(w_scale), _lib.ptr(out), out.stride(0), None, 0, _lib.ptr(bias), m, n, k, ROPE, rope_cols,
+              head_dim, _lib.ptr(cos), _lib.ptr(sin), _st(xq), _lib.stream(), work=2 * m * n * k)
+    return out
 
 
 def embed(ids, table, out=None):

@@ -29,6 +29,15 @@ class KernelTimer:
     def wants(self, name):
         return self.names is None or name in self.names
 
+    def total(self, prefix):
+        """Summed {launches, ms_total, work_total} over groups whose key starts with ``prefix``."""
+        out = {"launches": 0, "ms_total": 0.0, "work_total": 0}
+        for key, v in self.summary().items():
+            if key.startswith(prefix):
+                for f in out:
+                    out[f] += v[f]
+        return out
+
     def summary(self):
         """name -> {launches, ms_total, ms_per_launch, work_total} (synchronises)."""
         torch.cuda.synchronize()

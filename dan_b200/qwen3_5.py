@@ -1,8 +1,259 @@
-"""Qwen3.5 hybrid (Gated DeltaNet + gated attention) on the dan_b200 kernels."""
+"""Qwen3.5 hybrid (Gated DeltaNet + gated attention), text only, prefill only, on the
+dan_b200 kernels.
+
+Same interface and numerics as the reference's ``Qwen35ForReads``
+(dan/models/qwen3_5.py:375-420): three of every four layers are Gated DeltaNet,
+the rest gated attention with q/k zero-centred RMSNorm, partial RoPE and a
+per-head sigmoid output gate; norms are zero-centred (x_hat * (1 + w)).
+
+Per DeltaNet layer on the GPU (qwen3_5.py:183-212): merged in_proj GEMM ->
+causal depthwise conv + SiLU over each run's ``[history; tokens]``
+(``dan_causal_conv``, history from a per-row index table) -> gated delta scan
+over the tree of runs with gates, l2-norms and q scaling fused
+(``dan_gated_delta_scan``; branches fork from the trunk's final state kept on
+chip) -> gated RMSNorm -> out_proj GEMM with the residual add fused. Prefix
+saves store the state at the save cut and the conv tail into the pool's slot.
+
+Per attention layer (qwen3_5.py:316-329): merged q/k/v GEMM -> per-head q/k
+norms in place -> partial RoPE in place -> tree attention reading the strided
+q (head stride 2d, the gate interleaved) -> sigmoid gate in place -> o GEMM +
+residual. The MLP matches the Llama path (SwiGLU fused into the gate/up GEMM).
+"""
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib, ops
+from .attention import layout_of, tree_attention
+from .llama import Linear
+
+PRE = "model.language_model."
+
+
+def remap(name):
+    """Checkpoint key -> this module's key, or None to skip (vision, MTP) (qwen3_5.py:394-401)."""
+    if name.startswith(PRE):
+        return "model." + name[len(PRE):]
+    if name.startswith("model.") and not name.startswith("model.visual"):
+        return name
+    if name.startswith("lm_head."):
+        return name
+    return None
+
+
+@dataclass
+class RecurrentLayout:
+    """Index tables of one batch for the DeltaNet layers (the reference's RecurrentLayout,
+    qwen3_5.py:240-298, as per-row conv sources and per-segment scan records)."""
+    prev: torch.Tensor  # int32 [N, 3]: conv source codes of the 1st/2nd/3rd previous rows
+    segs: torch.Tensor  # int32 [S, 8]: trunk_start, trunk_len, cut, init_slot, save_slot, branch0, n_br, 0
+    branches: torch.Tensor  # int32 [B, 2]: start, len
+    tail_codes: torch.Tensor  # int32 [saves * (k-1)]: conv-tail source codes at each save cut
+    tail_dst: list  # (slot) per save
+    n_segs: int
+    n_rows: int
+
+    @classmethod
+    def build(cls, segments, n_rows, k1, device):
+        prev = np.full((max(n_rows, 1), k1), -1, dtype=np.int32)
+        segs, brs, tail, tail_dst = [], [], [], []
+        for s in segments:
+            slot = s.past.slot if s.past else -1
+            hist = [-(2 + slot * k1 + j) for j in range(k1)] if s.past else [-1] * k1
+            virt = hist + list(range(s.start, s.start + s.trunk))
+            for t in range(s.trunk):
+                for j in range(k1):
+                    prev[s.start + t, j] = virt[k1 + t - 1 - j]
+            tail_hist = virt[-k1:]
+            for a, b in s.branches:
+                bv = tail_hist + list(range(a, b))
+                for t in range(b - a):
+                    for j in range(k1):
+                        prev[a + t, j] = bv[k1 + t - 1 - j]
+            cut = s.save if 0 < s.save < s.trunk else s.trunk
+            save_slot = s.save_entry.slot if getattr(s, "save_entry", None) is not None else -1
+            if save_slot >= 0:
+                tail += virt[cut:k1 + cut]
+                tail_dst.append(save_slot)
+            segs.append((s.start, s.trunk, cut, slot, save_slot, len(brs), len(s.branches), 0))
+            brs += [(a, b - a) for a, b in s.branches]
+        dev = torch.device(device)
+
+        def up(a, shape):
+            t = torch.from_numpy(np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(shape)))
+            return t.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else t
+
+        return cls(up(prev[:max(n_rows, 1)], (-1, k1)), up(segs, (-1, 8)), up(brs or [(0, 0)], (-1, 2)),
+                   up(tail or [0], (-1,)), tail_dst, len(segs), n_rows)
 
 
 class Qwen35ForReads:
     MODEL_TYPES = frozenset({"qwen3_5", "qwen3_5_text"})
 
-    def __init__(self, *args, **kwargs):
-        raise NotImplementedError("the Qwen3.5 DeltaNet kernels are not built yet")
+    def __init__(self, config, state, device="cuda", dtype=torch.bfloat16, quantization=None):
+        if dtype != torch.bfloat16:
+            raise ValueError("dan_b200 runs the decoder in bf16")
+        if quantization:
+            raise ValueError("FP8 is supported for the Llama family only")
+        c = self.config = dict(config.get("text_config", config))
+        self.device = torch.device(device)
+        st = {}
+        for k, v in state.items():
+            k2 = remap(k)
+            if k2 is not None:
+                st[k2] = v
+        self.h, self.hkv, self.d = c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"]
+        self.hk, self.hv = c["linear_num_key_heads"], c["linear_num_value_heads"]
+        self.dk, self.dv = c["linear_key_head_dim"], c["linear_value_head_dim"]
+        self.kconv = c["linear_conv_kernel_dim"]
+        self.conv_dim = 2 * self.hk * self.dk + self.hv * self.dv
+        self.eps = c["rms_norm_eps"]
+        self.kinds = list(c["layer_types"])
+        rp = c.get("rope_parameters") or {"rope_theta": c.get("rope_theta", 10000.0)}
+        self.rot = int(self.d * rp.get("partial_rotary_factor", 1.0))
+
+        def g(name):
+            return st[name].to(self.device, torch.bfloat16)
+
+        def g32(name):  # stored in the model dtype, used in fp32 (qwen3_5.py:188, fused.py:79-82)
+            return st[name].to(self.device, torch.bfloat16).float()
+
+        self.embed_tokens = g("model.embed_tokens.weight").contiguous()
+        self.lm_head = g("lm_head.weight").contiguous() if "lm_head.weight" in st else self.embed_tokens
+        self.norm = g("model.norm.weight")
+        self.layers = []
+        self.attn_index, self.delta_index = {}, {}
+        for i, kind in enumerate(self.kinds):
+            p = f"model.layers.{i}."
+            L = {"kind": kind, "in_norm": g(p + "input_layernorm.weight"),
+                 "post_norm": g(p + "post_attention_layernorm.weight"),
+                 "gate_up": Linear(ops.interleave_gate_up(g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight"))),
+                 "down": Linear(g(p + "mlp.down_proj.weight"))}
+            if kind == "linear_attention":
+                a = p + "linear_attn."
+                w = torch.cat([g(a + "in_proj_qkv.weight"), g(a + "in_proj_z.weight"), g(a + "in_proj_b.weight"),
+                               g(a + "in_proj_a.weight")])
+                pad = (-w.shape[0]) % 64  # keep the output row stride 16-byte aligned
+                if pad:
+                    w = torch.cat([w, w.new_zeros(pad, w.shape[1])])
+                L.update(in_proj=Linear(w), conv=g(a + "conv1d.weight").reshape(self.conv_dim, self.kconv).contiguous(),
+                         dt_bias=g32(a + "dt_bias"), a_log=g32(a + "A_log"), gnorm=g(a + "norm.weight"),
+                         out_proj=Linear(g(a + "out_proj.weight")))
+                self.delta_index[i] = len(self.delta_index)
+            else:
+                a = p + "self_attn."
+                L.update(qkv=Linear(torch.cat([g(a + "q_proj.weight"), g(a + "k_proj.weight"), g(a + "v_proj.weight")])),
+                         o=Linear(g(a + "o_proj.weight")), q_norm=g(a + "q_norm.weight"),
+                         k_norm=g(a + "k_norm.weight"))
+                self.attn_index[i] = len(self.attn_index)
+            self.layers.append(L)
+        self.inv_freq = self.frequencies(c).to(self.device)
+        self.pool = None
+
+    @staticmethod
+    def frequencies(c):
+        rp = c.get("rope_parameters") or {"rope_theta": c.get("rope_theta", 10000.0)}
+        dim = int(c["head_dim"] * rp.get("partial_rotary_factor", 1.0))
+        return 1.0 / (rp["rope_theta"] ** (torch.arange(0, dim, 2, dtype=torch.float) / dim))
+
+    def kv_layout(self):
+        return len(self.attn_index), self.hkv, self.d
+
+    def recurrent_layout(self):
+        return len(self.delta_index), self.kconv - 1, self.conv_dim, self.hv, self.dk, self.dv
+
+    def _recurrent(self, segments, n):
+        lay = getattr(segments, "recurrent", None)
+        if lay is None or lay.n_rows != n:
+            lay = RecurrentLayout.build(segments, n, self.kconv - 1, self.device)
+            segments.recurrent = lay
+        return lay
+
+    # ------------------------------------------------------------------ forward
+    def hidden(self, ids, positions, segments, saves=None):
+        """Residual-stream states [N, hidden] after the last layer (before the final norm)."""
+        n = ids.shape[0]
+        x = ops.embed(ids, self.embed_tokens)
+        table = ops.rope_table(positions, self.inv_freq)
+        lay = layout_of(segments, n, self.device)
+        rl = self._recurrent(segments, n) if self.delta_index else None
+        for i, L in enumerate(self.layers):
+            hn = ops.rms_norm(x, L["in_norm"], self.eps, zero_centered=True)
+            if L["kind"] == "linear_attention":
+                self._deltanet(i, L, hn, x, rl)
+            else:
+                self._attention(i, L, hn, x, table, lay, saves)
+            hn = ops.rms_norm(x, L["post_norm"], self.eps, zero_centered=True)
+            act = ops.linear_swiglu(hn, L["gate_up"].w)
+            ops.linear(act, L["down"].w, residual=x)
+        return x
+
+    def _deltanet(self, i, L, hn, x, rl):
+        n = hn.shape[0]
+        li = self.delta_index[i]
+        kd, vd, hv, C = self.hk * self.dk, self.hv * self.dv, self.hv, self.conv_dim
+        P = ops.linear(hn, L["in_proj"].w)
+        qkv, z = P[:, :C], P[:, C:C + vd]
+        b, a = P[:, C + vd:C + vd + hv], P[:, C + vd + hv:C + vd + 2 * hv]
+        pool = self.pool
+        hist = pool.conv[li].view(-1, C) if (pool is not None and pool.n_slots) else None
+        conv = torch.empty(n, C, dtype=torch.bfloat16, device=self.device)
+        _lib.call("dan_causal_conv", _lib.ptr(qkv), P.stride(0), _lib.ptr(hist), C if hist is not None else 0,
+                  _lib.ptr(L["conv"]), _lib.ptr(rl.prev), _lib.ptr(conv), C, n, C, _lib.stream())
+        if rl.tail_dst and hist is not None:  # conv tails at the save cuts -> pool slots
+            k1 = self.kconv - 1
+            tails = torch.empty(len(rl.tail_dst) * k1, C, dtype=torch.bfloat16, device=self.device)
+            _lib.call("dan_gather_rows", _lib.ptr(qkv), P.stride(0), _lib.ptr(hist), C, _lib.ptr(rl.tail_codes),
+                      tails.shape[0], _lib.ptr(tails), C, C, _lib.stream())
+            for j, slot in enumerate(rl.tail_dst):
+                pool.conv[li, slot].copy_(tails[j * k1:(j + 1) * k1])
+        state = pool.state[li] if (pool is not None and pool.n_slots) else None
+        out = torch.empty(n, vd, dtype=torch.bfloat16, device=self.device)
+        _lib.call("dan_gated_delta_scan", _lib.ptr(conv[:, :kd]), _lib.ptr(conv[:, kd:2 * kd]), _lib.ptr(conv[:, 2 * kd:]),
+                  C, _lib.ptr(b), _lib.ptr(a), P.stride(0), _lib.ptr(L["a_log"]), _lib.ptr(L["dt_bias"]),
+                  _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), _lib.ptr(state),
+                  state.stride(0) if state is not None else 0, _lib.ptr(out), vd, self.hk, hv, self.dk, self.dv,
+                  float(self.dk ** -0.5), _lib.stream())
+        y = torch.empty_like(out)
+        _lib.call("dan_gated_rms_norm", _lib.ptr(out), vd, _lib.ptr(z), P.stride(0), _lib.ptr(L["gnorm"]),
+                  float(self.eps), _lib.ptr(y), vd, n, hv, self.dv, _lib.stream())
+        ops.linear(y, L["out_proj"].w, residual=x)
+
+    def _attention(self, i, L, hn, x, table, lay, saves):
+        n = hn.shape[0]
+        h, hkv, d = self.h, self.hkv, self.d
+        qkv = ops.linear(hn, L["qkv"].w)
+        qg = qkv[:, :h * 2 * d].view(n, h, 2 * d)
+        q, gate = qg[:, :, :d], qg[:, :, d:]
+        k = qkv[:, h * 2 * d:h * 2 * d + hkv * d].view(n, hkv, d)
+        v = qkv[:, h * 2 * d + hkv * d:].view(n, hkv, d)
+        ops.rms_norm(q, L["q_norm"], self.eps, zero_centered=True, out=q)
+        ops.rms_norm(k, L["k_norm"], self.eps, zero_centered=True, out=k)
+        ops.rope_(q, table, self.rot)
+        ops.rope_(k, table, self.rot)
+        ai = self.attn_index[i]
+        if saves is not None and self.pool is not None:
+            ops.kv_store(k, v, self.pool.k[ai], self.pool.v[ai], saves[0], saves[1])
+        ao = torch.empty(n, h * d, dtype=torch.bfloat16, device=self.device)
+        tree_attention(q, k, v, lay, out=ao.view(n, h, d), pool=self.pool, layer=ai)
+        ops.sigmoid_gate_(ao, gate, d)
+        ops.linear(ao, L["o"].w, residual=x)
+
+    def readout(self, x, read_rows, label_ids, offsets, max_labels):
+        return ops.label_readout(x, read_rows, self.norm, self.eps, True, self.lm_head, label_ids, offsets,
+                                 max_labels)
+
+    def label_logits(self, h, label_ids):
+        return self.lm_head[torch.as_tensor(label_ids, device=self.device)].float() @ h.float()
+
+    def linear_params(self):
+        c, hd = self.config, self.config["hidden_size"]
+        total = 0
+        for L in self.layers:
+            total += 3 * hd * c["intermediate_size"]
+            if L["kind"] == "linear_attention":
+                total += hd * (self.conv_dim + self.hv * self.dv + 2 * self.hv) + self.hv * self.dv * hd
+            else:
+                total += hd * (self.h * 2 * self.d + 2 * self.hkv * self.d) + self.h * self.d * hd
+        return total

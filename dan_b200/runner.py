@@ -85,6 +85,7 @@ class Runner:
                 seg.save = 0
                 continue
             pinned.append(entry)
+            seg.save_entry = entry
             out.append((static, seg, entry))
             src += range(seg.start, seg.start + seg.save)
             dst += self.cache.rows(entry, seg.save)
@@ -117,8 +118,6 @@ class Runner:
                 self.cache.release(entry)
             raise
         for static, seg, entry in held:
-            if hasattr(model, "save_recurrent"):
-                model.save_recurrent(seg, entry)
             self.cache.commit(static, entry)
         return logits, probs, offsets
 

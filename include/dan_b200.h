@@ -73,10 +73,27 @@ int dan_rms_norm(const void* x, int64_t x_outer, int64_t x_inner, int inner, con
 int dan_quantize_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, float* scale, int rows, int cols,
                       void* stream);
 
-/* In-place rotate-half RoPE on the first ``rot`` dims of each head (dan/models/llama.py:43-45,
- * 155-158; rotate_partial, dan/fused.py:69-76). */
-int dan_rope(void* x, int64_t ld_row, int64_t ld_head, int heads, int head_dim, int rot, const int64_t* pos,
-             const float* inv_freq, int rows, void* stream);
+/* GEMMs with epilogue 3: RoPE on every rope_hd-column head of the first rope_cols output
+ * columns, from cos/sin tables [m, rope_hd/2] (the q/k/v projection + rotary of
+ * dan/models/llama.py:78-85 in one kernel). Other epilogues as dan_gemm_bf16 / dan_gemm_e4m3. */
+int dan_gemm_bf16_rope(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
+                       const void* resid, int64_t ldr, const void* bias, int m, int n, int k, int epilogue,
+                       int rope_cols, int rope_hd, const float* cos_t, const float* sin_t, int32_t* status,
+                       void* stream);
+int dan_gemm_e4m3_rope(const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,
+                       const float* w_scale, void* c, int64_t ldc, const void* resid, int64_t ldr, const void* bias,
+                       int m, int n, int k, int epilogue, int rope_cols, int rope_hd, const float* cos_t,
+                       const float* sin_t, int32_t* status, void* stream);
+
+/* cos/sin tables [rows, half] of angle = float(pos) * inv_freq, rounded to bf16 as the reference
+ * casts them (dan/models/llama.py:155-158; qwen3_5.py:411-414). Built once per forward. */
+int dan_rope_table(const int64_t* pos, const float* inv_freq, int rows, int half, float* cos_t, float* sin_t,
+                   void* stream);
+
+/* In-place rotate-half RoPE on the first ``rot`` dims of each head from the tables
+ * (dan/models/llama.py:43-45; rotate_partial, dan/fused.py:69-76). */
+int dan_rope(void* x, int64_t ld_row, int64_t ld_head, int heads, int head_dim, int rot, const float* cos_t,
+             const float* sin_t, int rows, void* stream);
 
 /* o *= sigmoid(gate), gate read per head (sigmoid_gate, dan/fused.py:64-66; qwen3_5.py:328). */
 int dan_sigmoid_gate(void* o, int64_t ldo, const void* g, int64_t ldg, int64_t g_head_stride, int head_dim, int rows,

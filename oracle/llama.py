@@ -64,7 +64,19 @@ def head_dim(config):
     return config.get("head_dim") or config["hidden_size"] // config["num_attention_heads"]
 
 
-def hidden(state, config, ids, positions, segments):
+def _linear(state, name, x, fp8):
+    """x @ W^T in fp32, or the FP8 restatement (oracle.fp8) with per-output-row weight scales and
+    per-token activation scales (dan/quant.py:26-42) when ``fp8``."""
+    w = state[name]
+    if not fp8:
+        return x @ w.T
+    from . import fp8 as F8
+
+    wq, ws = F8.quantize_rows(w)
+    return F8.linear(x, wq, ws.flatten())
+
+
+def hidden(state, config, ids, positions, segments, fp8=False):
     """Final-normed hidden states [N, hidden] of a packed batch.
 
     ``segments``: list of dicts ``{"start", "end", "branch", "past": {layer: (k, v)} or None,
@@ -83,9 +95,9 @@ def hidden(state, config, ids, positions, segments):
     for i in range(c["num_hidden_layers"]):
         p = f"model.layers.{i}."
         h = rms_norm(x, state[p + "input_layernorm.weight"], eps)
-        q = (h @ state[p + "self_attn.q_proj.weight"].T).reshape(n, nh, d)
-        k = (h @ state[p + "self_attn.k_proj.weight"].T).reshape(n, nkv, d)
-        v = (h @ state[p + "self_attn.v_proj.weight"].T).reshape(n, nkv, d)
+        q = _linear(state, p + "self_attn.q_proj.weight", h, fp8).reshape(n, nh, d)
+        k = _linear(state, p + "self_attn.k_proj.weight", h, fp8).reshape(n, nkv, d)
+        v = _linear(state, p + "self_attn.v_proj.weight", h, fp8).reshape(n, nkv, d)
         if c["model_type"] == "qwen3":
             q = rms_norm(q, state[p + "self_attn.q_norm.weight"], eps)
             k = rms_norm(k, state[p + "self_attn.k_norm.weight"], eps)
@@ -101,11 +113,11 @@ def hidden(state, config, ids, positions, segments):
             segs.append({"start": s["start"], "end": s["end"], "branch": s["branch"], "past": past})
         o = attention.attend(q, k, v, segs)
         o = o.transpose(0, 1).reshape(n, nh * d)
-        x = x + o @ state[p + "self_attn.o_proj.weight"].T
+        x = x + _linear(state, p + "self_attn.o_proj.weight", o, fp8)
         h = rms_norm(x, state[p + "post_attention_layernorm.weight"], eps)
-        g = h @ state[p + "mlp.gate_proj.weight"].T
-        u = h @ state[p + "mlp.up_proj.weight"].T
-        x = x + (F.silu(g) * u) @ state[p + "mlp.down_proj.weight"].T
+        g = _linear(state, p + "mlp.gate_proj.weight", h, fp8)
+        u = _linear(state, p + "mlp.up_proj.weight", h, fp8)
+        x = x + _linear(state, p + "mlp.down_proj.weight", F.silu(g) * u, fp8)
     return rms_norm(x, state["model.norm.weight"], eps)
 
 

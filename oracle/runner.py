@@ -91,13 +91,14 @@ def pack(plans, cache=None, use_cache=True):
     return ids, pos, segs, reads, stores
 
 
-def read_many(state, config, plans, cache=None):
-    """Per plan, per branch: fp32 label logits (runner.py:66-82)."""
+def read_many(state, config, plans, cache=None, fp8=False):
+    """Per plan, per branch: fp32 label logits (runner.py:66-82); ``fp8``: decoder linears
+    through the FP8 restatement (Llama family only)."""
     arch = qwen3_5 if config["model_type"].startswith("qwen3_5") else llama
     ids, pos, segs, reads, stores = pack(plans, cache)
     flat = []
     if reads:
-        h = arch.hidden(state, config, ids, pos, segs)
+        h = arch.hidden(state, config, ids, pos, segs, fp8=True) if fp8 else arch.hidden(state, config, ids, pos, segs)
         flat = [arch.label_logits(state, h[r], labels) for r, labels in reads]
         for static, seg in stores:
             cache.put(static, seg["saved"])

@@ -192,7 +192,8 @@ def main():
                              ("mixed", [cache_plans[1], extra[0], cache_plans[0]])], "tiny_llama.json")
 
     # a small Qwen3.5 hybrid; trunks longer than one 64-token delta-rule chunk
-    cfgh = weights.qwen35_config()
+    # DeltaNet heads of 128 (the Qwen3.5 head size the scan kernel is built for), small elsewhere
+    cfgh = weights.qwen35_config(heads=2, kv_heads=1, lin_k_heads=1, lin_v_heads=2, lin_k_dim=128, lin_v_dim=128)
     rng = random.Random(3)
     hp = small_plans(rng, cfgh["vocab_size"], 3, trunk=(70, 150), nb=(1, 3), blen=(3, 9), static=(20, 60))
     hx = small_plans(rng, cfgh["vocab_size"], 1, trunk=(70, 150), nb=(1, 3), blen=(3, 9), static=(20, 60))

@@ -48,3 +48,21 @@ def test_without_cache_same_answers(cuda, tiny_dir):
     for pp, want in zip(probs, b["runner"]):
         for p, w in zip(pp, want):
             assert (p - torch.softmax(torch.tensor(w).double(), 0).float()).abs().max() < 5e-3
+
+
+def test_tiny_llama_fp8_matches_fp8_oracle(cuda, tiny_dir):
+    """FP8 e4m3 decoder linears (configuration 5's quantisation) vs the FP8 restatement of the
+    reference (oracle.fp8, parity unpinned upstream) at the north-star 3e-2 probability bound."""
+    from oracle import runner as OR
+
+    path, g = tiny_dir
+    runner = Runner(path, cuda, quantization="fp8", cache_bytes=0)
+    state = weights.random_state(g["config"], g["seed"])
+    plans = plans_from_json(g["batches"][0]["plans"])
+    _, probs = runner.read_many(plans, probabilities=True)
+    want = OR.read_many(state, g["config"], plans, fp8=True)
+    worst = 0.0
+    for pp, ww in zip(probs, want):
+        for p, w in zip(pp, ww):
+            worst = max(worst, (p - torch.softmax(w.double(), 0).float()).abs().max().item())
+    assert worst < 3e-2, worst

@@ -98,21 +98,51 @@ def test_rms_norm_fp8_fused(cuda):
     assert torch.equal(q8.float().cpu(), oq) and torch.allclose(sc.cpu(), osc.flatten())
 
 
-@pytest.mark.parametrize("rot", [128, 64])
-def test_rope(cuda, rot):
+def _rope_ref(x, pos, inv, rot):
     from oracle.llama import rotate
 
+    ang = pos.float()[:, None] * inv[None]
+    ang = torch.cat([ang, ang], -1)
+    cos, sin = ang.cos().bfloat16().float(), ang.sin().bfloat16().float()
+    return torch.cat([rotate(x.float()[..., :rot], cos[:, None], sin[:, None]), x.float()[..., rot:]], -1)
+
+
+@pytest.mark.parametrize("rot", [128, 64])
+def test_rope(cuda, rot):
     g = torch.Generator(device=cuda).manual_seed(6)
     n, heads, d = 50, 6, 128
     x = torch.randn(n, heads, d, device=cuda, generator=g).bfloat16()
     pos = torch.randint(0, 5000, (n,), device=cuda, generator=g)
     inv = 1.0 / (500000.0 ** (torch.arange(0, rot, 2, dtype=torch.float32, device=cuda) / rot))
-    ang = pos.float()[:, None] * inv[None]
-    ang = torch.cat([ang, ang], -1)
-    cos, sin = ang.cos().bfloat16().float(), ang.sin().bfloat16().float()
-    want = torch.cat([rotate(x.float()[..., :rot], cos[:, None], sin[:, None]), x.float()[..., rot:]], -1)
-    ops.rope_(x, pos, inv, rot)
+    want = _rope_ref(x, pos, inv, rot)
+    ops.rope_(x, ops.rope_table(pos, inv), rot)
     assert rel_err(x, want) < 1e-2
+
+
+@pytest.mark.parametrize("d,heads,kv", [(128, 4, 2), (64, 9, 3)])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_gemm_rope_epilogue(cuda, d, heads, kv, fp8):
+    """q/k/v projection with RoPE on the q and k heads in the GEMM epilogue."""
+    g = torch.Generator(device=cuda).manual_seed(8)
+    m, k = 300, 256
+    n = (heads + 2 * kv) * d
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=cuda, generator=g) * 0.1).bfloat16()
+    pos = torch.randint(0, 3000, (m,), device=cuda, generator=g)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, d, 2, dtype=torch.float32, device=cuda) / d))
+    table = ops.rope_table(pos, inv)
+    if fp8:
+        xq, xs = ops.quantize_e4m3(x)
+        wq, ws = ops.quantize_e4m3(w)
+        y = ops.linear_e4m3_rope(xq, xs, wq, ws, table, (heads + kv) * d, d)
+        proj = ops.linear_e4m3(xq, xs, wq, ws)
+    else:
+        y = ops.linear_rope(x, w, table, (heads + kv) * d, d)
+        proj = ops.linear(x, w)
+    want = proj.float().clone()
+    want[:, :(heads + kv) * d] = _rope_ref(proj[:, :(heads + kv) * d].view(m, heads + kv, d), pos, inv,
+                                           d).reshape(m, -1)
+    assert rel_err(y, want) < 1e-2
 
 
 def test_embed_and_readout(cuda):
