@@ -360,16 +360,18 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, 
 }
 
 // ---------------------------------------------------------------------------------
-// Paired-head variant: one CTA = one 128-row query tile x two query heads that share a
-// KV head (GQA). Both heads have the same key blocks and masks, so each K/V tile is
-// loaded once for 2 x 128 query rows, and the two softmax warpgroups ping-pong with
-// the tensor core:
+// Paired-head persistent variant. A work item is one 128-row query tile x two query
+// heads that share a KV head (GQA): both heads have the same key blocks and masks, so
+// each K/V tile is loaded once for 2 x 128 query rows. One CTA per SM walks the
+// LPT-ordered items (tile-major, so CTAs running at the same time share K/V in L2) with
+// barrier phases carried across items: the next item's Q, K and V loads and its first
+// QK products overlap the current item's softmax tail and epilogue.
+// The two softmax warpgroups ping-pong with the tensor core:
 //   MMA issue order  QK0(0) QK1(0) PV0(0) | QK0(j) PV1(j-1) QK1(j) PV0(j) | ... PV1(last)
-// so softmax 0 of block j runs under QK1(j) + PV1(j-1), softmax 1 under PV0(j) + QK0(j+1).
-// A commit arrives only after every earlier MMA of the issuing thread completed, so
-// when a softmax warp sees S_h(j) the product PV_h(j-1) is already in O_h and the
-// lazy O rescale needs no further wait. S is read from TMEM in two passes (row max,
-// then exp + bf16 pack into P over the consumed S columns) to keep registers low.
+// A commit arrives only after every earlier MMA of the issuing thread completed, so when
+// a softmax warp sees S_h(j) the product PV_h(j-1) is already in O_h and the lazy O
+// rescale needs no further wait. Each row's visible keys within a block are three
+// intervals (past, trunk, own branch), turned into a 128-bit mask once per block.
 // Warps: 0 TMA, 1 MMA, 2-5 softmax head 2p, 6-9 softmax head 2p+1 (320 threads).
 // TMEM: S_0 [0,128), S_1 [128,256), O_0 [256, 256+D), O_1 [256+D, 256+2D).
 template <int D>
@@ -383,11 +385,20 @@ struct PairCfg {
   static constexpr int THREADS = 320;
 };
 
+// bits [lo, hi) of a 32-bit word (arguments relative to the word's first column)
+__device__ __forceinline__ uint32_t span_bits(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 32);
+  if (hi <= lo) return 0u;
+  const uint32_t upto = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+  return upto & ~((1u << lo) - 1u);
+}
+
 template <int D>
 __global__ void __launch_bounds__(320, 1)
     tree_attention_pair_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                                const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tpk,
-                               const __grid_constant__ CUtensorMap tpv, Params p) {
+                               const __grid_constant__ CUtensorMap tpv, Params p, int n_items) {
   using C = PairCfg<D>;
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
@@ -397,23 +408,25 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sv = sk + NS * C::KV_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sv + NS * C::KV_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
+  uint64_t* q_empty = q_full + 1;
+  uint64_t* k_full = q_empty + 1;
   uint64_t* v_full = k_full + NS;
   uint64_t* k_empty = v_full + NS;
   uint64_t* v_empty = k_empty + NS;
   uint64_t* s_full = v_empty + NS;  // [2] per head
   uint64_t* p_full = s_full + 2;    // [2] per head
   uint64_t* pv_done = p_full + 2;   // [2] per head
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* o_free = pv_done + 2;   // [2] per head: epilogue finished reading O_h
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
 
-  const int head0 = 2 * blockIdx.x;
-  const int kvh = head0 / (p.n_heads / p.n_kv_heads);
-  const Tile tile = reinterpret_cast<const Tile*>(p.tiles)[blockIdx.y];
-  const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+  const int npairs = p.n_heads / 2;
+  const int rep = p.n_heads / p.n_kv_heads;
+  const Tile* tiles = reinterpret_cast<const Tile*>(p.tiles);
   const int warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -424,6 +437,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&s_full[h], 1);
       mbar_init(&p_full[h], 4);
       mbar_init(&pv_done[h], 1);
+      mbar_init(&o_free[h], 4);
     }
     fence_barrier_init();
   }
@@ -441,49 +455,62 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_expect_tx(q_full, 2 * C::Q_BYTES);
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_3d(sq + h * C::Q_BYTES + c * CHUNK, &tq, q_full, c * 64, head0 + h, tile.row0);
-      for (int j = 0; j < nblk; ++j) {
-        const int stage = j % NS;
-        const uint32_t ph = (j / NS) & 1;
-        const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
-        const int kb = b * BN;
-        const bool pool = kb < tile.ppad;
-        const int row = pool ? p.pages[tile.page0 + b] * BN : tile.seg_start + (kb - tile.ppad);
-        const CUtensorMap* mk = pool ? &tpk : &tk;
-        const CUtensorMap* mv = pool ? &tpv : &tv;
-        if (!mbar_wait(&k_empty[stage], ph ^ 1)) {
+      uint32_t gb = 0, it = 0;
+      for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++it) {
+        const Tile tile = tiles[w / npairs];
+        const int head0 = 2 * (w % npairs), kvh = head0 / rep;
+        const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+        if (!mbar_wait(q_empty, (it & 1) ^ 1)) {
           report(p.status, kTimeoutEmpty);
           break;
         }
-        mbar_expect_tx(&k_full[stage], C::KV_BYTES);
+        mbar_expect_tx(q_full, 2 * C::Q_BYTES);
 #pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_3d(sk + stage * C::KV_BYTES + c * CHUNK, mk, &k_full[stage], c * 64, kvh, row);
-        if (!mbar_wait(&v_empty[stage], ph ^ 1)) {
-          report(p.status, kTimeoutEmpty);
-          break;
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_3d(sq + h * C::Q_BYTES + c * CHUNK, &tq, q_full, c * 64, head0 + h, tile.row0);
+        bool ok = true;
+        for (int j = 0; j < nblk; ++j, ++gb) {
+          const int stage = gb % NS;
+          const uint32_t ph = (gb / NS) & 1;
+          const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
+          const int kb = b * BN;
+          const bool pool = kb < tile.ppad;
+          const int row = pool ? p.pages[tile.page0 + b] * BN : tile.seg_start + (kb - tile.ppad);
+          const CUtensorMap* mk = pool ? &tpk : &tk;
+          const CUtensorMap* mv = pool ? &tpv : &tv;
+          if (!mbar_wait(&k_empty[stage], ph ^ 1)) {
+            report(p.status, kTimeoutEmpty);
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&k_full[stage], C::KV_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_3d(sk + stage * C::KV_BYTES + c * CHUNK, mk, &k_full[stage], c * 64, kvh, row);
+          if (!mbar_wait(&v_empty[stage], ph ^ 1)) {
+            report(p.status, kTimeoutEmpty);
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&v_full[stage], C::KV_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_3d(sv + stage * C::KV_BYTES + c * CHUNK, mv, &v_full[stage], c * 64, kvh, row);
         }
-        mbar_expect_tx(&v_full[stage], C::KV_BYTES);
-#pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_3d(sv + stage * C::KV_BYTES + c * CHUNK, mv, &v_full[stage], c * 64, kvh, row);
+        if (!ok) break;
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc_qk = idesc_bf16(BM, BN, false, false);
       constexpr uint32_t idesc_pv = idesc_bf16(BM, D, false, true);
-      bool ok = mbar_wait(q_full, 0);
-      if (!ok) report(p.status, kTimeoutFull);
-      tc_fence_after();
-      auto qk = [&](int h, int j) -> bool {
-        const int st = j % NS;
-        if (h == 0 && !mbar_wait(&k_full[st], (j / NS) & 1)) {
+      uint32_t gb = 0, it = 0;
+      bool ok = true;
+      auto qk = [&](int h, uint32_t g, bool last) -> bool {
+        const int st = g % NS;
+        if (h == 0 && !mbar_wait(&k_full[st], (g / NS) & 1)) {
           report(p.status, kTimeoutFull);
           return false;
         }
@@ -496,16 +523,23 @@ __global__ void __launch_bounds__(320, 1)
                      kk > 0);
         }
         mma_commit(&s_full[h]);
-        if (h == 1) mma_commit(&k_empty[st]);
+        if (h == 1) {
+          mma_commit(&k_empty[st]);
+          if (last) mma_commit(q_empty);
+        }
         return true;
       };
-      auto pv = [&](int h, int j) -> bool {
-        const int st = j % NS;
-        if (!mbar_wait(&p_full[h], j & 1)) {
+      auto pv = [&](int h, uint32_t g, bool first) -> bool {
+        const int st = g % NS;
+        if (first && !mbar_wait(&o_free[h], (it & 1) ^ 1)) {
           report(p.status, kTimeoutSoftmax);
           return false;
         }
-        if (h == 0 && !mbar_wait(&v_full[st], (j / NS) & 1)) {
+        if (!mbar_wait(&p_full[h], g & 1)) {
+          report(p.status, kTimeoutSoftmax);
+          return false;
+        }
+        if (h == 0 && !mbar_wait(&v_full[st], (g / NS) & 1)) {
           report(p.status, kTimeoutFull);
           return false;
         }
@@ -514,121 +548,155 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
           mma_f16_ts(tmem + 256 + h * D, tmem + h * 128 + kk * 8, desc_sw128(v0 + kk * 2048, CHUNK, 1024),
-                     idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                     idesc_pv, (!first || kk > 0) ? 1u : 0u);
         mma_commit(&pv_done[h]);
         if (h == 1) mma_commit(&v_empty[st]);
         return true;
       };
-      for (int j = 0; ok && j < nblk; ++j) {
-        if (!qk(0, j)) break;
-        if (j > 0 && !pv(1, j - 1)) break;
-        if (!qk(1, j)) break;
-        if (!pv(0, j)) break;
-        if (j == nblk - 1) pv(1, j);
+      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+        const Tile tile = tiles[w / npairs];
+        const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+        if (!mbar_wait(q_full, it & 1)) {
+          report(p.status, kTimeoutFull);
+          break;
+        }
+        for (int j = 0; j < nblk; ++j) {
+          const uint32_t g = gb + j;
+          if (!(ok = qk(0, g, false))) break;
+          if (j > 0 && !(ok = pv(1, g - 1, j == 1))) break;
+          if (!(ok = qk(1, g, j == nblk - 1))) break;
+          if (!(ok = pv(0, g, j == 0))) break;
+        }
+        if (ok && nblk > 0) ok = pv(1, gb + nblk - 1, nblk == 1);
+        gb += nblk;
       }
     }
   } else {
     const int hsel = (warp - 2) >> 2;  // 0: head 2p, 1: head 2p+1
-    const int head = head0 + hsel;
     const int sub = warp & 3;
     const int r_in = sub * 32 + lane;
-    const int row = tile.row0 + r_in;
-    const bool valid = r_in < tile.nrows;
-    const int qv = tile.q0v + r_in;
-    const int own = valid ? tile.ppad + (p.row_own[row] - tile.seg_start) : 0;
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + hsel * 128;
     const uint32_t o_addr = tmem + lane_base + 256 + hsel * D;
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f;  // m in log2 units (scaled)
+    uint32_t gb = 0;
     bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
-      const int kb = b * BN;
-      const bool full = (kb + BN <= tile.past) ||
-                        (kb >= tile.ppad && kb + BN <= tile.split && kb + BN - 1 <= tile.q0v);
-      if (!mbar_wait(&s_full[hsel], j & 1)) {
-        report(p.status, kTimeoutMma);
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // pass 1: row max of the visible raw scores
-      float mx = -INFINITY;
+    for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+      const Tile tile = tiles[w / npairs];
+      const int head = 2 * (w % npairs) + hsel;
+      const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+      const int row = tile.row0 + r_in;
+      const bool valid = r_in < tile.nrows;
+      const int qv = tile.q0v + r_in;
+      const int own = valid ? tile.ppad + (p.row_own[row] - tile.seg_start) : tile.ppad;
+      const int e_past = min(tile.past, qv + 1), e_trunk = min(tile.split, qv + 1);
+      float m = -INFINITY, l = 0.f;  // m in log2 units (scaled)
+      for (int j = 0; j < nblk; ++j) {
+        const uint32_t g = gb + j;
+        const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
+        const int kb = b * BN;
+        const bool full = (kb + BN <= tile.past) ||
+                          (kb >= tile.ppad && kb + BN <= tile.split && kb + BN - 1 <= tile.q0v);
+        uint32_t mw[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t s[32];
-        tmem_ld32(s_addr + 32 * c, s);
-        tmem_wait_ld();
-        if (full) {
+        for (int c = 0; c < 4; ++c) {
+          const int base = kb + 32 * c;
+          mw[c] = full ? 0xffffffffu
+                       : (span_bits(-base, e_past - base) | span_bits(tile.ppad - base, e_trunk - base) |
+                          span_bits(own - base, qv + 1 - base));
+        }
+        if (!mbar_wait(&s_full[hsel], g & 1)) {
+          report(p.status, kTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // pass 1: row max of the visible raw scores (two 64-column TMEM loads)
+        float mx = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
-        } else {
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t s0[32], s1[32];
+          tmem_ld32(s_addr + 64 * hh, s0);
+          tmem_ld32(s_addr + 64 * hh + 32, s1);
+          tmem_wait_ld();
+          const uint32_t m0 = mw[2 * hh], m1 = mw[2 * hh + 1];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int v = kb + 32 * c + i;
-            const bool vis = v <= qv && (v < tile.split || v >= own) && (v < tile.past || v >= tile.ppad);
-            if (vis) mx = fmaxf(mx, __uint_as_float(s[i]));
+            mx = fmaxf(mx, ((m0 >> i) & 1u) ? __uint_as_float(s0[i]) : -INFINITY);
+            mx = fmaxf(mx, ((m1 >> i) & 1u) ? __uint_as_float(s1[i]) : -INFINITY);
           }
         }
-      }
-      const float m_new = fmaxf(m, mx * sl2);
-      bool rescale = false;
-      float alpha = 1.f;
-      if (m_new != -INFINITY) {
-        if (m == -INFINITY) {
-          m = m_new;
-        } else if (m_new > m + 8.f) {
-          alpha = fast_exp2(m - m_new);
-          m = m_new;
-          rescale = true;
-        }
-      }
-      const float mu = m == -INFINITY ? 0.f : m;
-      // pass 2: P = exp2(s * scale_log2 - m) as bf16 pairs over the consumed S columns
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t s[32];
-        tmem_ld32(s_addr + 32 * c, s);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x0 = __uint_as_float(s[2 * i]), x1 = __uint_as_float(s[2 * i + 1]);
-          if (!full) {
-            const int v = kb + 32 * c + 2 * i;
-            if (!(v <= qv && (v < tile.split || v >= own) && (v < tile.past || v >= tile.ppad))) x0 = -INFINITY;
-            if (!(v + 1 <= qv && (v + 1 < tile.split || v + 1 >= own) && (v + 1 < tile.past || v + 1 >= tile.ppad)))
-              x1 = -INFINITY;
+        const float m_new = fmaxf(m, mx * sl2);
+        bool rescale = false;
+        float alpha = 1.f;
+        if (m_new != -INFINITY) {
+          if (m == -INFINITY) {
+            m = m_new;
+          } else if (m_new > m + 8.f) {
+            alpha = fast_exp2(m - m_new);
+            m = m_new;
+            rescale = true;
           }
-          const float p0 = fast_exp2(fmaf(x0, sl2, -mu)), p1 = fast_exp2(fmaf(x1, sl2, -mu));
-          sum += p0 + p1;
-          pk[i] = pack_bf16(p0, p1);
         }
-        tmem_st16(s_addr + 16 * c, pk);
-      }
-      l = l * alpha + sum;
-      if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c, o);
+        const float mu = m == -INFINITY ? 0.f : m;
+        // pass 2: P = exp2(s * scale_log2 - m) as bf16 pairs over the consumed S columns
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t s0[32], s1[32];
+          tmem_ld32(s_addr + 64 * hh, s0);
+          tmem_ld32(s_addr + 64 * hh + 32, s1);
           tmem_wait_ld();
+          const uint32_t m0 = mw[2 * hh], m1 = mw[2 * hh + 1];
+          {
+            uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(o_addr + c, o);
+            for (int i = 0; i < 16; ++i) {
+              const float a0 = ((m0 >> (2 * i)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s0[2 * i]), sl2, -mu)) : 0.f;
+              const float a1 =
+                  ((m0 >> (2 * i + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s0[2 * i + 1]), sl2, -mu)) : 0.f;
+              sum0 += a0 + a1;
+              pk[i] = pack_bf16(a0, a1);
+            }
+            tmem_st16(s_addr + 32 * hh, pk);
+          }
+          {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float b0 = ((m1 >> (2 * i)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s1[2 * i]), sl2, -mu)) : 0.f;
+              const float b1 =
+                  ((m1 >> (2 * i + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s1[2 * i + 1]), sl2, -mu)) : 0.f;
+              sum1 += b0 + b1;
+              pk[i] = pack_bf16(b0, b1);
+            }
+            tmem_st16(s_addr + 32 * hh + 16, pk);
+          }
         }
+        l = l * alpha + (sum0 + sum1);
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_addr + c, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[hsel]);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[hsel]);
-    }
-    if (ok && nblk > 0) {
-      if (!mbar_wait(&pv_done[hsel], (nblk - 1) & 1)) {
-        report(p.status, kTimeoutMma);
-      } else {
+      if (!ok) break;
+      if (nblk > 0) {
+        const uint32_t last = gb + nblk - 1;
+        if (!mbar_wait(&pv_done[hsel], last & 1)) {
+          report(p.status, kTimeoutMma);
+          break;
+        }
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
@@ -648,6 +716,10 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[hsel]);
+      gb += nblk;
     }
     tc_fence_before();
   }
@@ -668,8 +740,10 @@ int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
                                   PairCfg<D>::SMEM));
     configured = true;
   }
-  dim3 grid(p.n_heads / 2, n_tiles);
-  tree_attention_pair_kernel<D><<<grid, PairCfg<D>::THREADS, PairCfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, p);
+  const int items = n_tiles * (p.n_heads / 2);
+  const int grid = items < sm_count() ? items : sm_count();
+  tree_attention_pair_kernel<D><<<grid, PairCfg<D>::THREADS, PairCfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, p,
+                                                                                        items);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }
