@@ -28,7 +28,7 @@ SIGNATURES = {
                            I32),
     "dan_rope_table": ([P, P, I32, I32, P, P, P], I32),
     "dan_tree_attention": ([P, I64, I64, P, I64, I64, P, I64, I64, P, P, I64, I64, I32, P, I64, I64, I32, I32, I32,
-                            I32, P, I32, P, P, F32, P, P], I32),
+                            I32, P, I32, P, P, P, I32, F32, P, P], I32),
     "dan_embed": ([P, P, I64, I64, P, I64, I32, I32, P, P], I32),
     "dan_rms_norm": ([P, I64, I64, I32, P, F32, I32, P, I64, I64, P, I64, P, I32, I32, P], I32),
     "dan_quantize_e4m3": ([P, I64, P, I64, P, I32, I32, P], I32),

@@ -142,8 +142,54 @@ class TreeLayout:
             t = torch.from_numpy(np.ascontiguousarray(a))
             return t.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else t
 
-        return cls(up(tiles), up(own[:n_rows] if n_rows else own), up(pg), len(recs), n_rows,
-                   useful_pairs(segments), blocks)
+        lay = cls(up(tiles), up(own[:n_rows] if n_rows else own), up(pg), len(recs), n_rows,
+                  useful_pairs(segments), blocks)
+        lay.costs = (tiles[:, 6] + tiles[:, 8] - tiles[:, 7]).astype(np.int64) if len(recs) else np.zeros(0, np.int64)
+        lay.device = dev
+        lay._sched = {}
+        return lay
+
+    # A work item (one tile x one pair of query heads) costs its key blocks plus a fixed
+    # per-item share (Q load, pipeline fill, epilogue), in block units.
+    ITEM_OVERHEAD = 1.5
+
+    def schedule(self, n_pairs, n_ctas):
+        """Greedy longest-processing-time assignment of the paired kernel's work items to
+        ``n_ctas`` persistent CTAs: (device int32 CSR schedule, number of CTAs)."""
+        key = (n_pairs, n_ctas)
+        hit = self._sched.get(key)
+        if hit is not None:
+            return hit
+        import heapq
+
+        n_items = self.n_tiles * n_pairs
+        ctas = min(n_ctas, n_items)
+        cost = np.repeat(self.costs, n_pairs) + self.ITEM_OVERHEAD  # item w = tile * n_pairs + pair
+        order = np.argsort(-cost, kind="stable")
+        heap = [(0.0, c) for c in range(ctas)]
+        lists = [[] for _ in range(ctas)]
+        for w in order:
+            load, c = heapq.heappop(heap)
+            lists[c].append(int(w))
+            heapq.heappush(heap, (load + float(cost[w]), c))
+        offs = np.zeros(ctas + 1, dtype=np.int32)
+        offs[1:] = np.cumsum([len(x) for x in lists])
+        flat = np.concatenate([offs, np.asarray([w for x in lists for w in x], dtype=np.int32)])
+        t = torch.from_numpy(flat)
+        if self.device.type == "cuda":
+            t = t.pin_memory().to(self.device, non_blocking=True)
+        hit = self._sched[key] = (t, ctas)
+        return hit
+
+
+_SMS = {}
+
+
+def _sm_count(device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
 
 
 def layout_of(segments, n_rows, device):
@@ -166,15 +212,19 @@ def tree_attention(q, k, v, layout, out=None, pool=None, layer=0, scale=None):
     if layout.n_tiles == 0:
         return out
     scale = d ** -0.5 if scale is None else scale
-    if pool is not None:
+    if pool is not None and pool.k[layer].shape[0] > 0:
         pk, pv = pool.k[layer], pool.v[layer]
         pool_args = (_lib.ptr(pk), _lib.ptr(pv), pk.stride(0), pk.stride(1), pk.shape[0])
     else:
         pool_args = (None, None, 0, 0, 0)
+    sched, ctas = None, 0
+    if (h // hkv) % 2 == 0 and d <= 128:  # the paired-head persistent kernel runs this shape
+        sched, ctas = layout.schedule(h // 2, _sm_count(q.device))
     _lib.call("dan_tree_attention", _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(k), k.stride(0), k.stride(1),
               _lib.ptr(v), v.stride(0), v.stride(1), *pool_args, _lib.ptr(out), out.stride(0), out.stride(1), n, h,
               hkv, d, _lib.ptr(layout.tiles), layout.n_tiles, _lib.ptr(layout.row_own), _lib.ptr(layout.pages),
-              float(scale), _lib.ptr(_lib.status_word(q.device)), _lib.stream(), work=4 * h * d * layout.pairs)
+              _lib.ptr(sched), ctas, float(scale), _lib.ptr(_lib.status_word(q.device)), _lib.stream(),
+              work=4 * h * d * layout.pairs)
     return out
 
 

@@ -53,7 +53,20 @@ struct Params {
   int n_rows, n_heads, n_kv_heads;
   float scale_log2;
   int32_t* status;
+  const int* sched;  // optional: [ctas + 1] CSR offsets, then the item ids of each CTA
+  int sched_ctas;
 };
+
+// The k-th work item of this CTA, or -1: from the host's LPT schedule when given,
+// else round-robin over the LPT-sorted items.
+__device__ __forceinline__ int item_at(const Params& p, int k, int n_items) {
+  if (p.sched) {
+    const int b = p.sched[blockIdx.x] + k;
+    return b < p.sched[blockIdx.x + 1] ? p.sched[p.sched_ctas + 1 + b] : -1;
+  }
+  const int w = blockIdx.x + k * gridDim.x;
+  return w < n_items ? w : -1;
+}
 
 template <int D>
 struct Cfg {
@@ -394,6 +407,70 @@ __device__ __forceinline__ uint32_t span_bits(int lo, int hi) {
   return upto & ~((1u << lo) - 1u);
 }
 
+// 2^x on the FMA pipe, to share the exponentials with the MUFU unit: Cody-Waite range
+// reduction x = n + f with n = round(x) taken from a magic-constant add (1.5 * 2^23) and
+// f in [-1/2, 1/2], 2^f by a degree-3 polynomial (coefficients fitted for this kernel by
+// weighted least squares toward minimax: max relative error 7.7e-5, far below the bf16
+// rounding P takes next), and 2^n added into the exponent bits. For finite x <= 8.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float n = t - 12582912.f;
+  const float f = x - n;
+  const float q = fmaf(fmaf(fmaf(0.05518098f, f, 0.24263459f), f, 0.69326133f), f, 0.99992621f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
+
+// One pair in EXP_EMU_EVERY of a fully visible chunk takes exp2_fma instead of MUFU.EX2.
+constexpr int EXP_EMU_EVERY = 4;
+
+// Row max over 32 raw scores whose visibility bits are ``mw`` (all-visible and
+// all-masked chunks skip the per-element bit tests).
+__device__ __forceinline__ void chunk_max(const uint32_t (&s)[32], uint32_t mw, float& mx) {
+  if (mw == 0xffffffffu) {
+    float a = __uint_as_float(s[0]), b = __uint_as_float(s[1]);
+#pragma unroll
+    for (int i = 2; i < 32; i += 2) {
+      a = fmaxf(a, __uint_as_float(s[i]));
+      b = fmaxf(b, __uint_as_float(s[i + 1]));
+    }
+    mx = fmaxf(mx, fmaxf(a, b));
+  } else if (mw) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, ((mw >> i) & 1u) ? __uint_as_float(s[i]) : -INFINITY);
+  }
+}
+
+// P = exp2(s * scale_log2 - m) for 32 scores as 16 bf16 pairs; masked scores give 0.
+__device__ __forceinline__ void chunk_exp(const uint32_t (&s)[32], uint32_t mw, float sl2, float mu, float& sum,
+                                          uint32_t (&pk)[16]) {
+  if (mw == 0xffffffffu) {
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float xa = fmaf(__uint_as_float(s[2 * i]), sl2, -mu), xb = fmaf(__uint_as_float(s[2 * i + 1]), sl2, -mu);
+      const bool emu = (i % EXP_EMU_EVERY) == EXP_EMU_EVERY - 1;
+      const float a = emu ? exp2_fma(xa) : fast_exp2(xa);
+      const float b = emu ? exp2_fma(xb) : fast_exp2(xb);
+      acc0 += a;
+      acc1 += b;
+      pk[i] = pack_bf16(a, b);
+    }
+    sum += acc0 + acc1;
+  } else if (mw == 0u) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = 0u;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a = ((mw >> (2 * i)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s[2 * i]), sl2, -mu)) : 0.f;
+      const float b = ((mw >> (2 * i + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -mu)) : 0.f;
+      sum += a + b;
+      pk[i] = pack_bf16(a, b);
+    }
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(320, 1)
     tree_attention_pair_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -456,7 +533,9 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
       uint32_t gb = 0, it = 0;
-      for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++it) {
+      for (int kw = 0;; ++kw, ++it) {
+        const int w = item_at(p, kw, n_items);
+        if (w < 0) break;
         const Tile tile = tiles[w / npairs];
         const int head0 = 2 * (w % npairs), kvh = head0 / rep;
         const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
@@ -553,7 +632,9 @@ __global__ void __launch_bounds__(320, 1)
         if (h == 1) mma_commit(&v_empty[st]);
         return true;
       };
-      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+      for (int kw = 0; ok; ++kw, ++it) {
+        const int w = item_at(p, kw, n_items);
+        if (w < 0) break;
         const Tile tile = tiles[w / npairs];
         const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
         if (!mbar_wait(q_full, it & 1)) {
@@ -581,7 +662,9 @@ __global__ void __launch_bounds__(320, 1)
     const float sl2 = p.scale_log2;
     uint32_t gb = 0;
     bool ok = true;
-    for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+    for (int kw = 0; ok; ++kw) {
+      const int w = item_at(p, kw, n_items);
+      if (w < 0) break;
       const Tile tile = tiles[w / npairs];
       const int head = 2 * (w % npairs) + hsel;
       const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
@@ -619,12 +702,8 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld32(s_addr + 64 * hh, s0);
           tmem_ld32(s_addr + 64 * hh + 32, s1);
           tmem_wait_ld();
-          const uint32_t m0 = mw[2 * hh], m1 = mw[2 * hh + 1];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            mx = fmaxf(mx, ((m0 >> i) & 1u) ? __uint_as_float(s0[i]) : -INFINITY);
-            mx = fmaxf(mx, ((m1 >> i) & 1u) ? __uint_as_float(s1[i]) : -INFINITY);
-          }
+          chunk_max(s0, mw[2 * hh], mx);
+          chunk_max(s1, mw[2 * hh + 1], mx);
         }
         const float m_new = fmaxf(m, mx * sl2);
         bool rescale = false;
@@ -647,29 +726,14 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld32(s_addr + 64 * hh, s0);
           tmem_ld32(s_addr + 64 * hh + 32, s1);
           tmem_wait_ld();
-          const uint32_t m0 = mw[2 * hh], m1 = mw[2 * hh + 1];
           {
             uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float a0 = ((m0 >> (2 * i)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s0[2 * i]), sl2, -mu)) : 0.f;
-              const float a1 =
-                  ((m0 >> (2 * i + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s0[2 * i + 1]), sl2, -mu)) : 0.f;
-              sum0 += a0 + a1;
-              pk[i] = pack_bf16(a0, a1);
-            }
+            chunk_exp(s0, mw[2 * hh], sl2, mu, sum0, pk);
             tmem_st16(s_addr + 32 * hh, pk);
           }
           {
             uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float b0 = ((m1 >> (2 * i)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s1[2 * i]), sl2, -mu)) : 0.f;
-              const float b1 =
-                  ((m1 >> (2 * i + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s1[2 * i + 1]), sl2, -mu)) : 0.f;
-              sum1 += b0 + b1;
-              pk[i] = pack_bf16(b0, b1);
-            }
+            chunk_exp(s1, mw[2 * hh + 1], sl2, mu, sum1, pk);
             tmem_st16(s_addr + 32 * hh + 16, pk);
           }
         }
@@ -741,7 +805,7 @@ int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
     configured = true;
   }
   const int items = n_tiles * (p.n_heads / 2);
-  const int grid = items < sm_count() ? items : sm_count();
+  const int grid = p.sched ? p.sched_ctas : (items < sm_count() ? items : sm_count());
   tree_attention_pair_kernel<D><<<grid, PairCfg<D>::THREADS, PairCfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, p,
                                                                                         items);
   DAN_CUDA(cudaGetLastError());
@@ -766,8 +830,9 @@ DAN_API int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, con
                                const void* v_pool, int64_t pool_row, int64_t pool_head, int pool_rows, void* out,
                                int64_t out_row, int64_t out_head, int n_rows, int n_heads, int n_kv_heads,
                                int head_dim, const int* tiles, int n_tiles, const int* row_own, const int* pages,
-                               float scale, int32_t* status, void* stream) {
+                               const int* schedule, int sched_ctas, float scale, int32_t* status, void* stream) {
   DAN_REQUIRE(n_rows > 0 && n_tiles >= 0, "tree_attention: n_rows=%d n_tiles=%d", n_rows, n_tiles);
+  DAN_REQUIRE(!schedule || sched_ctas > 0, "tree_attention: a schedule needs its CTA count");
   DAN_REQUIRE(n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0,
               "tree_attention: %d query heads are not a multiple of %d kv heads", n_heads, n_kv_heads);
   DAN_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, "tree_attention: head_dim %d unsupported",
@@ -800,6 +865,8 @@ DAN_API int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, con
   p.n_kv_heads = n_kv_heads;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
+  p.sched = schedule;
+  p.sched_ctas = sched_ctas;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool paired = (n_heads / n_kv_heads) % 2 == 0 && head_dim <= 128;
   if (paired) return head_dim == 64 ? attn::launch_pair<64>(tq, tk, tv, tpk, tpv, p, n_tiles, s)

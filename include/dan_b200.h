@@ -36,13 +36,15 @@ int dan_read_status(int32_t* status_dev, int32_t* status_host, void* stream);
  * hold cached prefix pages of 128 tokens (may be NULL when no segment has a past).
  * tiles: int32 [n_tiles, 12] {row0, nrows, seg_start, past, ppad, split, nblk_a, blk_b0,
  * blk_b1, page0, q0v, 0}; row_own: int32 [n_rows] packed row where each row's run starts;
- * pages: int32 pool page per cached 128-token block. head_dim in {64, 128, 256}. */
+ * pages: int32 pool page per cached 128-token block. head_dim in {64, 128, 256}.
+ * schedule (optional, paired-head kernel): int32 [sched_ctas + 1] CSR offsets then the work
+ * items (tile * n_heads/2 + head pair) of each persistent CTA; NULL = round-robin. */
 int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, const void* k, int64_t k_row, int64_t k_head,
                        const void* v, int64_t v_row, int64_t v_head, const void* k_pool, const void* v_pool,
                        int64_t pool_row, int64_t pool_head, int pool_rows, void* out, int64_t out_row,
                        int64_t out_head, int n_rows, int n_heads, int n_kv_heads, int head_dim, const int* tiles,
-                       int n_tiles, const int* row_own, const int* pages, float scale, int32_t* status,
-                       void* stream);
+                       int n_tiles, const int* row_own, const int* pages, const int* schedule, int sched_ctas,
+                       float scale, int32_t* status, void* stream);
 
 /* C[m, n] = A[m, k] * W[n, k]^T in bf16 with fp32 accumulation on tcgen05 tensor cores.
  * Replaces nn.Linear in the decoder (dan/models/llama.py:78,87,102; qwen3_5.py:185,212,319,329,344)
@@ -112,6 +114,29 @@ int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, const vo
                       const void* w_lm, int64_t ldw, int64_t vocab, const int* label_ids, const int* offsets,
                       int n_questions, int hidden, int max_labels, float* logits, float* probs, int32_t* status,
                       void* stream);
+
+/* Gated DeltaNet layers (Qwen3.5), dan/models/qwen3_5.py:161-298.
+ * Row codes for conv sources: >= 0 packed row of src; -1 a zero row; <= -2 row (-code-2) of hist.
+ * dan_causal_conv: out[r] = silu(sum_j w[:, j] * row(prev[r][2-j]) ... ) over the run's
+ * [history; tokens] (F.conv1d + SiLU of _phase, qwen3_5.py:214-220); prev: int32 [rows, 3]
+ * codes of the 1st/2nd/3rd previous rows; w: [channels, 4]. */
+int dan_causal_conv(const void* src, int64_t ld_src, const void* hist, int64_t ld_hist, const void* weight,
+                    const int* prev, void* out, int64_t ld_out, int rows, int channels, void* stream);
+/* dst[i] = row(codes[i]): the conv tails stored with prefix-cache saves (qwen3_5.py:207-209). */
+int dan_gather_rows(const void* src, int64_t ld_src, const void* hist, int64_t ld_hist, const int* codes, int count,
+                    void* dst, int64_t ld_dst, int cols, void* stream);
+/* Gated delta rule over the tree of runs of a packed batch (delta_rule, qwen3_5.py:136-158; the
+ * trunk/branch phases of DeltaNet.forward, 196-210), with the gates (delta_gates, fused.py:79-82)
+ * and the q/k l2 norms fused. segs: int32 [n_segs, 8] {trunk_start, trunk_len, cut, init_slot,
+ * save_slot, branch0, n_branches, 0}; branches: int32 [.., 2] {start, len}; state_pool: fp32
+ * [slots, hv, 128, 128] of this layer (init / save slots, -1 = none). dk = dv = 128. */
+int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* b, const void* a,
+                         int64_t ld_ba, const float* a_log, const float* dt_bias, const int* segs, int n_segs,
+                         const int* branches, float* state_pool, int64_t slot_stride, void* out, int64_t ld_out,
+                         int hk, int hv, int dk, int dv, float q_scale, void* stream);
+/* y = bf16(w * bf16(x_hat)) * silu(z) per (row, head) (gated_rms_norm, dan/fused.py:51-56). */
+int dan_gated_rms_norm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* w, float eps, void* y,
+                       int64_t ldy, int rows, int heads, int dv, void* stream);
 
 #ifdef __cplusplus
 }

@@ -153,3 +153,18 @@ def test_prefix_pool_lru_and_budget():
     d = pool.reserve([6], 300, pinned=[a, c])  # needs 3 pages, only pinned entries left
     assert d is None
     assert pool.used == a.nbytes + c.nbytes
+
+
+def test_lpt_schedule_covers_every_item_once():
+    plans = synthetic.batch(2, seed=4)
+    runner = cpu_runner(0)
+    ids, pos, segs, reads, stores = runner.pack(plans)
+    lay = TreeLayout.build(segs, len(ids), "cpu")
+    sched, ctas = lay.schedule(16, 148)
+    s = sched.numpy()
+    offs, items = s[:ctas + 1], s[ctas + 1:]
+    assert offs[0] == 0 and offs[-1] == len(items) == lay.n_tiles * 16
+    assert sorted(items.tolist()) == list(range(lay.n_tiles * 16))
+    cost = lay.costs.repeat(16) + lay.ITEM_OVERHEAD
+    loads = [cost[items[offs[c]:offs[c + 1]]].sum() for c in range(ctas)]
+    assert max(loads) <= sum(loads) / ctas + cost.max()  # greedy LPT bound
