@@ -1,0 +1,134 @@
+"""Small standalone kernel cases for profiling (``ncu``) and quick timing.
+
+    python -m dan_b200.cases gemm|attention|deltanet|norm [--iters N]
+
+Each case builds seeded inputs with the shapes of a benchmark configuration,
+runs the kernel ``--iters`` times (4 by default) and prints one JSON line with
+the mean CUDA-event time per launch (the first launch is a warm-up). Inputs
+are larger than L2 where the configuration's are.
+
+- gemm: the four Llama-3-8B decoder projections of one <=8192-token batch
+  (M = 7089 tokens): q/k/v + RoPE epilogue, o + residual, gate/up + SwiGLU,
+  down + residual.
+- attention: tree attention of one configuration-2 batch (32/8 heads x 128).
+- deltanet: causal conv + gated delta scan of one configuration-4 batch
+  (Qwen3.5-4B-style: 16 key / 32 value heads x 128).
+- norm: RMSNorm of [7089, 4096].
+"""
+import argparse
+import json
+
+import torch
+
+from . import _lib, ops, synthetic
+from .attention import TreeLayout, tree_attention
+from .plan import Branch, ReadPlan  # noqa: F401  (re-exported for callers building cases)
+
+
+def _time(fn, iters):
+    fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters - 1):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / max(iters - 1, 1)
+
+
+def _pack(cfg, seed):
+    from .runner import Runner
+
+    r = Runner.__new__(Runner)
+    r.device, r.cache = torch.device("cuda"), None
+    return r.pack(synthetic.batch(cfg, seed=seed, vocab=1000), use_cache=False)
+
+
+def gemm(iters):
+    dev = torch.device("cuda")
+    m = 7089
+    g = torch.Generator(device=dev).manual_seed(0)
+    out = {}
+    pos = torch.arange(m, device=dev)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, dtype=torch.float32, device=dev) / 128))
+    table = ops.rope_table(pos, inv)
+    for name, n, k in (("qkv_rope", 6144, 4096), ("o_residual", 4096, 4096), ("gate_up_swiglu", 28672, 4096),
+                       ("down_residual", 4096, 14336)):
+        x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+        r = torch.randn(m, n, device=dev, generator=g).bfloat16()
+        fn = {"qkv_rope": lambda: ops.linear_rope(x, w, table, 5120, 128),
+              "o_residual": lambda: ops.linear(x, w, residual=r),
+              "gate_up_swiglu": lambda: ops.linear_swiglu(x, w),
+              "down_residual": lambda: ops.linear(x, w, residual=r)}[name]
+        ms = _time(fn, iters)
+        out[name] = {"m": m, "n": n, "k": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e9}
+    return out
+
+
+def attention(iters):
+    dev = torch.device("cuda")
+    ids, pos, segs, reads, _ = _pack(2, 0)
+    n = len(ids)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(n, 32, 128, device=dev, generator=g).bfloat16()
+    k = torch.randn(n, 8, 128, device=dev, generator=g).bfloat16()
+    v = torch.randn(n, 8, 128, device=dev, generator=g).bfloat16()
+    lay = TreeLayout.build(segs, n, dev)
+    ms = _time(lambda: tree_attention(q, k, v, lay), iters)
+    return {"tokens": n, "useful_pairs": lay.pairs, "tiles": lay.n_tiles, "ms": ms,
+            "tflops": 4 * 32 * 128 * lay.pairs / ms / 1e9}
+
+
+def deltanet(iters):
+    from .qwen3_5 import RecurrentLayout
+
+    dev = torch.device("cuda")
+    ids, pos, segs, reads, _ = _pack(4, 0)
+    n = len(ids)
+    hk, hv, dk, dv = 16, 32, 128, 128
+    C = 2 * hk * dk + hv * dv
+    g = torch.Generator(device=dev).manual_seed(0)
+    pre = (torch.randn(n, C, device=dev, generator=g) * 0.5).bfloat16()
+    ba = torch.randn(n, 2 * hv, device=dev, generator=g).bfloat16()
+    w = (torch.randn(C, 4, device=dev, generator=g) * 0.5).bfloat16()
+    a_log = torch.log(1 + 15 * torch.rand(hv, device=dev, generator=g))
+    dt = 0.5 + 0.5 * torch.rand(hv, device=dev, generator=g)
+    rl = RecurrentLayout.build(segs, n, 3, dev)
+    conv = torch.empty(n, C, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(n, hv * dv, dtype=torch.bfloat16, device=dev)
+    kd = hk * dk
+
+    def run():
+        _lib.call("dan_causal_conv", _lib.ptr(pre), C, None, 0, _lib.ptr(w), _lib.ptr(rl.prev), _lib.ptr(conv), C, n,
+                  C, _lib.stream())
+        _lib.call("dan_gated_delta_scan", _lib.ptr(conv[:, :kd]), _lib.ptr(conv[:, kd:2 * kd]),
+                  _lib.ptr(conv[:, 2 * kd:]), C, _lib.ptr(ba[:, :hv]), _lib.ptr(ba[:, hv:]), 2 * hv,
+                  _lib.ptr(a_log), _lib.ptr(dt), _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), None, 0,
+                  _lib.ptr(out), hv * dv, hk, hv, dk, dv, float(dk ** -0.5), _lib.stream())
+
+    ms = _time(run, iters)
+    return {"tokens": n, "segments": rl.n_segs, "ms": ms}
+
+
+def norm(iters):
+    dev = torch.device("cuda")
+    x = torch.randn(7089, 4096, device=dev).bfloat16()
+    w = torch.ones(4096, device=dev).bfloat16()
+    ms = _time(lambda: ops.rms_norm(x, w, 1e-5), iters)
+    return {"ms": ms, "gbs": 2 * x.numel() * 2 / ms / 1e6}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "norm"])
+    ap.add_argument("--iters", type=int, default=4)
+    a = ap.parse_args()
+    res = globals()[a.case](max(a.iters, 2))
+    _lib.check_status(torch.device("cuda"))
+    print(json.dumps({a.case: res}))
+
+
+if __name__ == "__main__":
+    main()

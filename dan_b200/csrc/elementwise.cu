@@ -43,11 +43,10 @@ __global__ void embed_kernel(const int64_t* ids, const __nv_bfloat16* table, int
 // mode 1 (zero-centred, fused.py:43-48): y = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))
 // With ``q8`` set, y is also quantised per row to e4m3 (fused.py:85-91):
 //   scale = max(amax |y|, 1e-12) / 448, q = e4m3(y / scale).
-template <int VEC>  // bf16 elements per lane per step (8 = one 16-byte load)
+template <int MAXV>  // 16-byte vectors per lane (a row holds at most 32 * MAXV * 8 elements)
 __global__ void rms_norm_kernel(const __nv_bfloat16* x, int64_t x_outer, int64_t x_inner, int inner,
                                 const __nv_bfloat16* w, float eps, int mode, __nv_bfloat16* y, int64_t y_outer,
                                 int64_t y_inner, uint8_t* q8, int64_t ldq, float* q8_scale, int rows, int cols) {
-  constexpr int MAXV = 8192 / (32 * 8);  // supports cols <= 8192
   const int warps = blockDim.x / 32;
   const int r = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -332,10 +331,30 @@ DAN_API int dan_rms_norm(const void* x, int64_t x_outer, int64_t x_inner, int in
               "rms_norm: strides must be multiples of 8");
   DAN_REQUIRE(y || q8, "rms_norm: no output");
   if (!rows) return 0;
-  const int warps = 4;
-  ew::rms_norm_kernel<8><<<(rows + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), x_outer, x_inner, inner, static_cast<const __nv_bfloat16*>(w), eps, mode,
-      static_cast<__nv_bfloat16*>(y), y_outer, y_inner, static_cast<uint8_t*>(q8), ldq, q8_scale, rows, cols);
+  const int warps = 8;
+  const int per_lane = (cols / 8 + 31) / 32;
+  const dim3 grid((rows + warps - 1) / warps), block(32 * warps);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  auto* yb = static_cast<__nv_bfloat16*>(y);
+  auto* qb = static_cast<uint8_t*>(q8);
+#define DAN_NORM(NV) \
+  ew::rms_norm_kernel<NV><<<grid, block, 0, s>>>(xb, x_outer, x_inner, inner, wb, eps, mode, yb, y_outer, y_inner, qb, \
+                                                 ldq, q8_scale, rows, cols)
+  if (per_lane <= 1)
+    DAN_NORM(1);
+  else if (per_lane <= 2)
+    DAN_NORM(2);
+  else if (per_lane <= 4)
+    DAN_NORM(4);
+  else if (per_lane <= 8)
+    DAN_NORM(8);
+  else if (per_lane <= 16)
+    DAN_NORM(16);
+  else
+    DAN_NORM(32);
+#undef DAN_NORM
   DAN_CUDA(cudaGetLastError());
   return 0;
 }
