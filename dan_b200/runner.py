@@ -130,10 +130,12 @@ class Runner:
     @torch.inference_mode()
     def read_many(self, plans, probabilities=False):
         """Per plan, per branch: the logits of its label tokens (fp32, CPU), from one
-        device-to-host copy per batch; with ``probabilities`` also the softmax of each."""
-        logits, probs, offsets = self.forward_flat(plans)
-        both = torch.stack([logits, probs]).cpu() if logits.numel() else torch.zeros(2, 0)
-        _lib.check_status(self.device)
+        device-to-host copy per batch; with ``probabilities`` also the softmax of each.
+        Runs on this runner's device whatever the calling thread's current device is."""
+        with torch.cuda.device(self.device):
+            logits, probs, offsets = self.forward_flat(plans)
+            both = torch.stack([logits, probs]).cpu() if logits.numel() else torch.zeros(2, 0)
+            _lib.check_status(self.device)
         lg = [both[0, offsets[i]:offsets[i + 1]] for i in range(len(offsets) - 1)]
         out = self._split(plans, lg)
         if probabilities:

@@ -1,0 +1,148 @@
+"""The serving engine and answer readout on the CPU with fake replicas (no GPU).
+
+Mirrors the reference's serving tests (tests/test_api.py:51-68: concurrent decides are
+batched and give the same answers as solo reads) and its failure isolation
+(engine.py:102-107: a failing batch fails only its own requests), over several
+replicas; fault injection is on the host (a replica that raises)."""
+import asyncio
+import random
+import threading
+
+import pytest
+import torch
+
+from dan_b200 import readout
+from dan_b200.engine import AsyncEngine, Overloaded
+from dan_b200.plan import Branch, ReadPlan
+
+
+class Spec:
+    def __init__(self, key, type_, options, legend=None):
+        self.key, self.type, self.options, self.legend = key, type_, options, legend
+
+
+class FakePlanner:
+    """Plans for a state string: trunk tokens from the text, one branch per question."""
+
+    def plans(self, state, questions, profile=None):
+        prefix = [ord(c) % 97 for c in state] or [1]
+        specs = [Spec(k, q["type"], [(o, "") for o in q["options"]]) for k, q in questions.items()]
+        branches = [Branch([len(k), 3], list(range(len(q["options"])))) for k, q in questions.items()]
+        return [ReadPlan(prefix, specs=specs, branches=branches, order=list(questions), perms=[])]
+
+
+class FakeRunner:
+    """Deterministic 'logits' from the plan; optionally raises on chosen batches."""
+
+    def __init__(self, fail_on=(), delay=0.0):
+        self.calls, self.fail_on, self.delay = 0, set(fail_on), delay
+        self.lock = threading.Lock()
+
+    def read_many(self, plans):
+        import time
+
+        with self.lock:
+            self.calls += 1
+            n = self.calls
+        time.sleep(self.delay)
+        if n in self.fail_on:
+            raise RuntimeError(f"injected failure on batch {n}")
+        return [[torch.tensor([float(sum(p.prefix) % 7), float(len(b.suffix))] + [0.0] * (len(b.label_ids) - 2))
+                 for b in p.branches] for p in plans]
+
+
+QUESTIONS = {"urgent": {"type": "noul", "options": ["yes", "no"]},
+             "topic": {"type": "choice", "options": ["a", "b", "c"]}}
+
+
+def run(coro):
+    return asyncio.run(coro)
+
+
+def test_concurrent_decides_are_batched_and_match_solo_reads():
+    runner = FakeRunner()
+    eng = AsyncEngine(FakePlanner(), runner, max_wait_ms=20)
+
+    async def main():
+        states = [f"state number {i}" for i in range(12)]
+        res = await asyncio.gather(*[eng.decide(s, QUESTIONS) for s in states])
+        await eng.stop()
+        return states, res
+
+    states, res = run(main())
+    assert eng.stats.batches < 12 and eng.stats.requests == 12
+    for s, (ans, tokens) in zip(states, res):
+        plan = FakePlanner().plans(s, QUESTIONS)[0]
+        solo = readout.answers(plan, FakeRunner().read_many([plan])[0])
+        assert ans == solo and tokens == AsyncEngine.cost(plan)
+
+
+def test_replicas_share_the_queue_and_failures_stay_in_their_batch():
+    runners = [FakeRunner(fail_on={1}, delay=0.01), FakeRunner(delay=0.01)]
+    eng = AsyncEngine(FakePlanner(), runners, max_batch_tokens=40, max_wait_ms=1)
+
+    async def main():
+        states = [f"s{i}" * 5 for i in range(16)]
+        res = await asyncio.gather(*[eng.decide(s, QUESTIONS) for s in states], return_exceptions=True)
+        await eng.stop()
+        return res
+
+    res = run(main())
+    failed = [r for r in res if isinstance(r, Exception)]
+    assert failed and all("injected" in str(e) for e in failed)
+    assert len(failed) < len(res)  # the engine kept serving after the failing batch
+    assert all(r.calls > 0 for r in runners)  # both replicas took batches
+    assert eng.stats.errors == len(failed)
+    assert 'replica="1"' in eng.metrics()
+
+
+def test_overloaded_at_queue_cap():
+    eng = AsyncEngine(FakePlanner(), FakeRunner(), max_queue=0)
+
+    async def main():
+        with pytest.raises(Overloaded):
+            await eng.decide("x", QUESTIONS)
+
+    run(main())
+
+
+def test_readout_shapes_and_rotation_inverse():
+    rng = random.Random(0)
+    spec = Spec("q", "choice", [("a", ""), ("b", ""), ("c", "")])
+    lg = [rng.gauss(0, 1) for _ in range(3)]
+    plan = ReadPlan([1], specs=[spec], branches=[], order=["q"], perms=[[1, 2, 0]])
+    ans = readout.answers(plan, [lg])["q"]
+    # shown position i held option perm[i]: canonical option o is read at position inv[o]
+    canon = [lg[2], lg[0], lg[1]]
+    want = readout.softmax(canon)
+    assert ans["choice"] == ["a", "b", "c"][max(range(3), key=want.__getitem__)]
+    assert all(abs(ans["probabilities"][k] - v) < 1e-6 for k, v in zip("abc", want))
+    assert 0 <= ans["confidence"] <= 1
+    # averaging over rotations in log space
+    plan2 = ReadPlan([1], specs=[spec], branches=[], order=["q"], perms=[[0, 1, 2]])
+    comb = readout.combine([plan, plan2], [[lg], [canon]])[0]
+    assert torch.allclose(comb, torch.log_softmax(torch.tensor(canon), 0), atol=1e-6)
+
+
+def test_readout_matches_reference_golden():
+    from conftest import golden
+
+    for case in golden("readout.json"):
+        specs = [Spec(k, t, [(o, "") for o in opts], legend) for k, t, opts, legend in case["specs"]]
+        plan = ReadPlan([1], specs=specs, branches=[], forced={"forced": {"type": "noul", "noul": 1.0}},
+                        order=["pick", "forced", "yn", "rate"], perms=case["perms"])
+        got = readout.answers(plan, case["logits"])
+        assert got.keys() == case["answers"].keys()
+        for k, want in case["answers"].items():
+            for f, v in want.items():
+                if isinstance(v, dict):
+                    assert v.keys() == got[k][f].keys()
+                    assert all(abs(got[k][f][x] - v[x]) < 1e-6 for x in v) if isinstance(next(iter(v.values())), float) \
+                        else got[k][f] == v
+                elif isinstance(v, float):
+                    assert abs(got[k][f] - v) < 1e-6
+                else:
+                    assert got[k][f] == v
+        comb = readout.combine([plan, plan], [case["logits"], case["logits"]])
+        for c, w in zip(comb, case["combine"]):
+            assert torch.allclose(c, torch.tensor(w), atol=1e-6)
