@@ -37,6 +37,9 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 
 METRIC = "prefill tokens/s & answers/s per B200 at Llama-3-8B bf16; attn TC % of peak"
+WORKLOADS = {3: "cfg3: Llama-3-8B bf16 packed prefill + label readout, <=8192-token batches",
+             4: "cfg4: Qwen3.5-4B-style hybrid bf16 (3 DeltaNet : 1 gated attention), <=8192-token batches",
+             5: "cfg5: Llama-3-8B FP8 e4m3 + shared 1024-token prefix in the prefix pool, <=8192-token batches"}
 
 
 def peaks():
@@ -183,13 +186,13 @@ def run_reference(args, world, rank):
 
 
 # ---------------------------------------------------------------------- GPU arm
-def prepare(runner, plans):
+def prepare(runner, plans, use_cache=False):
     """Pack and upload one batch (outside the timed region for ``value``)."""
     import numpy as np
 
     from dan_b200.attention import layout_of
 
-    ids, pos, segs, reads, _ = runner.pack(plans, use_cache=False)
+    ids, pos, segs, reads, _ = runner.pack(plans, use_cache=use_cache)
     dev = runner.device
     labels = [list(l) for _, l in reads]
     off = np.zeros(len(labels) + 1, dtype=np.int32)
@@ -213,14 +216,21 @@ def run_dan(args, world, rank, local):
     from dan_b200.loader import llama3_8b_config, random_model
     from dan_b200.runner import Runner
 
+    from dan_b200.loader import qwen35_4b_config
+
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    cfg = llama3_8b_config()
-    model = random_model(cfg, seed=0, device=device)
-    runner = Runner(model, device, cache_bytes=0)
+    cid = args.config
+    cfg = qwen35_4b_config() if cid == 4 else llama3_8b_config()
+    quant = "fp8" if cid == 5 else None
+    model = random_model(cfg, seed=0, device=device, quantization=quant)
+    runner = Runner(model, device, cache_bytes=(4 << 30) if cid == 5 else 0)
     n = args.warmup + args.steps
-    batches = synthetic.batches(3, n, seed=1000 + rank)
-    prepared = [prepare(runner, p) for p in batches]
+    batches = synthetic.batches(cid, n + 1, seed=1000 + rank, vocab=cfg["vocab_size"])
+    if cid == 5:  # the shared 1024-token prefix enters the prefix pool once, as in serving
+        runner.read_many(batches[0][:1])
+    batches = batches[1:]
+    prepared = [prepare(runner, p, use_cache=(cid == 5)) for p in batches]
     torch.cuda.synchronize()
 
     for b in prepared[:args.warmup]:
@@ -234,7 +244,8 @@ def run_dan(args, world, rank, local):
     hbm, pk_burst, pk_sust, pk_kind = peaks()
     launches0 = profiling.total_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    timer = profiling.KernelTimer({"dan_gemm_bf16", "dan_gemm_bf16_rope", "dan_tree_attention"})
+    timer = profiling.KernelTimer({"dan_gemm_bf16", "dan_gemm_bf16_rope", "dan_gemm_e4m3", "dan_gemm_e4m3_rope",
+                                   "dan_tree_attention"})
     with Clocks(local) as clocks:
         barrier(world, device)
         torch.cuda.synchronize()
@@ -248,7 +259,7 @@ def run_dan(args, world, rank, local):
     ms = ev0.elapsed_time(ev1)
     launches = profiling.total_launches() - launches0
     kern = timer.summary()
-    kern["gemm"] = timer.total("gemm_bf16")
+    kern["gemm"] = timer.total("gemm_")
     ms_max = reduce(ms, "max", world, device)
     tok_all = reduce(tokens, "sum", world, device)
     q_all = reduce(questions, "sum", world, device)
@@ -279,21 +290,23 @@ def run_dan(args, world, rank, local):
         return
     g = kern.get("gemm", {})
     a = kern.get("dan_tree_attention", {})
-    gemm_tflops = g["work_total"] / (g["ms_total"] * 1e-3) / 1e12 if g else None
-    attn_tflops = a["work_total"] / (a["ms_total"] * 1e-3) / 1e12 if a else None
-    traffic = None
+    gemm_tflops = g["work_total"] / (g["ms_total"] * 1e-3) / 1e12 if g and g["ms_total"] else None
+    attn_tflops = a["work_total"] / (a["ms_total"] * 1e-3) / 1e12 if a and a["ms_total"] else None
+    traffic = None  # DRAM bytes per GEMM launch from the committed ncu summary (configuration 3)
     try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get("dan_gemm_bf16")
+        with open(os.path.join(ROOT, "profiles", "gemm_bf16_cfg3_shapes.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:") and cid == 3:
+                    traffic = int(line.split(":")[1])
     except (OSError, ValueError):
         pass
     line = {
         "metric": METRIC, "value": tok_all / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3" if cid == 5 else "bf16", "data": "synthetic",
         "answers_per_s": q_all / (ms_max * 1e-3),
-        "config": {"workload": "cfg3: Llama-3-8B bf16 packed prefill + label readout, <=8192-token batches",
-                   "model": "llama-3-8b (random init)", "global_batch": int(tok_all / args.steps),
+        "config": {"workload": WORKLOADS[cid], "model": "qwen3.5-4b-style (random init)" if cid == 4 else
+                   "llama-3-8b (random init)", "global_batch": int(tok_all / args.steps),
                    "seq_len": 8192, "parallelism": f"replicas x{world}",
                    "l2": "weights (15 GB) streamed every step exceed the 126 MB L2"},
         "roofline": {"bound": "tensor", "kernel": "dan_gemm_bf16 (all decoder projections)", "achieved": gemm_tflops,
@@ -313,7 +326,7 @@ def run_dan(args, world, rank, local):
                     for k, v in kern.items() if v["launches"]},
         "clocks": clocks.summary(),
     }
-    if world == 1 and not args.no_cpu:
+    if world == 1 and not args.no_cpu and cid == 3:
         dt, ctok, cq, threads = cpu_sample()
         v = ctok / (dt * 32 / SAMPLE_LAYERS)
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -329,6 +342,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="dan", choices=["dan", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5],
+                    help="3 (default): Llama-3-8B bf16; 4: Qwen3.5-4B-style hybrid; 5: Llama-3-8B FP8 + prefix pool")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     try:

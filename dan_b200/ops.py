@@ -74,7 +74,7 @@ def linear_e4m3(xq, x_scale, wq, w_scale, bias=None, residual=None, swiglu=False
     _lib.call("dan_gemm_e4m3", _lib.ptr(xq), xq.stride(0), _lib.ptr(x_scale), _lib.ptr(wq), wq.stride(0),
               _lib.ptr(w_scale), _lib.ptr(out), out.stride(0), _lib.ptr(residual),
               residual.stride(0) if residual is not None else 0, _lib.ptr(bias), m, n, k, ep, _st(xq), _lib.stream(),
-              work=2 * m * n * k)
+              work=2 * m * n * k, key=f"gemm_e4m3 n={n} k={k} ep={ep}")
     return out
 
 
@@ -148,7 +148,8 @@ def linear_e4m3_rope(xq, x_scale, wq, w_scale, table, rope_cols, head_dim, bias=
     cos, sin = table
     _lib.call("dan_gemm_e4m3_rope", _lib.ptr(xq), xq.stride(0), _lib.ptr(x_scale), _lib.ptr(wq), wq.stride(0),
               _lib.ptr(w_scale), _lib.ptr(out), out.stride(0), None, 0, _lib.ptr(bias), m, n, k, ROPE, rope_cols,
-              head_dim, _lib.ptr(cos), _lib.ptr(sin), _st(xq), _lib.stream(), work=2 * m * n * k)
+              head_dim, _lib.ptr(cos), _lib.ptr(sin), _st(xq), _lib.stream(), work=2 * m * n * k,
+              key=f"gemm_e4m3 n={n} k={k} ep=rope")
     return out
 
 
