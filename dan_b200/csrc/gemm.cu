@@ -95,6 +95,113 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, i
   }
 }
 
+// The fused epilogue of one 128-row x 256-column accumulator tile held in TMEM at ``taddr``
+// (this warp's lanes): ``row`` is this thread's output row, ``tn`` the tile's column block.
+template <bool FP8>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, int row, int tn) {
+  const int cols_out = p.epilogue == kSwiglu ? p.n / 2 : p.n;
+  const float as = (FP8 && row < p.m) ? p.a_scale[row] : 1.f;
+  if (p.epilogue == kSwiglu) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 2; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld32(taddr + c, g);
+      tmem_ld32(taddr + BN / 2 + c, u);
+      tmem_wait_ld();
+      float v[32];
+      const int gcol = tn * BN + c, ucol = tn * BN + BN / 2 + c;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+        if (FP8) {
+          gv *= as * (gcol + i < p.n ? p.w_scale[gcol + i] : 0.f);
+          uv *= as * (ucol + i < p.n ? p.w_scale[ucol + i] : 0.f);
+        }
+        if (p.bias) {
+          gv += gcol + i < p.n ? __bfloat162float(p.bias[gcol + i]) : 0.f;
+          uv += ucol + i < p.n ? __bfloat162float(p.bias[ucol + i]) : 0.f;
+        }
+        gv = bf16_round(gv);
+        uv = bf16_round(uv);
+        v[i] = silu(gv) * uv;
+      }
+      store_chunk<FP8>(p, row, tn * (BN / 2) + c, cols_out, v);
+    }
+  } else if (p.epilogue == kRope) {
+    // q/k heads: rotate-half RoPE on the bf16-rounded projection with the reference's
+    // rounding points, bf16(bf16(a cos) + bf16(-b sin)) (llama.py:43-45); v heads: plain.
+    const int hd = p.rope_hd, half = hd / 2;
+    const int trow = row < p.m ? row : 0;
+#pragma unroll 1
+    for (int h0 = 0; h0 < BN; h0 += hd) {
+      const int hc = tn * BN + h0;
+      if (hc >= p.n) break;
+#pragma unroll 1
+      for (int c = 0; c < half; c += 32) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr + h0 + c, ra);
+        tmem_ld32(taddr + h0 + half + c, rb);
+        tmem_wait_ld();
+        float va[32], vb[32];
+        const bool rot = hc + hd <= p.rope_cols;
+        float ct[32], st[32];
+        if (rot) {  // 32 consecutive cos / sin of this row: 8 + 8 16-byte loads
+          const float4* c4 = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(trow) * half + c);
+          const float4* s4 = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(trow) * half + c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 cv = c4[i], sv = s4[i];
+            ct[4 * i] = cv.x, ct[4 * i + 1] = cv.y, ct[4 * i + 2] = cv.z, ct[4 * i + 3] = cv.w;
+            st[4 * i] = sv.x, st[4 * i + 1] = sv.y, st[4 * i + 2] = sv.z, st[4 * i + 3] = sv.w;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float a = __uint_as_float(ra[i]), b = __uint_as_float(rb[i]);
+          if (FP8) {
+            a *= as * p.w_scale[hc + c + i];
+            b *= as * p.w_scale[hc + half + c + i];
+          }
+          if (p.bias) {
+            a += __bfloat162float(p.bias[hc + c + i]);
+            b += __bfloat162float(p.bias[hc + half + c + i]);
+          }
+          if (rot) {
+            a = bf16_round(a);
+            b = bf16_round(b);
+            const float cs = ct[i], sn = st[i];
+            va[i] = bf16_round(a * cs) + bf16_round(-b * sn);
+            vb[i] = bf16_round(b * cs) + bf16_round(a * sn);
+          } else {
+            va[i] = a;
+            vb[i] = b;
+          }
+        }
+        store_chunk<FP8>(p, row, hc + c, cols_out, va);
+        store_chunk<FP8>(p, row, hc + half + c, cols_out, vb);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      const int col = tn * BN + c;
+      if (col >= p.n) break;
+      uint32_t r[32];
+      tmem_ld32(taddr + c, r);
+      tmem_wait_ld();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float x = __uint_as_float(r[i]);
+        if (FP8) x *= as * (col + i < p.n ? p.w_scale[col + i] : 0.f);
+        if (p.bias && col + i < p.n) x += __bfloat162float(p.bias[col + i]);
+        v[i] = x;
+      }
+      store_chunk<FP8>(p, row, col, cols_out, v);
+    }
+  }
+}
+
 template <bool FP8>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
@@ -199,7 +306,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int r_in = sub * 32 + lane;
     int buf = 0;
     uint32_t acc_phase = 0;
-    const int cols_out = p.epilogue == kSwiglu ? p.n / 2 : p.n;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int tm = t % p.tiles_m, tn = t / p.tiles_m;
       if (!mbar_wait(&tfull[buf], acc_phase)) {
@@ -209,106 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int row = tm * BM + r_in;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
-      const float as = (FP8 && row < p.m) ? p.a_scale[row] : 1.f;
-      if (p.epilogue == kSwiglu) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(taddr + c, g);
-          tmem_ld32(taddr + BN / 2 + c, u);
-          tmem_wait_ld();
-          float v[32];
-          const int gcol = tn * BN + c, ucol = tn * BN + BN / 2 + c;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
-            if (FP8) {
-              gv *= as * (gcol + i < p.n ? p.w_scale[gcol + i] : 0.f);
-              uv *= as * (ucol + i < p.n ? p.w_scale[ucol + i] : 0.f);
-            }
-            if (p.bias) {
-              gv += gcol + i < p.n ? __bfloat162float(p.bias[gcol + i]) : 0.f;
-              uv += ucol + i < p.n ? __bfloat162float(p.bias[ucol + i]) : 0.f;
-            }
-            gv = bf16_round(gv);
-            uv = bf16_round(uv);
-            v[i] = silu(gv) * uv;
-          }
-          store_chunk<FP8>(p, row, tn * (BN / 2) + c, cols_out, v);
-        }
-      } else if (p.epilogue == kRope) {
-        // q/k heads: rotate-half RoPE on the bf16-rounded projection with the reference's
-        // rounding points, bf16(bf16(a cos) + bf16(-b sin)) (llama.py:43-45); v heads: plain.
-        const int hd = p.rope_hd, half = hd / 2;
-        const int trow = row < p.m ? row : 0;
-#pragma unroll 1
-        for (int h0 = 0; h0 < BN; h0 += hd) {
-          const int hc = tn * BN + h0;
-          if (hc >= p.n) break;
-#pragma unroll 1
-          for (int c = 0; c < half; c += 32) {
-            uint32_t ra[32], rb[32];
-            tmem_ld32(taddr + h0 + c, ra);
-            tmem_ld32(taddr + h0 + half + c, rb);
-            tmem_wait_ld();
-            float va[32], vb[32];
-            const bool rot = hc + hd <= p.rope_cols;
-            float ct[32], st[32];
-            if (rot) {  // 32 consecutive cos / sin of this row: 8 + 8 16-byte loads
-              const float4* c4 = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(trow) * half + c);
-              const float4* s4 = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(trow) * half + c);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 cv = c4[i], sv = s4[i];
-                ct[4 * i] = cv.x, ct[4 * i + 1] = cv.y, ct[4 * i + 2] = cv.z, ct[4 * i + 3] = cv.w;
-                st[4 * i] = sv.x, st[4 * i + 1] = sv.y, st[4 * i + 2] = sv.z, st[4 * i + 3] = sv.w;
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              float a = __uint_as_float(ra[i]), b = __uint_as_float(rb[i]);
-              if (FP8) {
-                a *= as * p.w_scale[hc + c + i];
-                b *= as * p.w_scale[hc + half + c + i];
-              }
-              if (p.bias) {
-                a += __bfloat162float(p.bias[hc + c + i]);
-                b += __bfloat162float(p.bias[hc + half + c + i]);
-              }
-              if (rot) {
-                a = bf16_round(a);
-                b = bf16_round(b);
-                const float cs = ct[i], sn = st[i];
-                va[i] = bf16_round(a * cs) + bf16_round(-b * sn);
-                vb[i] = bf16_round(b * cs) + bf16_round(a * sn);
-              } else {
-                va[i] = a;
-                vb[i] = b;
-              }
-            }
-            store_chunk<FP8>(p, row, hc + c, cols_out, va);
-            store_chunk<FP8>(p, row, hc + half + c, cols_out, vb);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          const int col = tn * BN + c;
-          if (col >= p.n) break;
-          uint32_t r[32];
-          tmem_ld32(taddr + c, r);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float x = __uint_as_float(r[i]);
-            if (FP8) x *= as * (col + i < p.n ? p.w_scale[col + i] : 0.f);
-            if (p.bias && col + i < p.n) x += __bfloat162float(p.bias[col + i]);
-            v[i] = x;
-          }
-          store_chunk<FP8>(p, row, col, cols_out, v);
-        }
-      }
+      epilogue_tile<FP8>(p, taddr, row, tn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -322,6 +329,155 @@ done:
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a cluster of two CTAs on two SMs computes one 256 x 256
+// tile. CTA r stages rows [128 r, 128 r + 128) of the tile's A and W slices (32 KB per
+// stage, 6 stages); the even CTA issues tcgen05.mma.cta_group::2 (M = 256), which writes
+// each CTA's 128 accumulator rows into its own TMEM. Each CTA's TMA loads complete on the
+// even CTA's "full" barrier (no multicast); MMA completion is signalled to both CTAs'
+// barriers by a multicast commit; the odd CTA's epilogue releases an accumulator buffer on
+// the even CTA's barrier through a mapped cluster address. Per SM this halves the W bytes
+// staged per FLOP and leaves room for 6 stages.
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * KBYTES, P_B_BYTES = 128 * KBYTES;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+
+template <bool FP8>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + P_STAGES * P_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + P_STAGES * P_B_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_rank();  // 0: leader (issues the MMAs), 1: peer
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int tiles_m = (p.m + 255) / 256;
+  const int num_tiles = tiles_m * p.tiles_n;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int k_iters = (p.k * (FP8 ? 1 : 2) + KBYTES - 1) / KBYTES;
+  constexpr int KELEM = FP8 ? KBYTES : KBYTES / 2;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&ta);
+      tma_prefetch_desc(&tb);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < num_tiles; t += n_pairs) {
+        const int tm = t % tiles_m, tn = t / tiles_m;
+        for (int ki = 0; ki < k_iters; ++ki) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            report(p.status, kTimeoutEmpty);
+            goto done;
+          }
+          const uint32_t fb = map_shared(smem_u32(&full[stage]), 0);
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          tma_load_2d_pair(sa + stage * P_A_BYTES, &ta, fb, ki * KELEM, tm * 256 + rank * 128);
+          tma_load_2d_pair(sb + stage * P_B_BYTES, &tb, fb, ki * KELEM, tn * BN + rank * 128);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && elect_one()) {
+      constexpr uint32_t idesc = FP8 ? idesc_e4m3(256, BN) : idesc_bf16(256, BN, false, false);
+      int stage = 0, buf = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      for (int t = pair; t < num_tiles; t += n_pairs) {
+        if (!mbar_wait(&tempty[buf], acc_phase ^ 1)) {
+          report(p.status, kTimeoutEmpty);
+          goto done;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int ki = 0; ki < k_iters; ++ki) {
+          if (!mbar_wait(&full[stage], phase)) {
+            report(p.status, kTimeoutFull);
+            goto done;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + stage * P_A_BYTES), b0 = smem_u32(sb + stage * P_B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t da = desc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t db = desc_sw128(b0 + kk * 32, 16, 1024);
+            if (FP8)
+              mma_f8_ss_pair(d, da, db, idesc, (ki | kk) != 0);
+            else
+              mma_f16_ss_pair(d, da, db, idesc, (ki | kk) != 0);
+          }
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit_pair(&tfull[buf], 0x3);
+        buf ^= 1;
+        if (buf == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    const int sub = warp & 3;
+    const int r_in = sub * 32 + lane;
+    const uint32_t te0 = map_shared(smem_u32(&tempty[0]), 0), te1 = map_shared(smem_u32(&tempty[1]), 0);
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < num_tiles; t += n_pairs) {
+      const int tm = t % tiles_m, tn = t / tiles_m;
+      if (!mbar_wait(&tfull[buf], acc_phase)) {
+        report(p.status, kTimeoutMma);
+        break;
+      }
+      tc_fence_after();
+      const int row = tm * 256 + static_cast<int>(rank) * 128 + r_in;
+      epilogue_tile<FP8>(p, tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN, row, tn);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(buf ? te1 : te0);
+      buf ^= 1;
+      if (buf == 0) acc_phase ^= 1;
+    }
+  }
+done:
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the pair may still touch its shared memory or TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -358,6 +514,36 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
   }
   p.tiles_m = (p.m + BM - 1) / BM;
   p.tiles_n = (p.n + BN - 1) / BN;
+  if (p.m >= 256) {  // CTA pairs: 256 x 256 tiles, each CTA stages 128 rows of A and of W
+    CUtensorMap tb2;
+    uint64_t dims[2] = {static_cast<uint64_t>(p.k), static_cast<uint64_t>(p.n)};
+    uint64_t strides[1] = {static_cast<uint64_t>(ldw) * esize};
+    uint32_t box[2] = {kbox, 128};
+    int rc = make_tmap(&tb2, w, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const int tiles = ((p.m + 255) / 256) * p.tiles_n;
+    const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
+    static bool pconf[2] = {false, false};
+    if (!pconf[FP8]) {
+      DAN_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    P_SMEM_BYTES));
+      pconf[FP8] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    DAN_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, ta, tb2, p));
+    return 0;
+  }
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   static bool configured[2] = {false, false};
