@@ -112,6 +112,23 @@ def deltanet(iters):
     return {"tokens": n, "segments": rl.n_segs, "ms": ms}
 
 
+def fp8peak(iters):
+    """Library FP8 reference point: torch._scaled_mm (cuBLASLt) e4m3 8192^3 with row-wise scales,
+    best of ``iters`` back-to-back launches (burst) — the FP8 roofline denominator."""
+    dev = torch.device("cuda")
+    n = 8192
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    sa = torch.ones(n, 1, device=dev)
+    sb = torch.ones(1, n, device=dev)
+    best = min(_time(lambda: torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16), 4)
+               for _ in range(max(iters, 3)))
+    xq, xs = ops.quantize_e4m3(torch.randn(n, n, device=dev).bfloat16())
+    wq, ws = ops.quantize_e4m3(torch.randn(n, n, device=dev).bfloat16())
+    ours = min(_time(lambda: ops.linear_e4m3(xq, xs, wq, ws), 4) for _ in range(max(iters, 3)))
+    return {"scaled_mm_tflops": 2 * n ** 3 / best / 1e9, "ours_tflops": 2 * n ** 3 / ours / 1e9}
+
+
 def norm(iters):
     dev = torch.device("cuda")
     x = torch.randn(7089, 4096, device=dev).bfloat16()
@@ -122,7 +139,7 @@ def norm(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "norm"])
+    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "norm", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()
     res = globals()[a.case](max(a.iters, 2))
