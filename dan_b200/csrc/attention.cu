@@ -694,17 +694,24 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        // pass 1: row max of the visible raw scores (two 64-column TMEM loads)
+        // S is read in 32-column chunks through two register buffers, each load issued before
+        // the previous chunk is processed. Pass 1 (row max) walks chunks 3..0 so chunk 0 is still
+        // held for pass 2, which walks 0..3: P for chunk c overwrites S columns [16c, 16c + 16),
+        // all of which belong to chunks already consumed.
+        uint32_t x[32], y[32];
         float mx = -INFINITY;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t s0[32], s1[32];
-          tmem_ld32(s_addr + 64 * hh, s0);
-          tmem_ld32(s_addr + 64 * hh + 32, s1);
-          tmem_wait_ld();
-          chunk_max(s0, mw[2 * hh], mx);
-          chunk_max(s1, mw[2 * hh + 1], mx);
-        }
+        tmem_ld32(s_addr + 96, x);
+        tmem_wait_ld();
+        tmem_ld32(s_addr + 64, y);
+        chunk_max(x, mw[3], mx);
+        tmem_wait_ld();
+        tmem_ld32(s_addr + 32, x);
+        chunk_max(y, mw[2], mx);
+        tmem_wait_ld();
+        tmem_ld32(s_addr + 0, y);
+        chunk_max(x, mw[1], mx);
+        tmem_wait_ld();
+        chunk_max(y, mw[0], mx);
         const float m_new = fmaxf(m, mx * sl2);
         bool rescale = false;
         float alpha = 1.f;
@@ -718,24 +725,32 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         const float mu = m == -INFINITY ? 0.f : m;
-        // pass 2: P = exp2(s * scale_log2 - m) as bf16 pairs over the consumed S columns
         float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t s0[32], s1[32];
-          tmem_ld32(s_addr + 64 * hh, s0);
-          tmem_ld32(s_addr + 64 * hh + 32, s1);
+        {
+          uint32_t pk[16];
+          tmem_ld32(s_addr + 32, x);
+          chunk_exp(y, mw[0], sl2, mu, sum0, pk);
+          tmem_st16(s_addr + 0, pk);
           tmem_wait_ld();
-          {
-            uint32_t pk[16];
-            chunk_exp(s0, mw[2 * hh], sl2, mu, sum0, pk);
-            tmem_st16(s_addr + 32 * hh, pk);
-          }
-          {
-            uint32_t pk[16];
-            chunk_exp(s1, mw[2 * hh + 1], sl2, mu, sum1, pk);
-            tmem_st16(s_addr + 32 * hh + 16, pk);
-          }
+        }
+        {
+          uint32_t pk[16];
+          tmem_ld32(s_addr + 64, y);
+          chunk_exp(x, mw[1], sl2, mu, sum1, pk);
+          tmem_st16(s_addr + 16, pk);
+          tmem_wait_ld();
+        }
+        {
+          uint32_t pk[16];
+          tmem_ld32(s_addr + 96, x);
+          chunk_exp(y, mw[2], sl2, mu, sum0, pk);
+          tmem_st16(s_addr + 32, pk);
+          tmem_wait_ld();
+        }
+        {
+          uint32_t pk[16];
+          chunk_exp(x, mw[3], sl2, mu, sum1, pk);
+          tmem_st16(s_addr + 48, pk);
         }
         l = l * alpha + (sum0 + sum1);
         if (__any_sync(0xffffffffu, rescale)) {

@@ -7,7 +7,8 @@
 // back with tcgen05.ld and apply the fused epilogue. The kernel is persistent
 // (one CTA per SM, tiles strided by the grid) and double-buffers the TMEM
 // accumulator (2 x 256 columns) so the epilogue of tile i overlaps the main
-// loop of tile i+1.
+// loop of tile i+1. For M >= 256 a CTA-pair variant computes 256 x 256 tiles
+// in a grouped order that keeps the smaller operand's slice resident in L2.
 //
 // Epilogues (replacing separate passes of the reference):
 //   store     C = bf16(acc [+ bias])                          (nn.Linear, llama.py:78,102)
@@ -48,7 +49,26 @@ struct Params {
   const float* cos_t;   // kRope: [m, hd/2] bf16-rounded cos of each row's angles
   const float* sin_t;
   int32_t* status;
+  int order;    // pair kernel tile order: 0 = m fastest (A stays in L2), 1 = n fastest (W stays)
+  int group;    // pair kernel: tile rows (order 0) or columns (order 1) per raster group
 };
+
+constexpr int64_t kGroupBytes = 32LL << 20;
+
+// Tile t of the pair kernel's sequence. Tiles run in groups of ``group`` rows (order 0) or
+// columns (order 1) of the tile grid; inside a group the grouped dimension varies fastest, so
+// each wave re-touches the group's stationary operand slice and streams the other operand.
+__device__ __forceinline__ void pair_tile(int t, int tiles_m, int tiles_n, int order, int group, int& tm,
+                                          int& tn) {
+  const int gdim = order == 0 ? tiles_m : tiles_n, odim = order == 0 ? tiles_n : tiles_m;
+  const int per = group * odim;
+  const int g = t / per, r = t - g * per;
+  const int first = g * group;
+  const int span = gdim - first < group ? gdim - first : group;
+  const int a = first + r % span, b = r / span;
+  tm = order == 0 ? a : b;
+  tn = order == 0 ? b : a;
+}
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
@@ -392,8 +412,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       tma_prefetch_desc(&tb);
       int stage = 0;
       uint32_t phase = 0;
+      // The operand every wave of tiles touches in full (A for m-fastest order, W for n-fastest)
+      // is the one worth keeping in L2; the other streams through.
+      const uint64_t keep = l2_evict_last(), pass = l2_evict_normal();
+      const uint64_t pol_a = p.order == 0 ? keep : pass, pol_b = p.order == 0 ? pass : keep;
       for (int t = pair; t < num_tiles; t += n_pairs) {
-        const int tm = t % tiles_m, tn = t / tiles_m;
+        int tm, tn;
+        pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
         for (int ki = 0; ki < k_iters; ++ki) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             report(p.status, kTimeoutEmpty);
@@ -401,8 +426,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const uint32_t fb = map_shared(smem_u32(&full[stage]), 0);
           if (rank == 0) mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
-          tma_load_2d_pair(sa + stage * P_A_BYTES, &ta, fb, ki * KELEM, tm * 256 + rank * 128);
-          tma_load_2d_pair(sb + stage * P_B_BYTES, &tb, fb, ki * KELEM, tn * BN + rank * 128);
+          tma_load_2d_pair_hint(sa + stage * P_A_BYTES, &ta, fb, ki * KELEM, tm * 256 + rank * 128, pol_a);
+          tma_load_2d_pair_hint(sb + stage * P_B_BYTES, &tb, fb, ki * KELEM, tn * BN + rank * 128, pol_b);
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -456,7 +481,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     int buf = 0;
     uint32_t acc_phase = 0;
     for (int t = pair; t < num_tiles; t += n_pairs) {
-      const int tm = t % tiles_m, tn = t / tiles_m;
+      int tm, tn;
+      pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
       if (!mbar_wait(&tfull[buf], acc_phase)) {
         report(p.status, kTimeoutMma);
         break;
@@ -522,6 +548,14 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
     int rc = make_tmap(&tb2, w, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     const int tiles = ((p.m + 255) / 256) * p.tiles_n;
+    // Rasterization: the smaller operand is the stationary one (every wave of a group re-reads
+    // its slice, held in L2 with an evict_last policy) and tiles are grouped so that the
+    // stationary slice of a group is at most kGroupBytes (data read by SMs of both dies only
+    // gets about half of the 126 MB L2).
+    p.order = static_cast<int64_t>(p.m) <= p.n ? 0 : 1;
+    const int gdim = p.order == 0 ? (p.m + 255) / 256 : p.tiles_n;
+    const int64_t grp = kGroupBytes / (256LL * p.k * esize);
+    p.group = grp < 1 ? 1 : (grp < gdim ? static_cast<int>(grp) : gdim);
     const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
     static bool pconf[2] = {false, false};
     if (!pconf[FP8]) {
