@@ -109,7 +109,8 @@ def status_word(device):
 
 
 STATUS_TEXT = {1: "a TMA load never landed", 2: "a pipeline stage was never released",
-               3: "an MMA commit never arrived", 4: "the softmax warps never finished", 5: "an index was out of range"}
+               3: "an MMA commit never arrived", 4: "the softmax warps never finished", 5: "an index was out of range",
+               6: "a stream-K partial tile never arrived"}
 
 
 def check_status(device):

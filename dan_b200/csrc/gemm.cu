@@ -8,7 +8,11 @@
 // (one CTA per SM, tiles strided by the grid) and double-buffers the TMEM
 // accumulator (2 x 256 columns) so the epilogue of tile i overlaps the main
 // loop of tile i+1. For M >= 256 a CTA-pair variant computes 256 x 256 tiles
-// in a grouped order that keeps the smaller operand's slice resident in L2.
+// in a grouped order that keeps the smaller operand's slice resident in L2,
+// and splits the last ragged wave of deep (>= 128 K iterations) tiles by K
+// across all pairs (stream-K, partial sums reduced in a fixed order).
+// Each epilogue warp stages 32 x 32 output chunks in shared memory and sends
+// them with TMA stores (the residual arrives by TMA load the same way).
 //
 // Epilogues (replacing separate passes of the reference):
 //   store     C = bf16(acc [+ bias])                          (nn.Linear, llama.py:78,102)
@@ -18,6 +22,9 @@
 // The e4m3 variant multiplies acc by a_scale[row] * w_scale[col] first
 // (torch._scaled_mm with row-wise scales, quant.py:37-42).
 #include "common.cuh"
+
+#include <map>
+#include <mutex>
 
 namespace dan {
 namespace gemm {
@@ -29,7 +36,7 @@ constexpr int A_BYTES = BM * KBYTES;
 constexpr int B_BYTES = BN * KBYTES;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES_BASE = STAGES * STAGE_BYTES + 1024 + 512;  // + the epilogue sink
 
 enum Epilogue { kStore = 0, kResidual = 1, kSwiglu = 2, kRope = 3 };
 
@@ -51,6 +58,13 @@ struct Params {
   int32_t* status;
   int order;    // pair kernel tile order: 0 = m fastest (A stays in L2), 1 = n fastest (W stays)
   int group;    // pair kernel: tile rows (order 0) or columns (order 1) per raster group
+  // Stream-K (pair kernel): tiles [sk_first, tiles) are split by K iteration across the pairs,
+  // sk_iters iterations in all; 0 = every tile whole.
+  int sk_first, sk_iters;
+  float* sk_part;     // [pairs][2][BN][128] fp32 partial accumulators, column-major per CTA
+  uint32_t* sk_flag;  // [pairs][2][4] per-warp "partial written" flags (value = epoch + 1)
+  uint32_t* sk_ctrl;  // [0] epoch, [1] CTAs finished in this launch
+  int tma_out;        // epilogue writes through the shared-memory sink and TMA stores
 };
 
 constexpr int64_t kGroupBytes = 32LL << 20;
@@ -70,7 +84,36 @@ __device__ __forceinline__ void pair_tile(int t, int tiles_m, int tiles_n, int o
   tn = order == 0 ? b : a;
 }
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// The pair kernel's work list: whole tiles pair, pair + P, ... below sk_first, then this pair's
+// contiguous share [g, g1) of the stream-K iterations, cut at tile boundaries into segments
+// (t, kb, ke). A pair's share is contiguous, so only its first segment can start inside a
+// tile and only its last can stop inside one.
+struct PairWork {
+  int next_dp, dp_end, n_pairs, k_iters, g, g1;
+  __device__ __forceinline__ PairWork(int pair, int P, const Params& p, int ki)
+      : next_dp(pair), dp_end(p.sk_first), n_pairs(P), k_iters(ki) {
+    g = static_cast<int>(static_cast<long long>(pair) * p.sk_iters / P);
+    g1 = static_cast<int>(static_cast<long long>(pair + 1) * p.sk_iters / P);
+  }
+  __device__ __forceinline__ bool next(int& t, int& kb, int& ke) {
+    if (next_dp < dp_end) {
+      t = next_dp;
+      kb = 0;
+      ke = k_iters;
+      next_dp += n_pairs;
+      return true;
+    }
+    if (g >= g1) return false;
+    const int tr = g / k_iters;
+    t = dp_end + tr;
+    kb = g - tr * k_iters;
+    ke = kb + (g1 - g) < k_iters ? kb + (g1 - g) : k_iters;
+    g += ke - kb;
+    return true;
+  }
+};
+
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <bool FP8>
 __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, int cols_out, const float* v) {
@@ -109,16 +152,154 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, i
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+  } else {  // ragged edge or unaligned row: element stores (constant indices keep packed[] in registers)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (col + 2 * i < cols_out) dst[2 * i] = __ushort_as_bfloat16(static_cast<unsigned short>(packed[i] & 0xffffu));
+      if (col + 2 * i + 1 < cols_out) dst[2 * i + 1] = __ushort_as_bfloat16(static_cast<unsigned short>(packed[i] >> 16));
+    }
+  }
+}
+
+// Output path of one epilogue warp. With ``tma`` set (C, and R for the residual epilogue, are
+// 16-byte aligned with 16-byte row pitch) each 32-row x 32-column bf16 chunk is written to one
+// of the warp's four 2 KB shared-memory slots and leaves by a TMA store, which writes whole
+// lines and clips rows >= m and columns >= the output width; the residual of a chunk arrives
+// in its slot by TMA load one chunk ahead. Otherwise every thread stores its own row.
+struct Sink {
+  bool tma;
+  uint8_t* stage;  // this warp's 4 slots of 32 rows x 64 bytes
+  uint64_t* bar;   // this warp's 4 residual-load barriers
+  const CUtensorMap* tc;
+  const CUtensorMap* tr;
+  uint32_t seq;    // chunks this warp has sent so far (slot = seq % 4)
+  uint32_t phase;  // bit s: parity of slot s's next residual-load completion
+  int row0;        // first output row of this warp's 32 rows in the current tile
+  int lane;
+  int m;           // rows of C: a warp whose rows all lie at or past m sends nothing
+};
+
+constexpr int SLOT_BYTES = 32 * 64;
+constexpr int SINK_BYTES = 4 * 4 * SLOT_BYTES;  // 4 epilogue warps x 4 slots
+
+__device__ __forceinline__ void pack32(const float* v, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+}
+
+// Send one packed chunk (this lane's 32 values of row row0 + lane, columns [col, col + 32)).
+__device__ __forceinline__ void sink_put(Sink& o, int col, const uint32_t (&pk)[16]) {
+  if (o.row0 >= o.m) return;
+  uint8_t* slot = o.stage + (o.seq & 3) * SLOT_BYTES;
+  if (o.lane == 0) bulk_wait_read<3>();  // the store sent from this slot four chunks ago has read it
+  __syncwarp();
+  uint4* d = reinterpret_cast<uint4*>(slot + o.lane * 64);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+  fence_proxy_async();
+  __syncwarp();
+  if (o.lane == 0) {
+    tma_store_2d(o.tc, slot, col, o.row0);
+    bulk_commit();
+  }
+  __syncwarp();  // reconverge before the next warp-collective tcgen05.ld
+  ++o.seq;
+}
+
+// Write 32 epilogue values of one row: through the sink, or directly (store_chunk).
+template <bool FP8>
+__device__ __forceinline__ void emit(Sink& o, const Params& p, int row, int col, int cols_out, const float* v) {
+  if (o.tma) {
+    uint32_t pk[16];
+    pack32(v, pk);
+    sink_put(o, col, pk);
   } else {
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(packed);
-    for (int i = 0; i < 32 && col + i < cols_out; ++i) dst[i] = h[i];
+    store_chunk<FP8>(p, row, col, cols_out, v);
+  }
+}
+
+__device__ __forceinline__ void sink_load_resid(Sink& o, uint32_t seq, int col) {
+  const uint32_t s = seq & 3;
+  mbar_expect_tx(&o.bar[s], SLOT_BYTES);
+  tma_load_2d(o.stage + s * SLOT_BYTES, o.tr, &o.bar[s], col, o.row0);
+}
+
+// Residual epilogue through the sink: C = bf16(R + bf16(acc [+ bias])) chunk by chunk, the
+// next chunk's residual loading while this one is computed.
+template <bool FP8>
+__device__ __forceinline__ void residual_tma(Sink& o, const Params& p, uint32_t taddr, int col0, float as) {
+  if (o.row0 >= p.m) return;
+  const int width = p.n - col0 < BN ? p.n - col0 : BN;
+  const int nch = (width + 31) / 32;
+  if (o.lane == 0) {
+    bulk_wait_read<3>();
+    sink_load_resid(o, o.seq, col0);
+  }
+  __syncwarp();
+#pragma unroll 1
+  for (int i = 0; i < nch; ++i) {
+    const int col = col0 + 32 * i;
+    const uint32_t s = o.seq & 3;
+    uint32_t r[32];
+    tmem_ld32(taddr + 32 * i, r);
+    if (o.lane == 0 && i + 1 < nch) {
+      bulk_wait_read<2>();  // the slot the next residual lands in has been read by its last store
+      sink_load_resid(o, o.seq + 1, col + 32);
+    }
+    __syncwarp();
+    tmem_wait_ld_regs(r);
+    if (!mbar_wait(&o.bar[s], (o.phase >> s) & 1u)) report(p.status, kTimeoutFull);
+    o.phase ^= 1u << s;
+    uint4* slot = reinterpret_cast<uint4*>(o.stage + s * SLOT_BYTES + o.lane * 64);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint4 q = slot[g];
+      uint32_t pk[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = 8 * g + 2 * j;
+        float x0 = __uint_as_float(r[c]), x1 = __uint_as_float(r[c + 1]);
+        if (FP8) {
+          x0 *= as * (col + c < p.n ? p.w_scale[col + c] : 0.f);
+          x1 *= as * (col + c + 1 < p.n ? p.w_scale[col + c + 1] : 0.f);
+        }
+        if (p.bias) {
+          x0 += col + c < p.n ? __bfloat162float(p.bias[col + c]) : 0.f;
+          x1 += col + c + 1 < p.n ? __bfloat162float(p.bias[col + c + 1]) : 0.f;
+        }
+        const uint32_t rw = (&q.x)[j];
+        const float2 rf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw));
+        pk[j] = pack_bf16(rf.x + bf16_round(x0), rf.y + bf16_round(x1));
+      }
+      slot[g] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (o.lane == 0) {
+      tma_store_2d(o.tc, o.stage + s * SLOT_BYTES, col, o.row0);
+      bulk_commit();
+    }
+    __syncwarp();
+    ++o.seq;
+  }
+}
+
+// Pull the row's RoPE cos / sin into L2 while the tile's main loop still runs.
+__device__ __forceinline__ void epilogue_prefetch(const Params& p, int row, int tn) {
+  if (row >= p.m || p.epilogue != kRope || tn * BN >= p.rope_cols) return;
+  const int half = p.rope_hd / 2;
+  const char* c = reinterpret_cast<const char*>(p.cos_t + static_cast<int64_t>(row) * half);
+  const char* s = reinterpret_cast<const char*>(p.sin_t + static_cast<int64_t>(row) * half);
+  for (int b = 0; b < half * 4; b += 128) {
+    prefetch_l2(c + b);
+    prefetch_l2(s + b);
   }
 }
 
 // The fused epilogue of one 128-row x 256-column accumulator tile held in TMEM at ``taddr``
 // (this warp's lanes): ``row`` is this thread's output row, ``tn`` the tile's column block.
 template <bool FP8>
-__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, int row, int tn) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t taddr, int row, int tn) {
   const int cols_out = p.epilogue == kSwiglu ? p.n / 2 : p.n;
   const float as = (FP8 && row < p.m) ? p.a_scale[row] : 1.f;
   if (p.epilogue == kSwiglu) {
@@ -145,7 +326,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
         uv = bf16_round(uv);
         v[i] = silu(gv) * uv;
       }
-      store_chunk<FP8>(p, row, tn * (BN / 2) + c, cols_out, v);
+      emit<FP8>(o, p, row, tn * (BN / 2) + c, cols_out, v);
     }
   } else if (p.epilogue == kRope) {
     // q/k heads: rotate-half RoPE on the bf16-rounded projection with the reference's
@@ -197,14 +378,20 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
             vb[i] = b;
           }
         }
-        store_chunk<FP8>(p, row, hc + c, cols_out, va);
-        store_chunk<FP8>(p, row, hc + half + c, cols_out, vb);
+        emit<FP8>(o, p, row, hc + c, cols_out, va);
+        emit<FP8>(o, p, row, hc + half + c, cols_out, vb);
       }
     }
   } else {
+    const int col0 = tn * BN;
+    if (col0 >= p.n) return;
+    if (o.tma && p.epilogue == kResidual) {
+      residual_tma<FP8>(o, p, taddr, col0, as);
+      return;
+    }
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
-      const int col = tn * BN + c;
+      const int col = col0 + c;
       if (col >= p.n) break;
       uint32_t r[32];
       tmem_ld32(taddr + c, r);
@@ -217,23 +404,26 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
         if (p.bias && col + i < p.n) x += __bfloat162float(p.bias[col + i]);
         v[i] = x;
       }
-      store_chunk<FP8>(p, row, col, cols_out, v);
+      emit<FP8>(o, p, row, col, cols_out, v);
     }
   }
 }
 
 template <bool FP8>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                const __grid_constant__ CUtensorMap tc, const __grid_constant__ CUtensorMap tr, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * B_BYTES);
+  uint8_t* sink = sb + STAGES * B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sink + SINK_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // 4 warps x 4 residual-load barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 16);
 
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
@@ -245,6 +435,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);
     }
+    for (int b = 0; b < 16; ++b) mbar_init(&rbar[b], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -324,24 +515,28 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     const int sub = warp & 3;  // TMEM sub-partition this warp may read
     const int r_in = sub * 32 + lane;
+    Sink o{p.tma_out != 0, sink + sub * 4 * SLOT_BYTES, rbar + sub * 4, &tc, &tr, 0u, 0u, 0, lane, p.m};
     int buf = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int tm = t % p.tiles_m, tn = t / p.tiles_m;
+      epilogue_prefetch(p, tm * BM + r_in, tn);
       if (!mbar_wait(&tfull[buf], acc_phase)) {
         report(p.status, kTimeoutMma);
         break;
       }
       tc_fence_after();
       const int row = tm * BM + r_in;
+      o.row0 = tm * BM + sub * 32;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
-      epilogue_tile<FP8>(p, taddr, row, tn);
+      epilogue_tile<FP8>(p, o, taddr, row, tn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
       buf ^= 1;
       if (buf == 0) acc_phase ^= 1;
     }
+    if (lane == 0) bulk_wait_all();  // TMA stores done before the CTA (and its shared memory) ends
   }
 done:
   __syncwarp();
@@ -364,20 +559,74 @@ done:
 constexpr int P_STAGES = 6;
 constexpr int P_A_BYTES = 128 * KBYTES, P_B_BYTES = 128 * KBYTES;
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + SINK_BYTES + 1024 + 512;
+
+// Stream-K partials. Slot (pair, rank) holds one CTA's 128 x 256 fp32 accumulator stored
+// column-major ([col][row]) so a warp's 32 rows of one column are one 128-byte line.
+__device__ __forceinline__ float* sk_slot(const Params& p, int slot) {
+  return p.sk_part + static_cast<int64_t>(slot) * BN * 128;
+}
+
+__device__ __forceinline__ void sk_store_partial(const Params& p, uint32_t taddr, int slot, int r_in, int sub,
+                                                 int lane, uint32_t epoch) {
+  float* dst = sk_slot(p, slot) + r_in;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) __stcg(dst + (c + i) * 128, __uint_as_float(r[i]));
+  }
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_gpu(p.sk_flag + slot * 4 + sub, epoch + 1);
+}
+
+// Head of a split tile: add the partials of pairs pair+1, ... whose shares start inside the
+// tile (before iteration ``tile_end``), in pair order, into this warp's TMEM accumulator rows.
+__device__ __forceinline__ void sk_gather_partials(const Params& p, uint32_t taddr, int pair, int n_pairs, int rank,
+                                                   int r_in, int sub, uint32_t epoch, int tile_end) {
+  int q_end = pair + 1;
+  while (q_end < n_pairs && static_cast<int>(static_cast<long long>(q_end) * p.sk_iters / n_pairs) < tile_end)
+    ++q_end;
+  for (int q = pair + 1; q < q_end; ++q)
+    if (!wait_flag(p.sk_flag + (q * 2 + rank) * 4 + sub, epoch + 1)) report(p.status, kTimeoutPartial);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);
+    tmem_wait_ld();
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(r[i]);
+    for (int q = pair + 1; q < q_end; ++q) {
+      const float* src = sk_slot(p, q * 2 + rank) + r_in;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] += __ldcg(src + (c + i) * 128);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(acc[i]);
+    tmem_st32(taddr + c, r);
+  }
+  tmem_wait_st();
+}
 
 template <bool FP8>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                     const __grid_constant__ CUtensorMap tc, const __grid_constant__ CUtensorMap tr, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + P_STAGES * P_A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + P_STAGES * P_B_BYTES);
+  uint8_t* sink = sb + P_STAGES * P_B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sink + SINK_BYTES);
   uint64_t* empty = full + P_STAGES;
   uint64_t* tfull = empty + P_STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // 4 warps x 4 residual-load barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 16);
 
   const int warp = warp_id(), lane = lane_id();
   const uint32_t rank = cluster_rank();  // 0: leader (issues the MMAs), 1: peer
@@ -390,6 +639,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA of the pair
     }
+    for (int b = 0; b < 16; ++b) mbar_init(&rbar[b], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -401,7 +651,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int tiles_m = (p.m + 255) / 256;
-  const int num_tiles = tiles_m * p.tiles_n;
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
   const int k_iters = (p.k * (FP8 ? 1 : 2) + KBYTES - 1) / KBYTES;
   constexpr int KELEM = FP8 ? KBYTES : KBYTES / 2;
@@ -416,10 +665,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       // is the one worth keeping in L2; the other streams through.
       const uint64_t keep = l2_evict_last(), pass = l2_evict_normal();
       const uint64_t pol_a = p.order == 0 ? keep : pass, pol_b = p.order == 0 ? pass : keep;
-      for (int t = pair; t < num_tiles; t += n_pairs) {
+      PairWork work(pair, n_pairs, p, k_iters);
+      int t, kb, ke;
+      while (work.next(t, kb, ke)) {
         int tm, tn;
         pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
-        for (int ki = 0; ki < k_iters; ++ki) {
+        for (int ki = kb; ki < ke; ++ki) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             report(p.status, kTimeoutEmpty);
             goto done;
@@ -440,14 +691,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t idesc = FP8 ? idesc_e4m3(256, BN) : idesc_bf16(256, BN, false, false);
       int stage = 0, buf = 0;
       uint32_t phase = 0, acc_phase = 0;
-      for (int t = pair; t < num_tiles; t += n_pairs) {
+      PairWork work(pair, n_pairs, p, k_iters);
+      int t, kb, ke;
+      while (work.next(t, kb, ke)) {
         if (!mbar_wait(&tempty[buf], acc_phase ^ 1)) {
           report(p.status, kTimeoutEmpty);
           goto done;
         }
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int ki = 0; ki < k_iters; ++ki) {
+        for (int ki = kb; ki < ke; ++ki) {
           if (!mbar_wait(&full[stage], phase)) {
             report(p.status, kTimeoutFull);
             goto done;
@@ -459,9 +712,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t da = desc_sw128(a0 + kk * 32, 16, 1024);
             const uint64_t db = desc_sw128(b0 + kk * 32, 16, 1024);
             if (FP8)
-              mma_f8_ss_pair(d, da, db, idesc, (ki | kk) != 0);
+              mma_f8_ss_pair(d, da, db, idesc, (ki != kb) || (kk != 0));
             else
-              mma_f16_ss_pair(d, da, db, idesc, (ki | kk) != 0);
+              mma_f16_ss_pair(d, da, db, idesc, (ki != kb) || (kk != 0));
           }
           mma_commit_pair(&empty[stage], 0x3);
           if (++stage == P_STAGES) {
@@ -478,24 +731,41 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int sub = warp & 3;
     const int r_in = sub * 32 + lane;
     const uint32_t te0 = map_shared(smem_u32(&tempty[0]), 0), te1 = map_shared(smem_u32(&tempty[1]), 0);
+    Sink o{p.tma_out != 0, sink + sub * 4 * SLOT_BYTES, rbar + sub * 4, &tc, &tr, 0u, 0u, 0, lane, p.m};
     int buf = 0;
     uint32_t acc_phase = 0;
-    for (int t = pair; t < num_tiles; t += n_pairs) {
+    const uint32_t epoch = p.sk_iters ? __ldcg(p.sk_ctrl) : 0u;
+    PairWork work(pair, n_pairs, p, k_iters);
+    int t, kb, ke;
+    while (work.next(t, kb, ke)) {
       int tm, tn;
       pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
+      if (kb == 0) epilogue_prefetch(p, tm * 256 + static_cast<int>(rank) * 128 + r_in, tn);
       if (!mbar_wait(&tfull[buf], acc_phase)) {
         report(p.status, kTimeoutMma);
         break;
       }
       tc_fence_after();
       const int row = tm * 256 + static_cast<int>(rank) * 128 + r_in;
-      epilogue_tile<FP8>(p, tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN, row, tn);
+      o.row0 = tm * 256 + static_cast<int>(rank) * 128 + sub * 32;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
+      const int slot = pair * 2 + static_cast<int>(rank);
+      if (kb > 0) {
+        // Tail of a split tile: park the partial sum for the pair that owns the tile's head.
+        sk_store_partial(p, taddr, slot, r_in, sub, lane, epoch);
+      } else {
+        if (ke < k_iters)  // head of a split tile: fold in the later pairs' partials first
+          sk_gather_partials(p, taddr, pair, n_pairs, static_cast<int>(rank), r_in, sub, epoch,
+                             (t - p.sk_first + 1) * k_iters);
+        epilogue_tile<FP8>(p, o, taddr, row, tn);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(buf ? te1 : te0);
       buf ^= 1;
       if (buf == 0) acc_phase ^= 1;
     }
+    if (lane == 0) bulk_wait_all();  // TMA stores done before the CTA (and its shared memory) ends
   }
 done:
   __syncwarp();
@@ -505,6 +775,52 @@ done:
     tc_fence_after();
     tmem_dealloc_pair(tmem, 512);
   }
+  if (p.sk_iters && threadIdx.x == 0) {
+    // The last CTA out advances the epoch, so the next launch's flags never match this one's.
+    __threadfence();
+    if (atomicAdd(p.sk_ctrl + 1, 1u) == gridDim.x - 1) {
+      p.sk_ctrl[1] = 0;
+      __threadfence();
+      atomicAdd(p.sk_ctrl, 1u);
+    }
+  }
+}
+
+// Stream-K scratch, one per (device, stream): launches sharing one must be stream-ordered.
+// Allocated on first use (cudaMalloc) and kept for the life of the process.
+struct Workspace {
+  float* part;
+  uint32_t* flag;
+  uint32_t* ctrl;
+};
+
+static Workspace* workspace(cudaStream_t stream, int pairs) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, Workspace> all;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    set_error("cudaGetDevice failed");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = all.find({dev, stream});
+  if (it != all.end()) return &it->second;
+  Workspace w{};
+  const size_t part_bytes = static_cast<size_t>(pairs) * 2 * BN * 128 * sizeof(float);
+  const size_t flag_bytes = static_cast<size_t>(pairs) * 2 * 4 * sizeof(uint32_t) + 2 * sizeof(uint32_t);
+  void* a = nullptr;
+  void* b = nullptr;
+  if (cudaMalloc(&a, part_bytes) != cudaSuccess || cudaMalloc(&b, flag_bytes) != cudaSuccess ||
+      cudaMemset(b, 0, flag_bytes) != cudaSuccess) {
+    if (a) cudaFree(a);
+    if (b) cudaFree(b);
+    set_error("stream-K workspace allocation of %zu bytes failed", part_bytes + flag_bytes);
+    return nullptr;
+  }
+  w.part = static_cast<float*>(a);
+  w.flag = static_cast<uint32_t*>(b);
+  w.ctrl = w.flag + static_cast<size_t>(pairs) * 2 * 4;
+  return &(all[{dev, stream}] = w);
 }
 
 template <bool FP8>
@@ -538,6 +854,31 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
     int rc = make_tmap(&tb, w, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
+  // Output (and residual) maps for the TMA-store epilogue: 32 x 32 bf16 boxes, no swizzle.
+  CUtensorMap tc{}, tr{};
+  {
+    const int cols_out = p.epilogue == kSwiglu ? p.n / 2 : p.n;
+    const auto aligned = [](const void* q, int64_t ld) {
+      return (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (ld * 2) % 16 == 0;
+    };
+    p.tma_out = aligned(p.c, p.ldc) && (p.epilogue != kResidual || aligned(p.resid, p.ldr));
+    if (p.tma_out) {
+      uint64_t dims[2] = {static_cast<uint64_t>(cols_out), static_cast<uint64_t>(p.m)};
+      uint64_t strides[1] = {static_cast<uint64_t>(p.ldc) * 2};
+      uint32_t box[2] = {32, 32};
+      int rc = make_tmap(&tc, p.c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+      tr = tc;
+      if (p.epilogue == kResidual) {
+        uint64_t rdims[2] = {static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.m)};
+        uint64_t rstrides[1] = {static_cast<uint64_t>(p.ldr) * 2};
+        rc = make_tmap(&tr, p.resid, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rdims, rstrides, box,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+      }
+    }
+  }
   p.tiles_m = (p.m + BM - 1) / BM;
   p.tiles_n = (p.n + BN - 1) / BN;
   if (p.m >= 256) {  // CTA pairs: 256 x 256 tiles, each CTA stages 128 rows of A and of W
@@ -556,7 +897,31 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
     const int gdim = p.order == 0 ? (p.m + 255) / 256 : p.tiles_n;
     const int64_t grp = kGroupBytes / (256LL * p.k * esize);
     p.group = grp < 1 ? 1 : (grp < gdim ? static_cast<int>(grp) : gdim);
-    const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
+    const int max_pairs = sm_count() / 2;
+    int pairs = tiles < max_pairs ? tiles : max_pairs;
+    // Stream-K when whole tiles would leave the last wave less than 95% busy and a tile is at
+    // least 128 K iterations deep: the last (tiles % P) + P tiles (all of them if there are
+    // fewer than P) are split evenly by K iteration over all P pairs. Shallower tiles do not
+    // repay the partial-tile traffic and the reduction in the owning pair's epilogue.
+    p.sk_first = tiles;
+    p.sk_iters = 0;
+    {
+      const int k_iters = (p.k * esize + KBYTES - 1) / KBYTES;
+      const int waves = (tiles + max_pairs - 1) / max_pairs;
+      const bool ragged = static_cast<int64_t>(tiles) * 100 < static_cast<int64_t>(waves) * max_pairs * 95;
+      const int first = tiles <= max_pairs ? 0 : (tiles / max_pairs - 1) * max_pairs;
+      const int64_t iters = static_cast<int64_t>(tiles - first) * k_iters;
+      if (ragged && k_iters >= 128 && iters >= 8LL * max_pairs) {
+        Workspace* ws = workspace(stream, max_pairs);
+        if (!ws) return fail(2, "gemm: %s", last_error());
+        p.sk_first = first;
+        p.sk_iters = static_cast<int>(iters);
+        p.sk_part = ws->part;
+        p.sk_flag = ws->flag;
+        p.sk_ctrl = ws->ctrl;
+        pairs = max_pairs;
+      }
+    }
     static bool pconf[2] = {false, false};
     if (!pconf[FP8]) {
       DAN_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -575,17 +940,18 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    DAN_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, ta, tb2, p));
+    DAN_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, ta, tb2, tc, tr, p));
     return 0;
   }
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
+  constexpr int smem_bytes = SMEM_BYTES_BASE + SINK_BYTES;
   static bool configured[2] = {false, false};
   if (!configured[FP8]) {
-    DAN_CUDA(cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    DAN_CUDA(cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
     configured[FP8] = true;
   }
-  gemm_kernel<FP8><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  gemm_kernel<FP8><<<grid, THREADS, smem_bytes, stream>>>(ta, tb, tc, tr, p);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }

@@ -50,7 +50,11 @@ int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, const void*
  * Replaces nn.Linear in the decoder (dan/models/llama.py:78,87,102; qwen3_5.py:185,212,319,329,344)
  * and fuses: epilogue 0 store (+bias), 1 C = R + bf16(acc) (the residual adds, llama.py:116-117),
  * 2 SwiGLU over W rows interleaved in 128-row [gate | up] blocks, C has n/2 columns
- * (swiglu, dan/fused.py:59-61). C may alias R (in-place residual). */
+ * (swiglu, dan/fused.py:59-61). C may alias R (in-place residual).
+ * When m >= 256, k is at least 128 iterations of 128 bytes (8192 bf16 / 16384 e4m3) and the
+ * last wave of 256 x 256 tiles is ragged, the first such call on a (device, stream) allocates
+ * a stream-K workspace (cudaMalloc, ~19 MB on 148 SMs) kept for the life of the process;
+ * calls sharing a stream use it in stream order. */
 int dan_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, const void* resid,
                   int64_t ldr, const void* bias, int m, int n, int k, int epilogue, int32_t* status, void* stream);
 

@@ -28,6 +28,26 @@ def test_gemm_bf16(cuda, m, n, k):
     assert rel_err(y, x.float() @ w.float().T) < 1e-2
 
 
+@pytest.mark.parametrize("m", [100, 700])
+def test_gemm_unaligned_output(cuda, m):
+    """Outputs whose rows are not 16-byte aligned (a view at an odd column offset, odd row
+    pitch) take the per-thread store path instead of the TMA-store epilogue; residual too."""
+    g = torch.Generator(device=cuda).manual_seed(m)
+    k, n = 512, 520
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = torch.randn(n, k, device=cuda, generator=g).bfloat16()
+    buf = torch.zeros(m, n + 3, device=cuda, dtype=torch.bfloat16)
+    out = buf[:, 1:1 + n]
+    ops.linear(x, w, out=out)
+    assert rel_err(out, x.float() @ w.float().T) < 1e-2
+    assert torch.all(buf[:, 0] == 0) and torch.all(buf[:, 1 + n:] == 0)
+    rbuf = torch.randn(m, n + 3, device=cuda, generator=g).bfloat16()
+    r = rbuf[:, 1:1 + n]
+    want = r.float() + x.float() @ w.float().T
+    ops.linear(x, w, residual=r)
+    assert rel_err(r, want) < 1e-2
+
+
 def test_gemm_bias_residual(cuda):
     g = torch.Generator(device=cuda).manual_seed(1)
     m, n, k = 513, 768, 320
@@ -66,6 +86,44 @@ def test_gemm_e4m3(cuda, m, n, k):
     assert torch.equal(wq.float().cpu(), owq)
     want = OF.linear(x.cpu(), owq, ows.flatten())
     assert rel_err(y, want) < 1e-2
+
+
+# Shapes whose last wave of 256 x 256 tiles would leave CTA pairs idle, with tiles at least
+# 128 K iterations deep (K >= 8192 in bf16, 16384 in e4m3), take the stream-K path: the last
+# tiles are split by K iteration across all CTA pairs and the partial sums are reduced in pair
+# order. (7089, 4096, 14336) splits the last 78 of 448 tiles; (520, 2560, 9216) splits every
+# tile over 2-3 pairs and (300, 1024, 8192) over about nine. The result must match fp32 and be
+# bit-identical from one call to the next.
+@pytest.mark.parametrize("m,n,k", [(7089, 4096, 14336), (520, 2560, 9216), (300, 1024, 8192)])
+def test_gemm_stream_k(cuda, m, n, k):
+    g = torch.Generator(device=cuda).manual_seed(m + k)
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = torch.randn(n, k, device=cuda, generator=g).bfloat16()
+    y1 = ops.linear(x, w)
+    y2 = ops.linear(x, w)
+    assert torch.equal(y1, y2)
+    assert rel_err(y1, x.float() @ w.float().T) < 1e-2
+
+
+def test_gemm_stream_k_epilogues(cuda):
+    g = torch.Generator(device=cuda).manual_seed(9)
+    m, k = 300, 8192
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = torch.randn(4096, k, device=cuda, generator=g).bfloat16()
+    r = torch.randn(m, 4096, device=cuda, generator=g).bfloat16()
+    want = r.float() + x.float() @ w.float().T
+    ops.linear(x, w, residual=r)
+    assert rel_err(r, want) < 1e-2
+    wg, wu = w[:2048], w[2048:]
+    y = ops.linear_swiglu(x, ops.interleave_gate_up(wg, wu))
+    assert rel_err(y, F.silu(x.float() @ wg.float().T) * (x.float() @ wu.float().T)) < 1e-2
+    x8 = torch.randn(m, 2 * k, device=cuda, generator=g).bfloat16()
+    w8 = (torch.randn(4096, 2 * k, device=cuda, generator=g) * 0.05).bfloat16()
+    xq, xs = ops.quantize_e4m3(x8)
+    wq, ws = ops.quantize_e4m3(w8)
+    y8 = ops.linear_e4m3(xq, xs, wq, ws)
+    want8 = (xq.float() * xs.view(-1, 1)) @ (wq.float() * ws.view(-1, 1)).T
+    assert rel_err(y8, want8) < 1e-2
 
 
 def test_rms_norm_modes(cuda):
@@ -121,10 +179,12 @@ def test_rope(cuda, rot):
 
 @pytest.mark.parametrize("d,heads,kv", [(128, 4, 2), (64, 9, 3)])
 @pytest.mark.parametrize("fp8", [False, True])
-def test_gemm_rope_epilogue(cuda, d, heads, kv, fp8):
-    """q/k/v projection with RoPE on the q and k heads in the GEMM epilogue."""
+@pytest.mark.parametrize("k", [256, 8192])
+def test_gemm_rope_epilogue(cuda, d, heads, kv, fp8, k):
+    """q/k/v projection with RoPE on the q and k heads in the GEMM epilogue (k = 8192 in bf16
+    takes the stream-K path with each tile split over about nine CTA pairs)."""
     g = torch.Generator(device=cuda).manual_seed(8)
-    m, k = 300, 256
+    m = 300
     n = (heads + 2 * kv) * d
     x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
     w = (torch.randn(n, k, device=cuda, generator=g) * 0.1).bfloat16()
