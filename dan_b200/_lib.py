@@ -22,6 +22,7 @@ SIGNATURES = {
     "dan_last_error": ([], ctypes.c_char_p),
     "dan_read_status": ([P, P, P], I32),
     "dan_gemm_bf16": ([P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
+    "dan_gemm_bf16_noalloc": ([P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
     "dan_gemm_e4m3": ([P, I64, P, P, I64, P, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
     "dan_gemm_bf16_rope": ([P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, I32, I32, P, P, P, P], I32),
     "dan_gemm_e4m3_rope": ([P, I64, P, P, I64, P, P, I64, P, I64, P, I32, I32, I32, I32, I32, I32, P, P, P, P],

@@ -823,8 +823,42 @@ static Workspace* workspace(cudaStream_t stream, int pairs) {
   return &(all[{dev, stream}] = w);
 }
 
+// Allocation-free stream-K scratch for dan_gemm_bf16_noalloc: one static device array per
+// device (zero at module load), laid out like a Workspace for up to kStaticPairs CTA pairs.
+constexpr int kStaticPairs = 80;
+constexpr size_t kStaticPartBytes = static_cast<size_t>(kStaticPairs) * 2 * BN * 128 * sizeof(float);
+constexpr size_t kStaticFlagWords = static_cast<size_t>(kStaticPairs) * 2 * 4 + 2;
+static __device__ __align__(256) unsigned char g_sk_scratch[kStaticPartBytes + kStaticFlagWords * sizeof(uint32_t)];
+
+// The static scratch of the current device as a Workspace (its address looked up once per
+// device with cudaGetSymbolAddress); nullptr with the error text set if it is unavailable.
+static const Workspace* static_workspace() {
+  static std::mutex mu;
+  static std::map<int, Workspace> all;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    set_error("cudaGetDevice failed");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = all.find(dev);
+  if (it != all.end()) return &it->second;
+  void* base = nullptr;
+  if (cudaGetSymbolAddress(&base, g_sk_scratch) != cudaSuccess) {
+    set_error("cudaGetSymbolAddress of the static stream-K scratch failed");
+    return nullptr;
+  }
+  Workspace w{};
+  w.part = static_cast<float*>(base);
+  w.flag = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(base) + kStaticPartBytes);
+  w.ctrl = w.flag + static_cast<size_t>(kStaticPairs) * 2 * 4;
+  return &(all[dev] = w);
+}
+
+// ``fixed``: use this stream-K workspace (sized for kStaticPairs) instead of allocating one.
 template <bool FP8>
-int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cudaStream_t stream) {
+int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cudaStream_t stream,
+           const Workspace* fixed = nullptr) {
   const int esize = FP8 ? 1 : 2;
   DAN_REQUIRE(p.m > 0 && p.n > 0 && p.k > 0, "gemm: empty problem m=%d n=%d k=%d", p.m, p.n, p.k);
   DAN_REQUIRE((p.k * esize) % 16 == 0, "gemm: k=%d must make 16-byte rows", p.k);
@@ -912,7 +946,11 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
       const int first = tiles <= max_pairs ? 0 : (tiles / max_pairs - 1) * max_pairs;
       const int64_t iters = static_cast<int64_t>(tiles - first) * k_iters;
       if (ragged && k_iters >= 128 && iters >= 8LL * max_pairs) {
-        Workspace* ws = workspace(stream, max_pairs);
+        const Workspace* ws = fixed;
+        if (ws && max_pairs > kStaticPairs)
+          return fail(-22, "gemm: %d CTA pairs exceed the static stream-K scratch (%d pairs)", max_pairs,
+                      kStaticPairs);
+        if (!ws) ws = workspace(stream, max_pairs);
         if (!ws) return fail(2, "gemm: %s", last_error());
         p.sk_first = first;
         p.sk_iters = static_cast<int>(iters);
@@ -997,6 +1035,25 @@ DAN_API int dan_gemm_bf16_rope(const void* a, int64_t lda, const void* w, int64_
   p.epilogue = epilogue;
   p.status = status;
   return gemm::launch<false>(a, lda, w, ldw, p, static_cast<cudaStream_t>(stream));
+}
+
+DAN_API int dan_gemm_bf16_noalloc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
+                                  const void* resid, int64_t ldr, const void* bias, int m, int n, int k,
+                                  int epilogue, int32_t* status, void* stream) {
+  const gemm::Workspace* ws = gemm::static_workspace();
+  if (!ws) return fail(2, "gemm: %s", last_error());
+  gemm::Params p{};
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  p.resid = static_cast<const __nv_bfloat16*>(resid);
+  p.ldr = ldr;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.epilogue = epilogue;
+  p.status = status;
+  return gemm::launch<false>(a, lda, w, ldw, p, static_cast<cudaStream_t>(stream), ws);
 }
 
 DAN_API int dan_gemm_e4m3(const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,

@@ -8,7 +8,8 @@
  *     (a bounded wait that ran out, an out-of-range index) instead of hanging or
  *     faulting; read it with dan_read_status once per batch;
  *   - the return value is 0, or a negative code with the text in dan_last_error();
- *   - nothing allocates or frees device memory: callers own every buffer.
+ *   - callers own every buffer; the only allocation is the stream-K workspace of the GEMMs
+ *     (dan_gemm_bf16 below), and dan_gemm_bf16_noalloc is the same GEMM without it.
  *
  * Each function names the reference (quangliz/dan) interface it replaces.
  */
@@ -57,6 +58,16 @@ int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, const void*
  * calls sharing a stream use it in stream order. */
 int dan_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, const void* resid,
                   int64_t ldr, const void* bias, int m, int n, int k, int epilogue, int32_t* status, void* stream);
+
+/* dan_gemm_bf16 without any allocation: the stream-K partials live in a static device array of
+ * the library (sized for up to 80 CTA pairs, i.e. 160 SMs; its address is looked up once per
+ * device), so the call never allocates and can be captured in a CUDA graph from its first use.
+ * Returns -22 (and allocates nothing) on a device with more SMs than the array covers. Calls on
+ * one device share the array and must be stream-ordered with each other. Same arguments and
+ * results as dan_gemm_bf16 (dan/models/llama.py:78,87,102). */
+int dan_gemm_bf16_noalloc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
+                          const void* resid, int64_t ldr, const void* bias, int m, int n, int k, int epilogue,
+                          int32_t* status, void* stream);
 
 /* e4m3 x e4m3 GEMM with per-row (token) and per-column (output channel) fp32 scales, bf16 out.
  * Replaces FP8Linear.forward (dan/quant.py:37-42, torch._scaled_mm row-wise); epilogues as above. */
