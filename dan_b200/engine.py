@@ -7,13 +7,19 @@ thread (``runner.read_many``; ctypes launches release the GIL) and resolves its
 requests' futures; a failing batch fails only its own requests; the queue is
 capped (``Overloaded``).
 
-Difference: ``runner`` may be a list of runners, one per GPU. Each replica has
-its own worker pulling whole batches from the shared queue, so a batch goes to
-whichever replica is free (least loaded). Replicas share nothing on the data
-path (no collective). ``stats`` aggregates; ``replica_stats`` is per replica.
+Difference: ``runner`` may be a list of runners, one per GPU, each with its own
+prefix pool and its own queue. A plan whose static prefix was routed before goes
+to the same replica (prefix affinity: its cached K/V or recurrent state lives
+there); any other plan goes to the least-loaded replica (queued tokens, plus a
+batch for a busy one), which becomes that prefix's home. A replica with nothing
+queued takes work from another replica's queue only when that queue holds more
+than a batch or its oldest plan has waited ``steal_after_ms`` behind a busy
+replica. Replicas share nothing on the data path (no collective). ``stats``
+aggregates; ``replica_stats`` is per replica.
 """
 import asyncio
 import time
+from collections import OrderedDict, deque
 from dataclasses import dataclass, field
 
 from .readout import answers, combine
@@ -31,18 +37,29 @@ class Stats:
     busy_s: float = 0.0
     latency_s: float = 0.0
     errors: int = 0
+    plans: int = 0
+    stolen: int = 0
     started: float = field(default_factory=time.time)
 
 
 class AsyncEngine:
-    def __init__(self, planner, runner, max_batch_tokens=8192, max_wait_ms=2.0, max_queue=1024):
+    def __init__(self, planner, runner, max_batch_tokens=8192, max_wait_ms=2.0, max_queue=1024,
+                 steal_after_ms=20.0, max_homes=65536):
         self.planner = planner
         self.runners = list(runner) if isinstance(runner, (list, tuple)) else [runner]
         self.runner = self.runners[0]  # dan's /metrics reads engine.runner.cache
         self.max_batch_tokens = max_batch_tokens
         self.max_wait = max_wait_ms / 1000
         self.max_queue = max_queue
-        self.queue = asyncio.Queue()
+        self.steal_after = steal_after_ms / 1000
+        self.max_homes = max_homes
+        n = len(self.runners)
+        self._queues = [deque() for _ in range(n)]  # (plan, future, enqueue time, cost)
+        self._queued = [0] * n  # tokens waiting per replica
+        self._busy = [False] * n
+        self._homes = OrderedDict()  # static-prefix key -> replica
+        self._arrived = asyncio.Event()
+        self.affinity_hits = 0
         self.stats = Stats()
         self.replica_stats = [Stats() for _ in self.runners]
         self._workers = []
@@ -62,18 +79,24 @@ class AsyncEngine:
                 pass
         self._workers = []
 
+    def queued(self):
+        return sum(len(q) for q in self._queues)
+
     async def decide(self, state, questions, profile=None):
         """Answers keyed by question id, and the input tokens the reads took (engine.py:55-72)."""
         plans = self.planner.plans(state, questions, profile)
         if not plans[0].branches:
             return answers(plans[0], []), 0
-        if self.queue.qsize() + len(plans) > self.max_queue:
+        if self.queued() + len(plans) > self.max_queue:
             raise Overloaded("dan is at capacity. Retry shortly.")
         self.start()
         loop, t0 = asyncio.get_running_loop(), time.perf_counter()
         futs = [loop.create_future() for _ in plans]
         for plan, fut in zip(plans, futs):
-            await self.queue.put((plan, fut, t0))
+            r, cost = self.route(plan), self.cost(plan)
+            self._queues[r].append((plan, fut, time.perf_counter(), cost))
+            self._queued[r] += cost
+        self._arrived.set()
         reads = await asyncio.gather(*futs)
         self.stats.requests += 1
         self.stats.latency_s += time.perf_counter() - t0
@@ -84,27 +107,81 @@ class AsyncEngine:
     def cost(plan):
         return len(plan.prefix) + sum(len(b.suffix) for b in plan.branches)
 
+    @staticmethod
+    def prefix_key(plan):
+        """The prefix pool's key for ``plan`` (its static prefix, runner.py:56), or None."""
+        return hash(tuple(plan.prefix[:plan.static])) if getattr(plan, "static", 0) else None
+
+    def route(self, plan):
+        """Replica for ``plan``: its static prefix's home, else the least-loaded replica."""
+        key = self.prefix_key(plan)
+        if key is not None and key in self._homes:
+            self._homes.move_to_end(key)
+            self.affinity_hits += 1
+            return self._homes[key]
+        load = [q + (self.max_batch_tokens if b else 0) for q, b in zip(self._queued, self._busy)]
+        r = min(range(len(load)), key=load.__getitem__)
+        if key is not None:
+            self._homes[key] = r
+            if len(self._homes) > self.max_homes:
+                self._homes.popitem(last=False)
+        return r
+
+    def _source(self, i):
+        """Queue replica ``i`` takes its next plan from: its own, else one it may steal from."""
+        if self._queues[i]:
+            return i
+        now, best = time.perf_counter(), None
+        for j, q in enumerate(self._queues):
+            if j == i or not q:
+                continue
+            if self._queued[j] > self.max_batch_tokens or (self._busy[j] and now - q[0][2] >= self.steal_after):
+                if best is None or self._queued[j] > self._queued[best]:
+                    best = j
+        return best
+
+    def _pop(self, i, src):
+        item = self._queues[src].popleft()
+        self._queued[src] -= item[3]
+        if src != i:
+            self.replica_stats[i].stolen += 1
+        return item
+
     async def _loop(self, replica):
         while True:
-            batch = [await self.queue.get()]
-            budget = self.cost(batch[0][0])
+            while True:
+                self._arrived.clear()
+                src = self._source(replica)
+                if src is not None:
+                    break
+                try:
+                    await asyncio.wait_for(self._arrived.wait(), timeout=self.steal_after)
+                except asyncio.TimeoutError:
+                    pass
+            batch = [self._pop(replica, src)]
+            budget = batch[0][3]
+            self._busy[replica] = True  # collecting a batch counts as load for routing and stealing
             deadline = time.perf_counter() + self.max_wait
             while budget < self.max_batch_tokens:
-                if self.queue.empty():
+                src = self._source(replica)
+                if src is None:
                     left = deadline - time.perf_counter()
                     if left <= 0:
                         break
                     await asyncio.sleep(min(left, 0.0005))
                     continue
-                plan = self.queue._queue[0][0]  # peek: stop before the budget is exceeded
-                if budget + self.cost(plan) > self.max_batch_tokens:
+                if budget + self._queues[src][0][3] > self.max_batch_tokens:  # stop before the budget
                     break
-                batch.append(self.queue.get_nowait())
-                budget += self.cost(plan)
-            await self._run(replica, batch, budget)
+                batch.append(self._pop(replica, src))
+                budget += batch[-1][3]
+            try:
+                await self._run(replica, batch, budget)
+            finally:
+                self._busy[replica] = False
+                self._arrived.set()  # a replica that just went idle may now be stolen from
 
     async def _run(self, replica, batch, tokens):
-        plans = [p for p, _, _ in batch]
+        plans = [item[0] for item in batch]
         st = self.replica_stats[replica]
         t = time.perf_counter()
         try:
@@ -112,18 +189,19 @@ class AsyncEngine:
         except Exception as e:  # noqa: BLE001 - fail this batch's requests, keep serving
             self.stats.errors += len(batch)
             st.errors += len(batch)
-            for _, fut, _ in batch:
-                if not fut.done():
-                    fut.set_exception(e)
+            for item in batch:
+                if not item[1].done():
+                    item[1].set_exception(e)
             return
         dt = time.perf_counter() - t
         for s in (self.stats, st):
             s.batches += 1
             s.tokens += tokens
             s.busy_s += dt
-        for (_, fut, _), lg in zip(batch, logits):
-            if not fut.done():
-                fut.set_result(lg)
+            s.plans += len(batch)
+        for item, lg in zip(batch, logits):
+            if not item[1].done():
+                item[1].set_result(lg)
 
     def metrics(self):
         """Prometheus-style rows (dan/entrypoints/api_server.py:137-147) plus one set per replica."""
@@ -131,10 +209,14 @@ class AsyncEngine:
         rows = [("dan_requests_total", s.requests), ("dan_request_errors_total", s.errors),
                 ("dan_batches_total", s.batches), ("dan_prompt_tokens_total", s.tokens),
                 ("dan_busy_seconds_total", round(s.busy_s, 6)),
-                ("dan_request_latency_seconds_sum", round(s.latency_s, 6)), ("dan_queue_size", self.queue.qsize())]
+                ("dan_request_latency_seconds_sum", round(s.latency_s, 6)), ("dan_queue_size", self.queued()),
+                ("dan_route_affinity_total", self.affinity_hits)]
         for i, (r, rs) in enumerate(zip(self.runners, self.replica_stats)):
             rows += [(f'dan_replica_batches_total{{replica="{i}"}}', rs.batches),
-                     (f'dan_replica_busy_seconds_total{{replica="{i}"}}', round(rs.busy_s, 6))]
+                     (f'dan_replica_busy_seconds_total{{replica="{i}"}}', round(rs.busy_s, 6)),
+                     (f'dan_replica_plans_total{{replica="{i}"}}', rs.plans),
+                     (f'dan_replica_stolen_total{{replica="{i}"}}', rs.stolen),
+                     (f'dan_replica_queued_tokens{{replica="{i}"}}', self._queued[i])]
             cache = getattr(r, "cache", None)
             if cache is not None:
                 rows += [(f'dan_prefix_cache_hits_total{{replica="{i}"}}', cache.hits),

@@ -146,3 +146,64 @@ def test_readout_matches_reference_golden():
         comb = readout.combine([plan, plan], [case["logits"], case["logits"]])
         for c, w in zip(comb, case["combine"]):
             assert torch.allclose(c, torch.tensor(w), atol=1e-6)
+
+
+class PrefixPlanner(FakePlanner):
+    """Plans whose prompt (the text before '|') is a cacheable static prefix."""
+
+    def plans(self, state, questions, profile=None):
+        plans = super().plans(state.split("|")[0], questions, profile)
+        for p in plans:
+            p.static = len(p.prefix)
+        return plans
+
+
+class RecordingRunner(FakeRunner):
+    def __init__(self, delay=0.0):
+        super().__init__(delay=delay)
+        self.prefixes = []
+
+    def read_many(self, plans):
+        with self.lock:
+            self.prefixes += [tuple(p.prefix) for p in plans]
+        return super().read_many(plans)
+
+
+def test_prefix_affinity_keeps_each_prefix_on_one_replica():
+    """Plans sharing a static prefix go to the replica whose pool holds it (the prefix's home);
+    new prefixes go to the least-loaded replica, so two prefixes land on different replicas."""
+    runners = [RecordingRunner(delay=0.005), RecordingRunner(delay=0.005)]
+    eng = AsyncEngine(PrefixPlanner(), runners, max_batch_tokens=10_000, max_wait_ms=1, steal_after_ms=10_000)
+
+    async def main():
+        for wave in range(4):
+            await asyncio.gather(*[eng.decide(f"{tag} shared prompt|{wave}{i}", QUESTIONS)
+                                   for tag in ("alpha", "beta") for i in range(3)])
+        await eng.stop()
+
+    run(main())
+    homes = {}
+    for i, r in enumerate(runners):
+        for pre in r.prefixes:
+            homes.setdefault(pre, set()).add(i)
+    assert len(homes) == 2 and all(len(v) == 1 for v in homes.values())
+    assert set().union(*homes.values()) == {0, 1}
+    assert eng.affinity_hits == 4 * 6 - 2  # every plan but the first of each prefix
+    assert "dan_route_affinity_total 22" in eng.metrics()
+
+
+def test_idle_replica_steals_a_backlog_from_a_busy_one():
+    """All plans share one prefix (home: replica 0, which is slow); once its queue holds more
+    than a batch, the idle replica takes work from it, and every request is answered."""
+    runners = [RecordingRunner(delay=0.05), RecordingRunner(delay=0.0)]
+    eng = AsyncEngine(PrefixPlanner(), runners, max_batch_tokens=60, max_wait_ms=1, steal_after_ms=5)
+
+    async def main():
+        res = await asyncio.gather(*[eng.decide(f"same prefix|{i}", QUESTIONS) for i in range(12)])
+        await eng.stop()
+        return res
+
+    res = run(main())
+    assert len(res) == 12 and all(isinstance(r, tuple) for r in res)
+    assert runners[1].calls > 0 and eng.replica_stats[1].stolen > 0
+    assert sum(rs.plans for rs in eng.replica_stats) == 12
