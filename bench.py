@@ -239,13 +239,18 @@ def run_dan(args, world, rank, local):
     timed = prepared[args.warmup:]
     tokens = sum(b["tokens"] for b in timed)
     questions = sum(b["questions"] for b in timed)
+    # requests and prompt tokens as dan's usage counts them (cached prefix tokens included,
+    # engine.py:74-76), over the same timed batches
+    requests = sum(len(p) for p in batches[args.warmup:])
+    prompt_tokens = sum(len(pl.prefix) + sum(len(br.suffix) for br in pl.branches)
+                        for p in batches[args.warmup:] for pl in p)
     pairs = sum(b["segs"].layout.pairs for b in timed)
 
     hbm, pk_burst, pk_sust, pk_kind = peaks()
     launches0 = profiling.total_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     timer = profiling.KernelTimer({"dan_gemm_bf16", "dan_gemm_bf16_rope", "dan_gemm_e4m3", "dan_gemm_e4m3_rope",
-                                   "dan_tree_attention"})
+                                   "dan_tree_attention", "dan_gated_delta_scan"})
     with Clocks(local) as clocks:
         barrier(world, device)
         torch.cuda.synchronize()
@@ -263,6 +268,8 @@ def run_dan(args, world, rank, local):
     ms_max = reduce(ms, "max", world, device)
     tok_all = reduce(tokens, "sum", world, device)
     q_all = reduce(questions, "sum", world, device)
+    req_all = reduce(requests, "sum", world, device)
+    prompt_all = reduce(prompt_tokens, "sum", world, device)
 
     # end to end through the public API: host plans -> read_many -> host logits
     h2d = d2h = 0
@@ -315,6 +322,8 @@ def run_dan(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "e4m3" if cid == 5 else "bf16", "data": "synthetic",
         "answers_per_s": q_all / (ms_max * 1e-3),
+        "requests_per_s": req_all / (ms_max * 1e-3),
+        "prompt_tokens_per_s": prompt_all / (ms_max * 1e-3),
         "config": {"workload": WORKLOADS[cid], "model": "qwen3.5-4b-style (random init)" if cid == 4 else
                    "llama-3-8b (random init)", "global_batch": int(tok_all / args.steps),
                    "seq_len": 8192, "parallelism": f"replicas x{world}",
@@ -333,10 +342,21 @@ def run_dan(args, world, rank, local):
                 "d2h_bytes_per_step": d2h // args.steps},
         "gpu_launches": launches,
         "kernels": {k: {"launches": v["launches"], "ms_per_step": v["ms_total"] / args.steps,
-                        "tflops": v["work_total"] / max(v["ms_total"], 1e-9) / 1e9}
+                        ("gbs" if k == "dan_gated_delta_scan" else "tflops"):
+                            v["work_total"] / max(v["ms_total"], 1e-9) / (1e6 if k == "dan_gated_delta_scan" else 1e9)}
                     for k, v in kern.items() if v["launches"]},
         "clocks": clocks.summary(),
     }
+    sc = kern.get("dan_gated_delta_scan")
+    if sc and sc["ms_total"]:  # configuration 4: the recurrent scan, HBM-bound by definition
+        n_lin = sum(1 for t in cfg.get("layer_types", []) if t == "linear_attention")
+        flops = tokens * n_lin * 4 * cfg["linear_num_value_heads"] * cfg["linear_key_head_dim"] * \
+            cfg["linear_value_head_dim"]
+        gbs = sc["work_total"] / (sc["ms_total"] * 1e-3) / 1e9
+        line["roofline_scan"] = {"bound": "hbm", "kernel": "dan_gated_delta_scan", "achieved": gbs, "peak": hbm,
+                                 "unit": "GB/s", "frac": gbs / hbm if hbm else None, "peak_kind": "measured",
+                                 "tflops": flops / (sc["ms_total"] * 1e-3) / 1e12,
+                                 "share_of_step": sc["ms_total"] / ms}
     if world == 1 and not args.no_cpu and cid == 3:
         dt, ctok, cq, threads = cpu_sample()
         v = ctok / (dt * 32 / SAMPLE_LAYERS)

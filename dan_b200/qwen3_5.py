@@ -53,6 +53,7 @@ class RecurrentLayout:
     tail_dst: list  # (slot) per save
     n_segs: int
     n_rows: int
+    n_state_io: int = 0  # fp32 states the scan reads (cached pasts) plus writes (save cuts)
 
     @classmethod
     def build(cls, segments, n_rows, k1, device):
@@ -84,8 +85,9 @@ class RecurrentLayout:
             t = torch.from_numpy(np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(shape)))
             return t.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else t
 
+        io = sum((r[3] >= 0) + (r[4] >= 0) for r in segs)
         return cls(up(prev[:max(n_rows, 1)], (-1, k1)), up(segs, (-1, 8)), up(brs or [(0, 0)], (-1, 2)),
-                   up(tail or [0], (-1,)), tail_dst, len(segs), n_rows)
+                   up(tail or [0], (-1,)), tail_dst, len(segs), n_rows, int(io))
 
 
 class Qwen35ForReads:
@@ -214,7 +216,8 @@ class Qwen35ForReads:
                   C, _lib.ptr(b), _lib.ptr(a), P.stride(0), _lib.ptr(L["a_log"]), _lib.ptr(L["dt_bias"]),
                   _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), _lib.ptr(state),
                   state.stride(0) if state is not None else 0, _lib.ptr(out), vd, self.hk, hv, self.dk, self.dv,
-                  float(self.dk ** -0.5), _lib.stream())
+                  float(self.dk ** -0.5), _lib.stream(),
+                  work=n * (2 * kd + vd) * 2 + n * hv * 2 * 2 + n * vd * 2 + rl.n_state_io * hv * self.dk * self.dv * 4)
         y = torch.empty_like(out)
         _lib.call("dan_gated_rms_norm", _lib.ptr(out), vd, _lib.ptr(z), P.stride(0), _lib.ptr(L["gnorm"]),
                   float(self.eps), _lib.ptr(y), vd, n, hv, self.dv, _lib.stream())
