@@ -39,8 +39,9 @@ SIGNATURES = {
     "dan_label_readout": ([P, I64, P, P, F32, I32, P, I64, I64, P, P, I32, I32, I32, P, P, P, P], I32),
     "dan_causal_conv": ([P, I64, P, I64, P, P, P, I64, I32, I32, P], I32),
     "dan_gather_rows": ([P, I64, P, I64, P, I32, P, I64, I32, P], I32),
-    "dan_gated_delta_scan": ([P, P, P, I64, P, P, I64, P, P, P, I32, P, P, I64, P, I64, I32, I32, I32, I32, F32, P],
-                             I32),
+    "dan_gated_delta_scan": ([P, P, P, I64, P, P, I64, P, P, P, I32, P, P, I32, P, I64, P, I64, I32, I32, I32, I32,
+                              F32, P, I64, P, P], I32),
+    "dan_gated_delta_scratch_bytes": ([I32, I32, I32], I64),
     "dan_gated_rms_norm": ([P, I64, P, I64, P, F32, P, I64, I32, I32, I32, P], I32),
 }
 
@@ -86,6 +87,12 @@ def call(name, *args, work=0, key=None):
     if rc != 0:
         raise RuntimeError(f"{name}: {lib().dan_last_error().decode()} (code {rc})")
     profiling.launches[name] += 1
+
+
+def delta_scratch(n_chunks, hk, hv, device):
+    """Scratch tensor for dan_gated_delta_scan (reused across the layers of one forward)."""
+    return torch.empty(max(int(lib().dan_gated_delta_scratch_bytes(n_chunks, hk, hv)), 16), dtype=torch.uint8,
+                       device=device)
 
 
 def ptr(t):

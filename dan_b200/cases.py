@@ -99,17 +99,19 @@ def deltanet(iters):
     conv = torch.empty(n, C, dtype=torch.bfloat16, device=dev)
     out = torch.empty(n, hv * dv, dtype=torch.bfloat16, device=dev)
     kd = hk * dk
+    scratch = _lib.delta_scratch(rl.n_chunks, hk, hv, dev)
 
     def run():
         _lib.call("dan_causal_conv", _lib.ptr(pre), C, None, 0, _lib.ptr(w), _lib.ptr(rl.prev), _lib.ptr(conv), C, n,
                   C, _lib.stream())
         _lib.call("dan_gated_delta_scan", _lib.ptr(conv[:, :kd]), _lib.ptr(conv[:, kd:2 * kd]),
                   _lib.ptr(conv[:, 2 * kd:]), C, _lib.ptr(ba[:, :hv]), _lib.ptr(ba[:, hv:]), 2 * hv,
-                  _lib.ptr(a_log), _lib.ptr(dt), _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), None, 0,
-                  _lib.ptr(out), hv * dv, hk, hv, dk, dv, float(dk ** -0.5), _lib.stream())
+                  _lib.ptr(a_log), _lib.ptr(dt), _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches),
+                  _lib.ptr(rl.chunks), rl.n_chunks, None, 0, _lib.ptr(out), hv * dv, hk, hv, dk, dv,
+                  float(dk ** -0.5), _lib.ptr(scratch), scratch.numel(), _lib.ptr(_lib.status_word(dev)), _lib.stream())
 
     ms = _time(run, iters)
-    return {"tokens": n, "segments": rl.n_segs, "ms": ms}
+    return {"tokens": n, "segments": rl.n_segs, "chunks": rl.n_chunks, "ms": ms}
 
 
 def fp8peak(iters):

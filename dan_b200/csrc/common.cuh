@@ -249,6 +249,15 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t v) {
   return true;
 }
 
+// 1-D bulk copy global -> shared (no tensor map, no multicast): ``bytes`` (a multiple of 16,
+// both addresses 16-byte aligned), completing on ``bar`` as transaction bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // TMA tiled store from shared memory (bulk-group completion) and its group bookkeeping.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(

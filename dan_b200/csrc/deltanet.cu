@@ -23,7 +23,7 @@
 namespace dan {
 namespace delta {
 
-__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // Row code for the conv source: >= 0 packed row of ``src``; -1 a zero row; <= -2 row
@@ -36,33 +36,71 @@ __device__ __forceinline__ const __nv_bfloat16* code_row(int code, const __nv_bf
 }
 
 // y[r, c] = silu(sum_j w[c, j] * ext_j) over ext = [prev3, prev2, prev1, row r] (qwen3_5.py:218-220).
-__global__ void causal_conv_kernel(const __nv_bfloat16* src, int64_t ld_src, const __nv_bfloat16* hist,
-                                   int64_t ld_hist, const __nv_bfloat16* w, const int* prev, __nv_bfloat16* out,
-                                   int64_t ld_out, int rows, int channels) {
-  const int r = blockIdx.x;
-  const int* pr = prev + 3 * r;
-  const __nv_bfloat16* rows4[4] = {code_row(pr[2], src, ld_src, hist, ld_hist),
-                                   code_row(pr[1], src, ld_src, hist, ld_hist),
-                                   code_row(pr[0], src, ld_src, hist, ld_hist), src + static_cast<int64_t>(r) * ld_src};
-  for (int c0 = threadIdx.x * 8; c0 < channels; c0 += blockDim.x * 8) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    // weights [C, 4]: 8 channels x 4 taps = 32 bf16 = 4 x 16 B
+// A block covers CONV_ROWS consecutive rows and 2048 channels (8 per thread, weights in
+// registers) and loads all its rows up front; a source that is the previous packed row (every
+// trunk row's) comes from those registers, only branch starts and history rows are gathered.
+constexpr int CONV_ROWS = 16;
+__global__ void __launch_bounds__(256) causal_conv_kernel(const __nv_bfloat16* src, int64_t ld_src,
+                                                          const __nv_bfloat16* hist, int64_t ld_hist,
+                                                          const __nv_bfloat16* w, const int* prev,
+                                                          __nv_bfloat16* out, int64_t ld_out, int rows, int channels) {
+  const int c0 = min((blockIdx.y * blockDim.x + threadIdx.x) * 8, channels - 8);  // tail threads redo the last 8
+  float wf[8][4];  // weights [C, 4]: 8 channels x 4 taps
+  {
     uint4 wv[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) wv[i] = reinterpret_cast<const uint4*>(w + static_cast<int64_t>(c0) * 4)[i];
+    for (int i = 0; i < 4; ++i) wv[i] = __ldg(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(c0) * 4) + i);
     const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(wv);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (!rows4[j]) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(rows4[j] + c0);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+    for (int t = 0; t < 8; ++t)
 #pragma unroll
-      for (int t = 0; t < 8; ++t) acc[t] += __bfloat162float(we[t * 4 + j]) * __bfloat162float(e[t]);
+      for (int j = 0; j < 4; ++j) wf[t][j] = __bfloat162float(we[t * 4 + j]);
+  }
+  const int r0 = blockIdx.x * CONV_ROWS;
+  const int nr = min(CONV_ROWS, rows - r0);
+  __shared__ int codes[CONV_ROWS * 3];
+  if (threadIdx.x < nr * 3) codes[threadIdx.x] = prev[3 * r0 + threadIdx.x];
+  uint4 cur[CONV_ROWS];  // every row's load issued before any is used
+#pragma unroll
+  for (int i = 0; i < CONV_ROWS; ++i)
+    cur[i] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(r0 + min(i, nr - 1)) * ld_src + c0));
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < CONV_ROWS; ++i) {
+    if (i >= nr) break;
+    const int r = r0 + i;
+    const int* pr = codes + 3 * i;
+    uint4 e[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int code = pr[j];
+      if (i > j && code == r - 1 - j) {  // the previous packed row: already in registers
+        e[j] = cur[i - 1 - j];
+      } else {
+        const __nv_bfloat16* row = code_row(code, src, ld_src, hist, ld_hist);
+        e[j] = row ? __ldg(reinterpret_cast<const uint4*>(row + c0)) : make_uint4(0, 0, 0, 0);
+      }
     }
+    const __nv_bfloat16* x0 = reinterpret_cast<const __nv_bfloat16*>(&e[2]);  // tap 0: third previous row
+    const __nv_bfloat16* x1 = reinterpret_cast<const __nv_bfloat16*>(&e[1]);
+    const __nv_bfloat16* x2 = reinterpret_cast<const __nv_bfloat16*>(&e[0]);
+    const __nv_bfloat16* x3 = reinterpret_cast<const __nv_bfloat16*>(&cur[i]);
     uint4 o;
     uint32_t* op = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) op[t] = pack_bf16(silu(acc[2 * t]), silu(acc[2 * t + 1]));
+    for (int t = 0; t < 4; ++t) {
+      float y[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int ch = 2 * t + u;
+        float acc = wf[ch][0] * __bfloat162float(x0[ch]);
+        acc += wf[ch][1] * __bfloat162float(x1[ch]);
+        acc += wf[ch][2] * __bfloat162float(x2[ch]);
+        acc += wf[ch][3] * __bfloat162float(x3[ch]);
+        y[u] = silu(acc);
+      }
+      op[t] = pack_bf16(y[0], y[1]);
+    }
     *reinterpret_cast<uint4*>(out + static_cast<int64_t>(r) * ld_out + c0) = o;
   }
 }
@@ -77,8 +115,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* src, int64_t ld_src, con
     *reinterpret_cast<uint4*>(d + c) = s ? *reinterpret_cast<const uint4*>(s + c) : make_uint4(0, 0, 0, 0);
 }
 
-// Segment record (int32 x 8): trunk_start, trunk_len, cut, init_slot, save_slot, branch0, n_branches, 0.
-// Branch record (int32 x 2): start, len.
+// Segment record (int32 x 8): trunk_start, trunk_len, cut, init_slot, save_slot, branch0, n_branches,
+// first chunk. Branch record (int32 x 4): start, len, first chunk, 0.
 struct Seg {
   int trunk_start, trunk_len, cut, init_slot, save_slot, branch0, n_branches, pad;
 };
@@ -101,43 +139,44 @@ struct ScanParams {
   int64_t ld_out;
   int hk, hv;
   float q_scale;
+  const int* chunks;  // [n_chunks, 2]: first row, rows
+  int n_chunks;
+  uint8_t* scratch;   // chunk records (REC_V per chunk and value head, REC_K per chunk and key head)
+  int32_t* status;
 };
 
 constexpr int DK = 128;
 
 // ---------------------------------------------------------------------------------
 // Chunked gated delta rule on the tensor cores (mma.sync m16n8k16, bf16 operands, fp32
-// accumulation). One CTA of 8 warps per (value head, segment) walks the segment's runs in
-// chunks of CH = 64 tokens. With Γ_t the cumulative log decay inside a chunk (γ_t = e^Γ_t),
-// the token recurrence S_t = d_t S_{t-1} + k_t u_t^T, u_t = β_t (v_t - k_t^T d_t S_{t-1}),
-// o_t = q_t^T S_t unrolls over a chunk that starts from state S0 to
+// accumulation). Runs are cut into chunks of CH = 64 tokens. With Γ_t the cumulative log
+// decay inside a chunk (γ_t = e^Γ_t), the token recurrence S_t = d_t S_{t-1} + k_t u_t^T,
+// u_t = β_t (v_t - k_t^T d_t S_{t-1}), o_t = q_t^T S_t unrolls over a chunk that starts from
+// state S0 to (the WY form; every decay factor is e^{difference} <= 1)
 //   A  = strictly_lower(β_t e^{Γ_t-Γ_s} k_t.k_s),  T = (I + A)^-1,  T' = T diag(β)
-//   U  = T' V - (T' diag(γ) K) S0                       (the chunk's u_t)
-//   O  = diag(γ) Q S0 + (e^{Γ_t-Γ_s} q_t.k_s, s <= t) U
+//   U  = T'V - W S0,  W = T' diag(γ) K
+//   O  = diag(γ) Q S0 + P U,  P = (e^{Γ_t-Γ_s} q_t.k_s for s <= t)
 //   S  = γ_C S0 + K^T diag(e^{Γ_C-Γ_t}) U
-// (the WY form of the delta rule; every decay factor is e^{difference} <= 1). The state
-// lives in registers in fp32 (warp w: rows [16w, 16w+16) of S, all 128 columns); a bf16
-// copy in shared memory is the operand of the S0 products. T is solved in fp32: 16x16
-// diagonal blocks by substitution, then two levels of block merges.
+// chunk_prep_kernel computes everything that does not depend on S0 for all chunks at once
+// (one CTA per chunk and value head): normalised q and k, gates, P, T (fp32, 16 x 16
+// diagonal blocks by substitution then two merge levels), -W and T'V, into a scratch
+// buffer. chunk_state_kernel then walks each segment's chunks in order (one CTA per value
+// head, 64-column half of the state and segment) doing only U, O and the state update, the
+// next chunk's inputs arriving by cp.async while this one is computed; the 128 x 64 fp32
+// state slice stays in registers for the whole segment.
 constexpr int CH = 64;
 constexpr int LDW = DK + 8;  // bf16 row stride of 128-wide tiles: 272 B, ldmatrix rows on distinct banks
 constexpr int LDN = CH + 8;  // bf16 row stride of 64-wide tiles
-constexpr int LDF = CH + 4;  // fp32 row stride of 64 x 64 tiles
+constexpr int LDF = CH + 1;  // fp32 row stride of 64 x 64 tiles
 
-struct ChunkSmem {
-  __nv_bfloat16 qn[CH * LDW];  // l2-normalised, scaled q
-  __nv_bfloat16 kn[CH * LDW];  // l2-normalised k
-  __nv_bfloat16 v[CH * LDW];
-  __nv_bfloat16 kg[CH * LDW];  // γ_t k_t, then -W
-  __nv_bfloat16 u[CH * LDW];   // U
-  __nv_bfloat16 us[CH * LDW];  // e^{Γ_C-Γ_t} U (fp32 scratch of the block merges before that)
-  __nv_bfloat16 s0[DK * LDW];  // chunk-start state, bf16
-  float a[CH * LDF];           // A
-  float tf[CH * LDF];          // T = (I + A)^-1
-  __nv_bfloat16 tb[CH * LDN];  // T diag(β)
-  __nv_bfloat16 pb[CH * LDN];  // e^{Γ_t-Γ_s} q_t.k_s (s <= t)
-  float gam[CH], eg[CH], beta[CH], graw[CH];
-};
+// Scratch records, rows padded exactly as in shared memory so a chunk loads with a few bulk
+// copies: per (chunk, value head) -W [64][LDW], T'V as two 64-column halves [64][LDN], P
+// [64][LDN] (bf16) and γ_t, e^{Γ_C-Γ_t}, e^{Γ_C} (fp32 x 64 each); per (chunk, key head) q̂ and
+// k̂ [64][LDW] bf16.
+constexpr int64_t TILE_W = CH * LDW * 2, TILE_N = CH * LDN * 2;  // 17408, 9216 B
+constexpr int64_t REC_W = 0, REC_UT = TILE_W, REC_P = REC_UT + 2 * TILE_N, REC_SC = REC_P + TILE_N;
+constexpr int64_t REC_V = REC_SC + 3 * CH * 4;  // 45824 B
+constexpr int64_t REC_K = 2 * TILE_W;           // 34816 B
 
 __device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -175,64 +214,100 @@ __device__ __forceinline__ void st_bf2(__nv_bfloat16* p, float x, float y) {
   *reinterpret_cast<uint32_t*>(p) = pack_bf16(x, y);
 }
 
-// One chunk of a run: rows [row0, row0 + nt) of the packed batch, state S in and out.
-__device__ __forceinline__ void scan_chunk(const ScanParams& p, ChunkSmem& sm, float (&S)[16][4], int h, int kh,
-                                           float a_neg, float dtb, int row0, int nt) {
+struct PrepSmem {
+  __nv_bfloat16 qn[CH * LDW];  // q̂, later -W
+  __nv_bfloat16 kn[CH * LDW];  // k̂
+  __nv_bfloat16 v[CH * LDW];   // v, later T'V
+  float a[CH * LDF];           // A
+  float tf[CH * LDF];          // T
+  __nv_bfloat16 tb[CH * LDN];  // T diag(β) (fp32 merge scratch before that)
+  __nv_bfloat16 tg[CH * LDN];  // T diag(βγ)
+  __nv_bfloat16 pb[CH * LDN];  // P
+  float gam[CH], eg[CH], beta[CH], graw[CH];
+};
+
+// Copy ``bytes`` of shared memory (a padded tile) to global memory, 16 bytes per thread step.
+__device__ __forceinline__ void copy_out(uint8_t* dst, const void* src, int bytes) {
+  for (int e = threadIdx.x; e < bytes / 16; e += blockDim.x)
+    reinterpret_cast<uint4*>(dst)[e] = reinterpret_cast<const uint4*>(src)[e];
+}
+
+__global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  PrepSmem& sm = *reinterpret_cast<PrepSmem*>(dsm);
+  const int ci = blockIdx.x, h = blockIdx.y;
+  const int row0 = p.chunks[2 * ci], nt = p.chunks[2 * ci + 1];
+  const int per = p.hv / p.hk, kh = h / per;
+  const bool owner = h % per == 0;  // writes this key head's q̂ and k̂
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  // ---- stage: q, k (l2-normalised), v, gates; S0 as bf16; T cleared
+  const float a_neg = -__expf(p.a_log[h]), dtb = p.dt_bias[h];
+  uint8_t* rv = p.scratch + (static_cast<int64_t>(ci) * p.hv + h) * REC_V;
+  uint8_t* rk = p.scratch + static_cast<int64_t>(p.n_chunks) * p.hv * REC_V + (static_cast<int64_t>(ci) * p.hk + kh) * REC_K;
+  // ---- stage: raw q, k, v rows by cp.async (16 B per thread step, all in flight), gates; T cleared
   {
-    if (lane < 8) {
-      const int t = warp * 8 + lane;
-      float bb = 0.f, gg = 0.f;
-      if (t < nt) {
-        const int64_t row = row0 + t;
-        bb = 1.f / (1.f + __expf(-__bfloat162float(p.b[row * p.ld_ba + h])));
-        gg = a_neg * softplus(__bfloat162float(p.a[row * p.ld_ba + h]) + dtb);
-      }
-      sm.beta[t] = bb;
-      sm.graw[t] = gg;
-    }
+    const __nv_bfloat16* srcs[3] = {p.q + kh * DK, p.k + kh * DK, p.v + h * DK};
+    __nv_bfloat16* dsts[3] = {sm.qn, sm.kn, sm.v};
+    const int c8 = (tid & 15) * 8;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint2 qw[4], kw[4], vw[4];
+    for (int w = 0; w < 3; ++w) {
+      const __nv_bfloat16* src = srcs[w] + static_cast<int64_t>(row0) * p.ld_qkv + c8;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {  // the four rows' loads issued before any is used
-        const int64_t row = row0 + min(warp * 8 + half * 4 + i, nt - 1);
-        qw[i] = __ldg(reinterpret_cast<const uint2*>(p.q + row * p.ld_qkv + kh * DK + lane * 4));
-        kw[i] = __ldg(reinterpret_cast<const uint2*>(p.k + row * p.ld_qkv + kh * DK + lane * 4));
-        vw[i] = __ldg(reinterpret_cast<const uint2*>(p.v + row * p.ld_qkv + h * DK + lane * 4));
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int t = warp * 8 + half * 4 + i;
-        const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qw[i]);
-        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kw[i]);
-        const float2 qa = __bfloat1622float2(q2[0]), qb = __bfloat1622float2(q2[1]);
-        const float2 ka = __bfloat1622float2(k2[0]), kb = __bfloat1622float2(k2[1]);
-        float sq = qa.x * qa.x + qa.y * qa.y + qb.x * qb.x + qb.y * qb.y;
-        float sk = ka.x * ka.x + ka.y * ka.y + kb.x * kb.x + kb.y * kb.y;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          sq += __shfl_xor_sync(0xffffffffu, sq, o);
-          sk += __shfl_xor_sync(0xffffffffu, sk, o);
-        }
-        const bool live = t < nt;
-        const float nq = live ? rsqrtf(sq + 1e-6f) * p.q_scale : 0.f, nk = live ? rsqrtf(sk + 1e-6f) : 0.f;
-        *reinterpret_cast<uint2*>(&sm.qn[t * LDW + lane * 4]) =
-            make_uint2(pack_bf16(qa.x * nq, qa.y * nq), pack_bf16(qb.x * nq, qb.y * nq));
-        *reinterpret_cast<uint2*>(&sm.kn[t * LDW + lane * 4]) =
-            make_uint2(pack_bf16(ka.x * nk, ka.y * nk), pack_bf16(kb.x * nk, kb.y * nk));
-        *reinterpret_cast<uint2*>(&sm.v[t * LDW + lane * 4]) = live ? vw[i] : make_uint2(0u, 0u);
+      for (int t = tid >> 4; t < CH; t += 16) {  // 16 threads per row, 16 rows per pass
+        if (t < nt)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dsts[w] + t * LDW + c8)),
+                       "l"(src + static_cast<int64_t>(t) * p.ld_qkv)
+                       : "memory");
       }
     }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      st_bf2(&sm.s0[(16 * warp + g) * LDW + 8 * j + 2 * c], S[j][0], S[j][1]);
-      st_bf2(&sm.s0[(16 * warp + g + 8) * LDW + 8 * j + 2 * c], S[j][2], S[j][3]);
-    }
-    for (int i = tid; i < CH * LDF; i += blockDim.x) sm.tf[i] = 0.f;
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (lane < 8) {
+    const int t = warp * 8 + lane;
+    float bb = 0.f, gg = 0.f;
+    if (t < nt) {
+      const int64_t row = row0 + t;
+      bb = 1.f / (1.f + __expf(-__bfloat162float(p.b[row * p.ld_ba + h])));
+      gg = a_neg * softplus(__bfloat162float(p.a[row * p.ld_ba + h]) + dtb);
+    }
+    sm.beta[t] = bb;
+    sm.graw[t] = gg;
+  }
+  for (int e = tid; e < (CH - nt) * (DK / 8); e += blockDim.x) {  // rows past the chunk: zero
+    const int t = nt + e / (DK / 8), c8 = (e % (DK / 8)) * 8;
+    *reinterpret_cast<uint4*>(&sm.qn[t * LDW + c8]) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(&sm.kn[t * LDW + c8]) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(&sm.v[t * LDW + c8]) = make_uint4(0, 0, 0, 0);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {  // l2 norms in place (q also scaled), one row per step per warp
+    const int t = warp * 8 + i;
+    if (t >= nt) break;
+    uint2* qp = reinterpret_cast<uint2*>(&sm.qn[t * LDW + lane * 4]);
+    uint2* kp = reinterpret_cast<uint2*>(&sm.kn[t * LDW + lane * 4]);
+    const uint2 qw = *qp, kw = *kp;
+    const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qw);
+    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kw);
+    const float2 qa = __bfloat1622float2(q2[0]), qb = __bfloat1622float2(q2[1]);
+    const float2 ka = __bfloat1622float2(k2[0]), kb = __bfloat1622float2(k2[1]);
+    float sq = qa.x * qa.x + qa.y * qa.y + qb.x * qb.x + qb.y * qb.y;
+    float sk = ka.x * ka.x + ka.y * ka.y + kb.x * kb.x + kb.y * kb.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    }
+    const float nq = rsqrtf(sq + 1e-6f) * p.q_scale, nk = rsqrtf(sk + 1e-6f);
+    *qp = make_uint2(pack_bf16(qa.x * nq, qa.y * nq), pack_bf16(qb.x * nq, qb.y * nq));
+    *kp = make_uint2(pack_bf16(ka.x * nk, ka.y * nk), pack_bf16(kb.x * nk, kb.y * nk));
+  }
+  for (int i = tid; i < CH * LDF; i += blockDim.x) sm.tf[i] = 0.f;
+  __syncthreads();
+  if (owner) {
+    copy_out(rk, sm.qn, TILE_W);
+    copy_out(rk + TILE_W, sm.kn, TILE_W);
+  }
   if (warp == 0) {  // Γ: inclusive prefix sum of the log decays
     const float v0 = sm.graw[2 * lane], v1 = sm.graw[2 * lane + 1];
     float incl = v0 + v1;
@@ -241,25 +316,20 @@ __device__ __forceinline__ void scan_chunk(const ScanParams& p, ChunkSmem& sm, f
       const float y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    const float g0 = incl - v1, g1 = incl;
-    sm.gam[2 * lane] = g0;
-    sm.gam[2 * lane + 1] = g1;
-    sm.eg[2 * lane] = __expf(g0);
-    sm.eg[2 * lane + 1] = __expf(g1);
+    sm.gam[2 * lane] = incl - v1;
+    sm.gam[2 * lane + 1] = incl;
+    sm.eg[2 * lane] = __expf(incl - v1);
+    sm.eg[2 * lane + 1] = __expf(incl);
   }
   __syncthreads();
   const float gc = sm.gam[nt - 1];
-  for (int e = tid; e < CH * (DK / 8); e += blockDim.x) {  // kg = γ_t k_t, 8 elements at a time
-    const int t = e >> 4, col = (e & 15) * 8;
-    const float s = sm.eg[t];
-    uint4 w = *reinterpret_cast<const uint4*>(&sm.kn[t * LDW + col]);
-    __nv_bfloat162* w2 = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(w2[i]);
-      w2[i] = __floats2bfloat162_rn(f.x * s, f.y * s);
+  {  // scalars: γ_t, e^{Γ_C-Γ_t}, e^{Γ_C}
+    float* sc = reinterpret_cast<float*>(rv + REC_SC);
+    if (tid < CH) {
+      sc[tid] = sm.eg[tid];
+      sc[CH + tid] = __expf(gc - sm.gam[tid]);
+      sc[2 * CH + tid] = __expf(gc);
     }
-    *reinterpret_cast<uint4*>(&sm.kg[t * LDW + col]) = w;
   }
   // ---- K K^T -> A and Q K^T -> P (warp: rows [16 tm, +16), columns [32 sh, +32))
   {
@@ -300,6 +370,7 @@ __device__ __forceinline__ void scan_chunk(const ScanParams& p, ChunkSmem& sm, f
     }
   }
   __syncthreads();
+  copy_out(rv + REC_P, sm.pb, TILE_N);
   // ---- T = (I + A)^-1: diagonal 16 x 16 blocks by forward substitution (thread: one column)
   if (tid < 64) {
     const int d = tid >> 4, j = tid & 15;
@@ -308,13 +379,13 @@ __device__ __forceinline__ void scan_chunk(const ScanParams& p, ChunkSmem& sm, f
     for (int t = 0; t < 16; ++t) {
       float acc = (t == j) ? 1.f : 0.f;
 #pragma unroll
-      for (int s = 0; s < t; ++s) acc -= sm.a[(16 * d + t) * LDF + 16 * d + s] * x[s];
+      for (int s2 = 0; s2 < t; ++s2) acc -= sm.a[(16 * d + t) * LDF + 16 * d + s2] * x[s2];
       x[t] = acc;
       sm.tf[(16 * d + t) * LDF + 16 * d + j] = acc;
     }
   }
   __syncthreads();
-  float* ysc = reinterpret_cast<float*>(sm.us);  // 32 x 33 fp32 scratch
+  float* ysc = reinterpret_cast<float*>(sm.tb);  // 32 x 33 fp32 scratch
   {  // level 1: T[d+1][d] = -T[d+1][d+1] A[d+1][d] T[d][d] for d = 0, 2
     const int q = tid >> 7, r = (tid >> 3) & 15, cc = (tid & 7) * 2, d = 2 * q;
     float y0 = 0.f, y1 = 0.f;
@@ -359,150 +430,86 @@ __device__ __forceinline__ void scan_chunk(const ScanParams& p, ChunkSmem& sm, f
     for (int e = 0; e < 4; ++e) sm.tf[(32 + r) * LDF + cq + e] = x[e];
   }
   __syncthreads();
-  for (int e = tid; e < CH * CH / 2; e += blockDim.x) {  // T' = T diag(β), bf16
-    const int t = e >> 5, s = (e & 31) * 2;
-    st_bf2(&sm.tb[t * LDN + s], sm.tf[t * LDF + s] * sm.beta[s], sm.tf[t * LDF + s + 1] * sm.beta[s + 1]);
+  for (int e = tid; e < CH * CH / 2; e += blockDim.x) {  // T' = T diag(β) and T diag(βγ), bf16
+    const int t = e >> 5, s2 = (e & 31) * 2;
+    const float t0 = sm.tf[t * LDF + s2] * sm.beta[s2], t1 = sm.tf[t * LDF + s2 + 1] * sm.beta[s2 + 1];
+    st_bf2(&sm.tb[t * LDN + s2], t0, t1);
+    st_bf2(&sm.tg[t * LDN + s2], t0 * sm.eg[s2], t1 * sm.eg[s2 + 1]);
   }
   __syncthreads();
-  // ---- W = T' diag(γ) K  (warp: rows [16 tm, +16), columns [64 tn, +64))
+  // ---- T'V and W = T diag(βγ) K (warp: rows [16 tm, +16), columns [64 tn, +64))
   const int tm = warp & 3, tn = warp >> 2;
-  float acc[8][4];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  float au[8][4] = {}, aw[8][4] = {};
 #pragma unroll 1
   for (int kk = 0; kk < CH / 16; ++kk) {
-    uint32_t a[4];
-    ldsm4(a, a_rows(sm.tb, LDN, 16 * tm, 16 * kk, lane));
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b[4];
-      ldsm4t(b, b_krows(sm.kg, LDW, 16 * kk, 64 * tn + 16 * np, lane));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
-    }
-  }
-  __syncthreads();  // every warp is done reading kg: it now holds -W
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int t = 16 * tm + g, col = 64 * tn + 8 * j + 2 * c;
-    st_bf2(&sm.kg[t * LDW + col], -acc[j][0], -acc[j][1]);
-    st_bf2(&sm.kg[(t + 8) * LDW + col], -acc[j][2], -acc[j][3]);
-    acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  }
-  __syncthreads();
-  // ---- U = T' V - W S0
-#pragma unroll 1
-  for (int kk = 0; kk < CH / 16; ++kk) {
-    uint32_t a[4];
-    ldsm4(a, a_rows(sm.tb, LDN, 16 * tm, 16 * kk, lane));
+    uint32_t a1[4], a2[4];
+    ldsm4(a1, a_rows(sm.tb, LDN, 16 * tm, 16 * kk, lane));
+    ldsm4(a2, a_rows(sm.tg, LDN, 16 * tm, 16 * kk, lane));
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       uint32_t b[4];
       ldsm4t(b, b_krows(sm.v, LDW, 16 * kk, 64 * tn + 16 * np, lane));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
+      mma16816(au[2 * np], a1, b[0], b[1]);
+      mma16816(au[2 * np + 1], a1, b[2], b[3]);
+      ldsm4t(b, b_krows(sm.kn, LDW, 16 * kk, 64 * tn + 16 * np, lane));
+      mma16816(aw[2 * np], a2, b[0], b[1]);
+      mma16816(aw[2 * np + 1], a2, b[2], b[3]);
     }
   }
-#pragma unroll 1
-  for (int kk = 0; kk < DK / 16; ++kk) {
-    uint32_t a[4];
-    ldsm4(a, a_rows(sm.kg, LDW, 16 * tm, 16 * kk, lane));
+  __syncthreads();  // v and q̂ buffers are free: T'V -> v, -W -> qn
 #pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b[4];
-      ldsm4t(b, b_krows(sm.s0, LDW, 16 * kk, 64 * tn + 16 * np, lane));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
-    }
-  }
-  {
-    const int t = 16 * tm + g;
-    const float w0 = __expf(gc - sm.gam[t]), w1 = __expf(gc - sm.gam[t + 8]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int col = 64 * tn + 8 * j + 2 * c;
-      st_bf2(&sm.u[t * LDW + col], acc[j][0], acc[j][1]);
-      st_bf2(&sm.u[(t + 8) * LDW + col], acc[j][2], acc[j][3]);
-      st_bf2(&sm.us[t * LDW + col], acc[j][0] * w0, acc[j][1] * w0);
-      st_bf2(&sm.us[(t + 8) * LDW + col], acc[j][2] * w1, acc[j][3] * w1);
-      acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    }
+  for (int j = 0; j < 8; ++j) {
+    const int t = 16 * tm + g, col = 64 * tn + 8 * j + 2 * c;
+    st_bf2(&sm.v[t * LDW + col], au[j][0], au[j][1]);
+    st_bf2(&sm.v[(t + 8) * LDW + col], au[j][2], au[j][3]);
+    st_bf2(&sm.qn[t * LDW + col], -aw[j][0], -aw[j][1]);
+    st_bf2(&sm.qn[(t + 8) * LDW + col], -aw[j][2], -aw[j][3]);
   }
   __syncthreads();
-  // ---- O = diag(γ) Q S0 + P U -> out rows
-#pragma unroll 1
-  for (int kk = 0; kk < DK / 16; ++kk) {
-    uint32_t a[4];
-    ldsm4(a, a_rows(sm.qn, LDW, 16 * tm, 16 * kk, lane));
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b[4];
-      ldsm4t(b, b_krows(sm.s0, LDW, 16 * kk, 64 * tn + 16 * np, lane));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
-    }
+  copy_out(rv + REC_W, sm.qn, TILE_W);
+  for (int e = tid; e < CH * 16; e += blockDim.x) {  // T'V as two 64-column halves [64][LDN]
+    const int t = e >> 4, c8 = (e & 15) * 8, hf = c8 >> 6;
+    *reinterpret_cast<uint4*>(rv + REC_UT + hf * TILE_N + (t * LDN + (c8 & 63)) * 2) =
+        *reinterpret_cast<const uint4*>(&sm.v[t * LDW + c8]);
   }
-  {
-    const float e0 = sm.eg[16 * tm + g], e1 = sm.eg[16 * tm + g + 8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      acc[j][0] *= e0;
-      acc[j][1] *= e0;
-      acc[j][2] *= e1;
-      acc[j][3] *= e1;
-    }
-  }
-#pragma unroll 1
-  for (int kk = 0; kk < CH / 16; ++kk) {
-    uint32_t a[4];
-    ldsm4(a, a_rows(sm.pb, LDN, 16 * tm, 16 * kk, lane));
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b[4];
-      ldsm4t(b, b_krows(sm.u, LDW, 16 * kk, 64 * tn + 16 * np, lane));
-      mma16816(acc[2 * np], a, b[0], b[1]);
-      mma16816(acc[2 * np + 1], a, b[2], b[3]);
-    }
-  }
-  {
-    const int t = 16 * tm + g;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int col = h * DK + 64 * tn + 8 * j + 2 * c;
-      if (t < nt) st_bf2(p.out + static_cast<int64_t>(row0 + t) * p.ld_out + col, acc[j][0], acc[j][1]);
-      if (t + 8 < nt) st_bf2(p.out + static_cast<int64_t>(row0 + t + 8) * p.ld_out + col, acc[j][2], acc[j][3]);
-    }
-  }
-  // ---- S = γ_C S0 + K^T (e^{Γ_C - Γ_t} U)  (warp: rows [16 w, +16) of S)
-  {
-    const float ec = __expf(gc);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      S[j][0] *= ec;
-      S[j][1] *= ec;
-      S[j][2] *= ec;
-      S[j][3] *= ec;
-    }
-#pragma unroll 1
-    for (int kk = 0; kk < CH / 16; ++kk) {
-      uint32_t a[4];
-      ldsm4t(a, a_cols(sm.kn, LDW, 16 * warp, 16 * kk, lane));
-#pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        uint32_t b[4];
-        ldsm4t(b, b_krows(sm.us, LDW, 16 * kk, 16 * np, lane));
-        mma16816(S[2 * np], a, b[0], b[1]);
-        mma16816(S[2 * np + 1], a, b[2], b[3]);
-      }
-    }
-  }
-  __syncthreads();
 }
 
-__device__ __forceinline__ void state_io(float (&S)[16][4], float* st, bool load) {
+struct StateBuf {  // one chunk's inputs for one 64-column half of the state
+  __nv_bfloat16 w[CH * LDW];   // -W
+  __nv_bfloat16 qn[CH * LDW];  // q̂
+  __nv_bfloat16 kn[CH * LDW];  // k̂
+  __nv_bfloat16 ut[CH * LDN];  // T'V, this half's columns
+  __nv_bfloat16 p[CH * LDN];   // P
+  float eg[CH], ws[CH], ec[CH];
+};
+struct StateSmem {
+  StateBuf buf[2];
+  __nv_bfloat16 s0[DK * LDN];  // chunk-start state slice, bf16
+  __nv_bfloat16 u[CH * LDN];
+  __nv_bfloat16 us[CH * LDN];  // e^{Γ_C-Γ_t} U
+  uint64_t full[2];            // per buffer: the chunk's bulk copies landed
+};
+
+// One thread: the chunk's six bulk copies into ``b``, completing on ``bar``.
+__device__ __forceinline__ void load_chunk(const ScanParams& p, StateBuf& b, uint64_t* bar, int ci, int h, int kh,
+                                           int half) {
+  const uint8_t* rv = p.scratch + (static_cast<int64_t>(ci) * p.hv + h) * REC_V;
+  const uint8_t* rk =
+      p.scratch + static_cast<int64_t>(p.n_chunks) * p.hv * REC_V + (static_cast<int64_t>(ci) * p.hk + kh) * REC_K;
+  fence_proxy_async();  // this buffer's previous reads (generic proxy) before the async writes
+  mbar_expect_tx(bar, static_cast<uint32_t>(sizeof(StateBuf)));
+  bulk_load(b.w, rv + REC_W, TILE_W, bar);
+  bulk_load(b.qn, rk, TILE_W, bar);
+  bulk_load(b.kn, rk + TILE_W, TILE_W, bar);
+  bulk_load(b.ut, rv + REC_UT + half * TILE_N, TILE_N, bar);
+  bulk_load(b.p, rv + REC_P, TILE_N, bar);
+  bulk_load(b.eg, rv + REC_SC, 3 * CH * 4, bar);
+}
+
+__device__ __forceinline__ void state_io(float (&S)[8][4], float* st, bool load) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < 8; ++j) {
     float* r0 = st + (16 * warp + g) * DK + 8 * j + 2 * c;
     float* r1 = r0 + 8 * DK;
     if (load) {
@@ -515,50 +522,185 @@ __device__ __forceinline__ void state_io(float (&S)[16][4], float* st, bool load
   }
 }
 
-// One CTA: (value head blockIdx.x, segment blockIdx.y). Runs in order: trunk up to the save
-// cut, trunk after it, then each branch from the trunk's final state (kept in registers).
-__global__ void __launch_bounds__(256, 1) chunk_scan_kernel(ScanParams p) {
+// The state-dependent part of one chunk: U = T'V - W S0, O = diag(γ) Q S0 + P U (to ``out``),
+// S = γ_C S0 + K^T diag(e^{Γ_C-Γ_t}) U, for this CTA's 64 value columns.
+__device__ __forceinline__ void state_chunk(const ScanParams& p, StateSmem& sm, const StateBuf& b, float (&S)[8][4],
+                                            int h, int half, int row0, int nt) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int tm = warp & 3, tn = warp >> 2;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    st_bf2(&sm.s0[(16 * warp + g) * LDN + 8 * j + 2 * c], S[j][0], S[j][1]);
+    st_bf2(&sm.s0[(16 * warp + g + 8) * LDN + 8 * j + 2 * c], S[j][2], S[j][3]);
+  }
+  __syncthreads();
+  const int t = 16 * tm + g;
+  float acc[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {  // U starts from T'V
+    const int col = 32 * tn + 8 * j + 2 * c;
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.ut[t * LDN + col]));
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.ut[(t + 8) * LDN + col]));
+    acc[j][0] = x.x, acc[j][1] = x.y, acc[j][2] = y.x, acc[j][3] = y.y;
+  }
+  float acc2[4][4] = {};  // odd K steps: two independent accumulation chains per tile
+#pragma unroll
+  for (int kk = 0; kk < DK / 16; ++kk) {
+    float(&d)[4][4] = (kk & 1) ? acc2 : acc;
+    uint32_t a[4];
+    ldsm4(a, a_rows(b.w, LDW, 16 * tm, 16 * kk, lane));
+#pragma unroll
+    for (int np = 0; np < 2; ++np) {
+      uint32_t bb[4];
+      ldsm4t(bb, b_krows(sm.s0, LDN, 16 * kk, 32 * tn + 16 * np, lane));
+      mma16816(d[2 * np], a, bb[0], bb[1]);
+      mma16816(d[2 * np + 1], a, bb[2], bb[3]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[j][e] += acc2[j][e];
+      acc2[j][e] = 0.f;
+    }
+  {
+    const float w0 = b.ws[t], w1 = b.ws[t + 8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = 32 * tn + 8 * j + 2 * c;
+      st_bf2(&sm.u[t * LDN + col], acc[j][0], acc[j][1]);
+      st_bf2(&sm.u[(t + 8) * LDN + col], acc[j][2], acc[j][3]);
+      st_bf2(&sm.us[t * LDN + col], acc[j][0] * w0, acc[j][1] * w0);
+      st_bf2(&sm.us[(t + 8) * LDN + col], acc[j][2] * w1, acc[j][3] * w1);
+      acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int kk = 0; kk < DK / 16; ++kk) {  // Q S0
+    float(&d)[4][4] = (kk & 1) ? acc2 : acc;
+    uint32_t a[4];
+    ldsm4(a, a_rows(b.qn, LDW, 16 * tm, 16 * kk, lane));
+#pragma unroll
+    for (int np = 0; np < 2; ++np) {
+      uint32_t bb[4];
+      ldsm4t(bb, b_krows(sm.s0, LDN, 16 * kk, 32 * tn + 16 * np, lane));
+      mma16816(d[2 * np], a, bb[0], bb[1]);
+      mma16816(d[2 * np + 1], a, bb[2], bb[3]);
+    }
+  }
+  {
+    const float e0 = b.eg[t], e1 = b.eg[t + 8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[j][0] = (acc[j][0] + acc2[j][0]) * e0;
+      acc[j][1] = (acc[j][1] + acc2[j][1]) * e0;
+      acc[j][2] = (acc[j][2] + acc2[j][2]) * e1;
+      acc[j][3] = (acc[j][3] + acc2[j][3]) * e1;
+    }
+  }
+#pragma unroll
+  for (int kk = 0; kk < CH / 16; ++kk) {  // + P U
+    uint32_t a[4];
+    ldsm4(a, a_rows(b.p, LDN, 16 * tm, 16 * kk, lane));
+#pragma unroll
+    for (int np = 0; np < 2; ++np) {
+      uint32_t bb[4];
+      ldsm4t(bb, b_krows(sm.u, LDN, 16 * kk, 32 * tn + 16 * np, lane));
+      mma16816(acc[2 * np], a, bb[0], bb[1]);
+      mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int col = h * DK + 64 * half + 32 * tn + 8 * j + 2 * c;
+    if (t < nt) st_bf2(p.out + static_cast<int64_t>(row0 + t) * p.ld_out + col, acc[j][0], acc[j][1]);
+    if (t + 8 < nt) st_bf2(p.out + static_cast<int64_t>(row0 + t + 8) * p.ld_out + col, acc[j][2], acc[j][3]);
+  }
+  {  // S = γ_C S0 + K^T Us (warp: rows [16 w, +16) of the slice)
+    const float ec = b.ec[0];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      S[j][0] *= ec;
+      S[j][1] *= ec;
+      S[j][2] *= ec;
+      S[j][3] *= ec;
+    }
+#pragma unroll
+    for (int kk = 0; kk < CH / 16; ++kk) {
+      uint32_t a[4];
+      ldsm4t(a, a_cols(b.kn, LDW, 16 * warp, 16 * kk, lane));
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bb[4];
+        ldsm4t(bb, b_krows(sm.us, LDN, 16 * kk, 16 * np, lane));
+        mma16816(S[2 * np], a, bb[0], bb[1]);
+        mma16816(S[2 * np + 1], a, bb[2], bb[3]);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// One CTA: (value head blockIdx.x / 2, value columns [64 (blockIdx.x % 2), +64), segment
+// blockIdx.y). Runs in order: trunk up to the save cut, trunk after it, then each branch from
+// the trunk's final state (kept in registers); the segment's chunks are contiguous in that
+// order, the next one loading while the current one is computed.
+__global__ void __launch_bounds__(256, 1) chunk_state_kernel(ScanParams p) {
   extern __shared__ __align__(16) uint8_t dsm[];
-  ChunkSmem& sm = *reinterpret_cast<ChunkSmem*>(dsm);
-  const int h = blockIdx.x;
+  StateSmem& sm = *reinterpret_cast<StateSmem*>(dsm);
+  const int h = blockIdx.x >> 1, half = blockIdx.x & 1;
   const Seg sg = p.segs[blockIdx.y];
   const int kh = h / (p.hv / p.hk);
-  const float a_neg = -__expf(p.a_log[h]), dtb = p.dt_bias[h];
-  float S[16][4], F[16][4];
+  const int64_t head_off = static_cast<int64_t>(h) * DK * DK + 64 * half;
+  float S[8][4], F[8][4];
   if (sg.init_slot >= 0) {
-    state_io(S, p.state_pool + static_cast<int64_t>(sg.init_slot) * p.slot_stride + static_cast<int64_t>(h) * DK * DK,
-             true);
+    state_io(S, p.state_pool + static_cast<int64_t>(sg.init_slot) * p.slot_stride + head_off, true);
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
+    for (int j = 0; j < 8; ++j) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
   }
+  int total = (sg.cut + CH - 1) / CH + (sg.trunk_len - sg.cut + CH - 1) / CH;
+  for (int bi = 0; bi < sg.n_branches; ++bi) total += (p.branches[4 * (sg.branch0 + bi) + 1] + CH - 1) / CH;
+  const int c0 = sg.pad;  // first chunk of the segment
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.full[0], 1);
+    mbar_init(&sm.full[1], 1);
+    fence_barrier_init();
+    if (total > 0) load_chunk(p, sm.buf[0], &sm.full[0], c0, h, kh, half);
+  }
+  __syncthreads();
+  int done = 0;
   const int n_runs = 2 + sg.n_branches;
   for (int ri = 0; ri < n_runs; ++ri) {
-    int start, len;
+    int len;
     if (ri == 0) {
-      start = sg.trunk_start;
       len = sg.cut;
     } else if (ri == 1) {
-      start = sg.trunk_start + sg.cut;
       len = sg.trunk_len - sg.cut;
     } else {
-      const int* br = p.branches + 2 * (sg.branch0 + ri - 2);
-      start = br[0];
-      len = br[1];
+      len = p.branches[4 * (sg.branch0 + ri - 2) + 1];
       if (ri > 2) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < 8; ++j)
 #pragma unroll
           for (int e = 0; e < 4; ++e) S[j][e] = F[j][e];
       }
     }
-    for (int t0 = 0; t0 < len; t0 += CH) scan_chunk(p, sm, S, h, kh, a_neg, dtb, start + t0, min(CH, len - t0));
+    for (int t0 = 0; t0 < len; t0 += CH) {
+      const int ci = c0 + done;
+      if (threadIdx.x == 0 && done + 1 < total)  // the other buffer's last reader finished (barrier below)
+        load_chunk(p, sm.buf[(done + 1) & 1], &sm.full[(done + 1) & 1], ci + 1, h, kh, half);
+      if (!mbar_wait(&sm.full[done & 1], (done >> 1) & 1)) report(p.status, kTimeoutFull);
+      state_chunk(p, sm, sm.buf[done & 1], S, h, half, p.chunks[2 * ci], p.chunks[2 * ci + 1]);
+      ++done;
+    }
     if (ri == 0 && sg.save_slot >= 0)  // state after the cached prefix -> the pool slot
-      state_io(S, p.state_pool + static_cast<int64_t>(sg.save_slot) * p.slot_stride + static_cast<int64_t>(h) * DK * DK,
-               false);
+      state_io(S, p.state_pool + static_cast<int64_t>(sg.save_slot) * p.slot_stride + head_off, false);
     if (ri == 1 && sg.n_branches > 1) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
+      for (int j = 0; j < 8; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) F[j][e] = S[j][e];
     }
@@ -600,7 +742,8 @@ DAN_API int dan_causal_conv(const void* src, int64_t ld_src, const void* hist, i
   DAN_REQUIRE(channels % 8 == 0 && ld_src % 8 == 0 && ld_out % 8 == 0 && (!hist || ld_hist % 8 == 0),
               "causal_conv: channels and strides must be multiples of 8");
   if (!rows) return 0;
-  delta::causal_conv_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  const dim3 grid((rows + delta::CONV_ROWS - 1) / delta::CONV_ROWS, (channels / 8 + 255) / 256);
+  delta::causal_conv_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(src), ld_src, static_cast<const __nv_bfloat16*>(hist), ld_hist,
       static_cast<const __nv_bfloat16*>(weight), prev, static_cast<__nv_bfloat16*>(out), ld_out, rows, channels);
   DAN_CUDA(cudaGetLastError());
@@ -618,16 +761,29 @@ DAN_API int dan_gather_rows(const void* src, int64_t ld_src, const void* hist, i
   return 0;
 }
 
+DAN_API int64_t dan_gated_delta_scratch_bytes(int n_chunks, int hk, int hv) {
+  return static_cast<int64_t>(n_chunks) * (hv * delta::REC_V + hk * delta::REC_K);
+}
+
 DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* b,
                                  const void* a, int64_t ld_ba, const float* a_log, const float* dt_bias,
-                                 const int* segs, int n_segs, const int* branches, float* state_pool,
-                                 int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv, int dk, int dv,
-                                 float q_scale, void* stream) {
+                                 const int* segs, int n_segs, const int* branches, const int* chunks, int n_chunks,
+                                 float* state_pool, int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv,
+                                 int dk, int dv, float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status,
+                                 void* stream) {
   DAN_REQUIRE(dk == delta::DK && dv == delta::DK, "gated_delta_scan: needs dk = dv = 128 (got %d, %d)", dk, dv);
   DAN_REQUIRE(ld_qkv % 8 == 0 && ld_out % 8 == 0, "gated_delta_scan: strides must be multiples of 8");
+  DAN_REQUIRE(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(k) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(v) % 16 == 0,
+              "gated_delta_scan: q, k, v must be 16-byte aligned (their rows are bulk-copied)");
   DAN_REQUIRE(hk > 0 && hv % hk == 0, "gated_delta_scan: %d value heads not a multiple of %d key heads", hv, hk);
-  DAN_REQUIRE(n_segs < 65536, "gated_delta_scan: too many segments");
-  if (!n_segs) return 0;
+  DAN_REQUIRE(n_segs < 65536 && n_chunks < (1 << 30), "gated_delta_scan: too many segments or chunks");
+  DAN_REQUIRE(scratch_bytes >= dan_gated_delta_scratch_bytes(n_chunks, hk, hv) &&
+                  reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
+              "gated_delta_scan: scratch needs %lld bytes, 16-byte aligned (got %lld)",
+              static_cast<long long>(dan_gated_delta_scratch_bytes(n_chunks, hk, hv)),
+              static_cast<long long>(scratch_bytes));
+  if (!n_segs || !n_chunks) return 0;
   delta::ScanParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k);
@@ -647,13 +803,22 @@ DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, in
   p.hk = hk;
   p.hv = hv;
   p.q_scale = q_scale;
+  p.chunks = chunks;
+  p.n_chunks = n_chunks;
+  p.scratch = static_cast<uint8_t*>(scratch);
+  p.status = status;
   static bool configured = false;
   if (!configured) {
-    DAN_CUDA(cudaFuncSetAttribute(delta::chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(sizeof(delta::ChunkSmem))));
+    DAN_CUDA(cudaFuncSetAttribute(delta::chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(sizeof(delta::PrepSmem))));
+    DAN_CUDA(cudaFuncSetAttribute(delta::chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(sizeof(delta::StateSmem))));
     configured = true;
   }
-  delta::chunk_scan_kernel<<<dim3(hv, n_segs), 256, sizeof(delta::ChunkSmem), static_cast<cudaStream_t>(stream)>>>(p);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  delta::chunk_prep_kernel<<<dim3(n_chunks, hv), 256, sizeof(delta::PrepSmem), st>>>(p);
+  DAN_CUDA(cudaGetLastError());
+  delta::chunk_state_kernel<<<dim3(2 * hv, n_segs), 256, sizeof(delta::StateSmem), st>>>(p);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }

@@ -42,23 +42,40 @@ def remap(name):
     return None
 
 
+CHUNK = 64  # tokens per chunk of the scan
+
+
 @dataclass
 class RecurrentLayout:
     """Index tables of one batch for the DeltaNet layers (the reference's RecurrentLayout,
-    qwen3_5.py:240-298, as per-row conv sources and per-segment scan records)."""
+    qwen3_5.py:240-298, as per-row conv sources, per-segment scan records and the chunk list).
+
+    A segment's runs are its trunk up to the save cut, the rest of the trunk and each
+    branch; every run is cut into chunks of ``CHUNK`` rows, listed contiguously per segment in
+    processing order. Segment records are sorted longest first (the scan's CTAs for the
+    longest chains start first)."""
     prev: torch.Tensor  # int32 [N, 3]: conv source codes of the 1st/2nd/3rd previous rows
-    segs: torch.Tensor  # int32 [S, 8]: trunk_start, trunk_len, cut, init_slot, save_slot, branch0, n_br, 0
-    branches: torch.Tensor  # int32 [B, 2]: start, len
+    segs: torch.Tensor  # int32 [S, 8]: trunk_start, trunk_len, cut, init_slot, save_slot, branch0, n_br, chunk0
+    branches: torch.Tensor  # int32 [B, 4]: start, len, chunk0, 0
+    chunks: torch.Tensor  # int32 [C, 2]: first row, rows (<= CHUNK)
     tail_codes: torch.Tensor  # int32 [saves * (k-1)]: conv-tail source codes at each save cut
     tail_dst: list  # (slot) per save
     n_segs: int
     n_rows: int
+    n_chunks: int = 0
     n_state_io: int = 0  # fp32 states the scan reads (cached pasts) plus writes (save cuts)
 
     @classmethod
     def build(cls, segments, n_rows, k1, device):
         prev = np.full((max(n_rows, 1), k1), -1, dtype=np.int32)
-        segs, brs, tail, tail_dst = [], [], [], []
+        segs, brs, tail, tail_dst, chunks = [], [], [], [], []
+
+        def cut_runs(start, length):
+            first = len(chunks)
+            for t0 in range(0, length, CHUNK):
+                chunks.append((start + t0, min(CHUNK, length - t0)))
+            return first
+
         for s in segments:
             slot = s.past.slot if s.past else -1
             hist = [-(2 + slot * k1 + j) for j in range(k1)] if s.past else [-1] * k1
@@ -77,8 +94,13 @@ class RecurrentLayout:
             if save_slot >= 0:
                 tail += virt[cut:k1 + cut]
                 tail_dst.append(save_slot)
-            segs.append((s.start, s.trunk, cut, slot, save_slot, len(brs), len(s.branches), 0))
-            brs += [(a, b - a) for a, b in s.branches]
+            chunk0 = cut_runs(s.start, cut)
+            cut_runs(s.start + cut, s.trunk - cut)
+            b0 = len(brs)
+            for a, b in s.branches:
+                brs.append((a, b - a, cut_runs(a, b - a), 0))
+            segs.append((s.start, s.trunk, cut, slot, save_slot, b0, len(s.branches), chunk0))
+        segs.sort(key=lambda r: -(r[1] + sum(brs[r[5] + i][1] for i in range(r[6]))))
         dev = torch.device(device)
 
         def up(a, shape):
@@ -86,8 +108,9 @@ class RecurrentLayout:
             return t.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else t
 
         io = sum((r[3] >= 0) + (r[4] >= 0) for r in segs)
-        return cls(up(prev[:max(n_rows, 1)], (-1, k1)), up(segs, (-1, 8)), up(brs or [(0, 0)], (-1, 2)),
-                   up(tail or [0], (-1,)), tail_dst, len(segs), n_rows, int(io))
+        return cls(up(prev[:max(n_rows, 1)], (-1, k1)), up(segs, (-1, 8)), up(brs or [(0, 0, 0, 0)], (-1, 4)),
+                   up(chunks or [(0, 0)], (-1, 2)), up(tail or [0], (-1,)), tail_dst, len(segs), n_rows,
+                   len(chunks), int(io))
 
 
 class Qwen35ForReads:
@@ -180,10 +203,11 @@ class Qwen35ForReads:
         table = ops.rope_table(positions, self.inv_freq)
         lay = layout_of(segments, n, self.device)
         rl = self._recurrent(segments, n) if self.delta_index else None
+        scratch = _lib.delta_scratch(rl.n_chunks, self.hk, self.hv, self.device) if rl is not None else None
         for i, L in enumerate(self.layers):
             hn = ops.rms_norm(x, L["in_norm"], self.eps, zero_centered=True)
             if L["kind"] == "linear_attention":
-                self._deltanet(i, L, hn, x, rl)
+                self._deltanet(i, L, hn, x, rl, scratch)
             else:
                 self._attention(i, L, hn, x, table, lay, saves)
             hn = ops.rms_norm(x, L["post_norm"], self.eps, zero_centered=True)
@@ -191,7 +215,7 @@ class Qwen35ForReads:
             ops.linear(act, L["down"].w, residual=x)
         return x
 
-    def _deltanet(self, i, L, hn, x, rl):
+    def _deltanet(self, i, L, hn, x, rl, scratch):
         n = hn.shape[0]
         li = self.delta_index[i]
         kd, vd, hv, C = self.hk * self.dk, self.hv * self.dv, self.hv, self.conv_dim
@@ -214,9 +238,10 @@ class Qwen35ForReads:
         out = torch.empty(n, vd, dtype=torch.bfloat16, device=self.device)
         _lib.call("dan_gated_delta_scan", _lib.ptr(conv[:, :kd]), _lib.ptr(conv[:, kd:2 * kd]), _lib.ptr(conv[:, 2 * kd:]),
                   C, _lib.ptr(b), _lib.ptr(a), P.stride(0), _lib.ptr(L["a_log"]), _lib.ptr(L["dt_bias"]),
-                  _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), _lib.ptr(state),
-                  state.stride(0) if state is not None else 0, _lib.ptr(out), vd, self.hk, hv, self.dk, self.dv,
-                  float(self.dk ** -0.5), _lib.stream(),
+                  _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), _lib.ptr(rl.chunks), rl.n_chunks,
+                  _lib.ptr(state), state.stride(0) if state is not None else 0, _lib.ptr(out), vd, self.hk, hv,
+                  self.dk, self.dv, float(self.dk ** -0.5), _lib.ptr(scratch), scratch.numel(),
+                  _lib.ptr(_lib.status_word(self.device)), _lib.stream(),
                   work=n * (2 * kd + vd) * 2 + n * hv * 2 * 2 + n * vd * 2 + rl.n_state_io * hv * self.dk * self.dv * 4)
         y = torch.empty_like(out)
         _lib.call("dan_gated_rms_norm", _lib.ptr(out), vd, _lib.ptr(z), P.stride(0), _lib.ptr(L["gnorm"]),

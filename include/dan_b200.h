@@ -142,13 +142,22 @@ int dan_gather_rows(const void* src, int64_t ld_src, const void* hist, int64_t l
                     void* dst, int64_t ld_dst, int cols, void* stream);
 /* Gated delta rule over the tree of runs of a packed batch (delta_rule, qwen3_5.py:136-158; the
  * trunk/branch phases of DeltaNet.forward, 196-210), with the gates (delta_gates, fused.py:79-82)
- * and the q/k l2 norms fused. segs: int32 [n_segs, 8] {trunk_start, trunk_len, cut, init_slot,
- * save_slot, branch0, n_branches, 0}; branches: int32 [.., 2] {start, len}; state_pool: fp32
- * [slots, hv, 128, 128] of this layer (init / save slots, -1 = none). dk = dv = 128. */
+ * and the q/k l2 norms fused, in 64-token chunks (the WY form of chunk_gated_delta_rule).
+ * segs: int32 [n_segs, 8] {trunk_start, trunk_len, cut, init_slot, save_slot, branch0,
+ * n_branches, first chunk}; branches: int32 [.., 4] {start, len, first chunk, 0}; chunks: int32
+ * [n_chunks, 2] {first row, rows <= 64}, each segment's runs (trunk to the cut, rest of the
+ * trunk, each branch) cut into chunks listed contiguously in that order; state_pool: fp32
+ * [slots, hv, 128, 128] of this layer (init / save slots, -1 = none). dk = dv = 128.
+ * scratch: caller-owned device buffer of dan_gated_delta_scratch_bytes(n_chunks, hk, hv) bytes
+ * (16-byte aligned) for the per-chunk intermediates; it is fully rewritten by each call. */
 int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* b, const void* a,
                          int64_t ld_ba, const float* a_log, const float* dt_bias, const int* segs, int n_segs,
-                         const int* branches, float* state_pool, int64_t slot_stride, void* out, int64_t ld_out,
-                         int hk, int hv, int dk, int dv, float q_scale, void* stream);
+                         const int* branches, const int* chunks, int n_chunks, float* state_pool,
+                         int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv, int dk, int dv,
+                         float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream);
+/* Bytes of scratch dan_gated_delta_scan needs for n_chunks chunks (45824 per chunk and value head
+ * plus 34816 per chunk and key head). */
+int64_t dan_gated_delta_scratch_bytes(int n_chunks, int hk, int hv);
 /* y = bf16(w * bf16(x_hat)) * silu(z) per (row, head) (gated_rms_norm, dan/fused.py:51-56). */
 int dan_gated_rms_norm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* w, float eps, void* y,
                        int64_t ldy, int rows, int heads, int dv, void* stream);

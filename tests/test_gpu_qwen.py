@@ -70,10 +70,12 @@ def _scan_case(cuda, hk, hv, seg_shapes, seed=0):
               _lib.ptr(conv), C, n, C, _lib.stream())
     out = torch.empty(n, hv * dv, dtype=torch.bfloat16, device=cuda)
     kd = hk * dk
+    scratch = _lib.delta_scratch(rl.n_chunks, hk, hv, cuda)
     _lib.call("dan_gated_delta_scan", _lib.ptr(conv[:, :kd]), _lib.ptr(conv[:, kd:2 * kd]), _lib.ptr(conv[:, 2 * kd:]),
               C, _lib.ptr(ba_d[:, :hv]), _lib.ptr(ba_d[:, hv:]), 2 * hv, _lib.ptr(a_log_d), _lib.ptr(dt_d),
-              _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), None, 0,
-              _lib.ptr(out), hv * dv, hk, hv, dk, dv, float(dk ** -0.5), _lib.stream())
+              _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), _lib.ptr(rl.chunks), rl.n_chunks, None, 0,
+              _lib.ptr(out), hv * dv, hk, hv, dk, dv, float(dk ** -0.5), _lib.ptr(scratch), scratch.numel(),
+              _lib.ptr(_lib.status_word(cuda)), _lib.stream())
     torch.cuda.synchronize()
     # oracle: same tree runs, token by token, from the same bf16 inputs
     w = conv_w[:, None, :].float()

@@ -168,3 +168,33 @@ def test_lpt_schedule_covers_every_item_once():
     cost = lay.costs.repeat(16) + lay.ITEM_OVERHEAD
     loads = [cost[items[offs[c]:offs[c + 1]]].sum() for c in range(ctas)]
     assert max(loads) <= sum(loads) / ctas + cost.max()  # greedy LPT bound
+
+
+def test_recurrent_layout_chunks_follow_each_segments_runs():
+    """The DeltaNet scan's chunk list: every run (trunk to the save cut, rest of the trunk, each
+    branch) is cut into chunks of at most 64 rows that tile it exactly; a segment's chunks are
+    contiguous in processing order from its record's first-chunk field; segment records are
+    sorted longest first (the longest chains start first)."""
+    from dan_b200.qwen3_5 import CHUNK, RecurrentLayout
+
+    segs, n, _ = build_segments([(70, [3, 64, 65], 0), (300, [], 0), (1, [129], 0), (64, [1], 0)],
+                                shuffle_pages=False)
+    segs[1].save = 130  # a save cut inside the trunk splits it into two runs
+    rl = RecurrentLayout.build(segs, n, 3, "cpu")
+    recs, brs, chunks = rl.segs.numpy(), rl.branches.numpy(), rl.chunks.numpy()
+    assert rl.n_chunks == len(chunks) and (chunks[:, 1] >= 1).all() and (chunks[:, 1] <= CHUNK).all()
+    lens = [r[1] + sum(brs[r[5] + i][1] for i in range(r[6])) for r in recs]
+    assert lens == sorted(lens, reverse=True)
+    seen = []
+    for r in recs:
+        start, trunk, cut, b0, nb, c = r[0], r[1], r[2], r[5], r[6], r[7]
+        runs = [(start, cut), (start + cut, trunk - cut)] + [(brs[b0 + i][0], brs[b0 + i][1]) for i in range(nb)]
+        for i, (rs, rlen) in enumerate(runs):
+            if i >= 2:
+                assert brs[b0 + i - 2][2] == c  # a branch record points at its first chunk
+            for t0 in range(0, rlen, CHUNK):
+                assert tuple(chunks[c]) == (rs + t0, min(CHUNK, rlen - t0))
+                seen.append(c)
+                c += 1
+    assert sorted(seen) == list(range(rl.n_chunks))  # every chunk belongs to exactly one run
+    assert recs[[r[1] for r in recs].index(300)][2] == 130
