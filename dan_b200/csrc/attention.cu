@@ -407,34 +407,44 @@ __device__ __forceinline__ uint32_t span_bits(int lo, int hi) {
   return upto & ~((1u << lo) - 1u);
 }
 
-// 2^x on the FMA pipe, to share the exponentials with the MUFU unit: Cody-Waite range
-// reduction x = n + f with n = round(x) taken from a magic-constant add (1.5 * 2^23) and
-// f in [-1/2, 1/2], 2^f by a degree-3 polynomial (coefficients fitted for this kernel by
-// weighted least squares toward minimax: max relative error 7.7e-5, far below the bf16
-// rounding P takes next), and 2^n added into the exponent bits. For finite x <= 8.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float n = t - 12582912.f;
-  const float f = x - n;
-  const float q = fmaf(fmaf(fmaf(0.05518098f, f, 0.24263459f), f, 0.69326133f), f, 0.99992621f);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+// Packed fp32 pairs (sm_100 f32x2 arithmetic) and the three-input max: the softmax warps are
+// issue-bound, and these halve the instructions per score of the max, scale and sum steps.
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
 }
-
-// One pair in EXP_EMU_EVERY of a fully visible chunk takes exp2_fma instead of MUFU.EX2.
-constexpr int EXP_EMU_EVERY = 4;
+__device__ __forceinline__ void f2_split(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 // Row max over 32 raw scores whose visibility bits are ``mw`` (all-visible and
 // all-masked chunks skip the per-element bit tests).
 __device__ __forceinline__ void chunk_max(const uint32_t (&s)[32], uint32_t mw, float& mx) {
   if (mw == 0xffffffffu) {
-    float a = __uint_as_float(s[0]), b = __uint_as_float(s[1]);
+    float a = fmax3(__uint_as_float(s[0]), __uint_as_float(s[1]), __uint_as_float(s[2]));
+    float b = fmax3(__uint_as_float(s[3]), __uint_as_float(s[4]), __uint_as_float(s[5]));
 #pragma unroll
-    for (int i = 2; i < 32; i += 2) {
-      a = fmaxf(a, __uint_as_float(s[i]));
-      b = fmaxf(b, __uint_as_float(s[i + 1]));
+    for (int i = 6; i + 3 < 32; i += 4) {
+      a = fmax3(a, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+      b = fmax3(b, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
     }
-    mx = fmaxf(mx, fmaxf(a, b));
+    mx = fmax3(mx, fmax3(a, b, __uint_as_float(s[30])), __uint_as_float(s[31]));
   } else if (mw) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) mx = fmaxf(mx, ((mw >> i) & 1u) ? __uint_as_float(s[i]) : -INFINITY);
@@ -445,18 +455,19 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&s)[32], uint32_t mw, 
 __device__ __forceinline__ void chunk_exp(const uint32_t (&s)[32], uint32_t mw, float sl2, float mu, float& sum,
                                           uint32_t (&pk)[16]) {
   if (mw == 0xffffffffu) {
-    float acc0 = 0.f, acc1 = 0.f;
+    const uint64_t scale = f2(sl2, sl2), shift = f2(-mu, -mu);
+    uint64_t acc = f2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float xa = fmaf(__uint_as_float(s[2 * i]), sl2, -mu), xb = fmaf(__uint_as_float(s[2 * i + 1]), sl2, -mu);
-      const bool emu = (i % EXP_EMU_EVERY) == EXP_EMU_EVERY - 1;
-      const float a = emu ? exp2_fma(xa) : fast_exp2(xa);
-      const float b = emu ? exp2_fma(xb) : fast_exp2(xb);
-      acc0 += a;
-      acc1 += b;
+      float xa, xb;
+      f2_split(ffma2(f2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), scale, shift), xa, xb);
+      const float a = fast_exp2(xa), b = fast_exp2(xb);
+      acc = fadd2(acc, f2(a, b));
       pk[i] = pack_bf16(a, b);
     }
-    sum += acc0 + acc1;
+    float s0, s1;
+    f2_split(acc, s0, s1);
+    sum += s0 + s1;
   } else if (mw == 0u) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) pk[i] = 0u;
