@@ -43,7 +43,9 @@ __global__ void embed_kernel(const int64_t* ids, const __nv_bfloat16* table, int
 // mode 1 (zero-centred, fused.py:43-48): y = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))
 // With ``q8`` set, y is also quantised per row to e4m3 (fused.py:85-91):
 //   scale = max(amax |y|, 1e-12) / 448, q = e4m3(y / scale).
-template <int MAXV>  // 16-byte vectors per lane (a row holds at most 32 * MAXV * 8 elements)
+// MAXV: 16-byte vectors per lane (a row holds at most 32 * MAXV * 8 elements); Q8: also
+// quantise the normalised row to e4m3 (the per-row amax is tracked only then).
+template <int MAXV, bool Q8>
 __global__ void rms_norm_kernel(const __nv_bfloat16* x, int64_t x_outer, int64_t x_inner, int inner,
                                 const __nv_bfloat16* w, float eps, int mode, __nv_bfloat16* y, int64_t y_outer,
                                 int64_t y_inner, uint8_t* q8, int64_t ldq, float* q8_scale, int rows, int cols) {
@@ -88,12 +90,12 @@ __global__ void rms_norm_kernel(const __nv_bfloat16* x, int64_t x_outer, int64_t
         else
           o = f * (1.f + __bfloat162float(we[t]));
         e[t] = __float2bfloat16_rn(o);
-        amax = fmaxf(amax, fabsf(__bfloat162float(e[t])));
+        if (Q8) amax = fmaxf(amax, fabsf(__bfloat162float(e[t])));
       }
       if (y) reinterpret_cast<uint4*>(yr)[v] = buf[i];
     }
   }
-  if (q8) {
+  if (Q8) {
     amax = warp_max(amax);
     const float scale = fmaxf(amax, 1e-12f) / 448.f;
     uint8_t* qr = q8 + static_cast<int64_t>(r) * ldq;
@@ -339,9 +341,15 @@ DAN_API int dan_rms_norm(const void* x, int64_t x_outer, int64_t x_inner, int in
   const auto* wb = static_cast<const __nv_bfloat16*>(w);
   auto* yb = static_cast<__nv_bfloat16*>(y);
   auto* qb = static_cast<uint8_t*>(q8);
-#define DAN_NORM(NV) \
-  ew::rms_norm_kernel<NV><<<grid, block, 0, s>>>(xb, x_outer, x_inner, inner, wb, eps, mode, yb, y_outer, y_inner, qb, \
-                                                 ldq, q8_scale, rows, cols)
+#define DAN_NORM(NV)                                                                                            \
+  do {                                                                                                          \
+    if (qb)                                                                                                     \
+      ew::rms_norm_kernel<NV, true><<<grid, block, 0, s>>>(xb, x_outer, x_inner, inner, wb, eps, mode, yb, y_outer, \
+                                                           y_inner, qb, ldq, q8_scale, rows, cols);             \
+    else                                                                                                        \
+      ew::rms_norm_kernel<NV, false><<<grid, block, 0, s>>>(xb, x_outer, x_inner, inner, wb, eps, mode, yb,        \
+                                                            y_outer, y_inner, qb, ldq, q8_scale, rows, cols);   \
+  } while (0)
   if (per_lane <= 1)
     DAN_NORM(1);
   else if (per_lane <= 2)
