@@ -433,52 +433,96 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Row max over 32 raw scores whose visibility bits are ``mw`` (all-visible and
-// all-masked chunks skip the per-element bit tests).
-__device__ __forceinline__ void chunk_max(const uint32_t (&s)[32], uint32_t mw, float& mx) {
-  if (mw == 0xffffffffu) {
-    float a = fmax3(__uint_as_float(s[0]), __uint_as_float(s[1]), __uint_as_float(s[2]));
-    float b = fmax3(__uint_as_float(s[3]), __uint_as_float(s[4]), __uint_as_float(s[5]));
-#pragma unroll
-    for (int i = 6; i + 3 < 32; i += 4) {
-      a = fmax3(a, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
-      b = fmax3(b, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
-    }
-    mx = fmax3(mx, fmax3(a, b, __uint_as_float(s[30])), __uint_as_float(s[31]));
-  } else if (mw) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, ((mw >> i) & 1u) ? __uint_as_float(s[i]) : -INFINITY);
-  }
+// 2^x for a pair of floats on the FMA pipe (packed f32x2), sharing the exponentials with the
+// MUFU unit, which limits the softmax otherwise (one warp's 4096 exponentials per block are
+// 1024 MUFU cycles on its SM sub-partition). Cody-Waite range reduction x = n + f with
+// n = round(x) taken from a magic-constant add (1.5 * 2^23) and f in [-1/2, 1/2]; 2^f by a
+// degree-3 polynomial (coefficients fitted for this kernel by weighted least squares toward
+// minimax: max relative error 7.7e-5, far below the bf16 rounding P takes next); 2^n added
+// into the exponent bits. For finite x <= 8; x below -125 gives 2^-125, not 0, so only fully
+// visible chunks (no -inf scores) use it.
+__device__ __forceinline__ void exp2_pair_fma(uint64_t x2, float& ra, float& rb) {
+  float xa, xb;
+  f2_split(x2, xa, xb);
+  const uint64_t xc = f2(fmaxf(xa, -125.f), fmaxf(xb, -125.f));
+  const uint64_t t = fadd2(xc, f2(12582912.f, 12582912.f));
+  const uint64_t n = fadd2(t, f2(-12582912.f, -12582912.f));
+  const uint64_t f = ffma2(n, f2(-1.f, -1.f), xc);
+  uint64_t q = ffma2(f2(0.05518098f, 0.05518098f), f, f2(0.24263459f, 0.24263459f));
+  q = ffma2(q, f, f2(0.69326133f, 0.69326133f));
+  q = ffma2(q, f, f2(0.99992621f, 0.99992621f));
+  float qa, qb, ta, tb;
+  f2_split(q, qa, qb);
+  f2_split(t, ta, tb);
+  ra = __int_as_float(__float_as_int(qa) + (__float_as_int(ta) << 23));
+  rb = __int_as_float(__float_as_int(qb) + (__float_as_int(tb) << 23));
 }
 
-// P = exp2(s * scale_log2 - m) for 32 scores as 16 bf16 pairs; masked scores give 0.
-__device__ __forceinline__ void chunk_exp(const uint32_t (&s)[32], uint32_t mw, float sl2, float mu, float& sum,
-                                          uint32_t (&pk)[16]) {
-  if (mw == 0xffffffffu) {
-    const uint64_t scale = f2(sl2, sl2), shift = f2(-mu, -mu);
-    uint64_t acc = f2(0.f, 0.f);
+// One score pair in EXP_EMU_EVERY of a fully visible chunk takes exp2_pair_fma (measured on
+// configuration-2 batches: none 535, 1 in 4 551, 1 in 3 547, 1 in 2 532 TFLOP/s).
+constexpr int EXP_EMU_EVERY = 4;
+
+// Masked scores become -inf in place (partially visible chunks then take the packed path:
+// exp2(-inf) = 0 and -inf never wins a max).
+__device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], uint32_t mw) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 32; ++i) s[i] = ((mw >> i) & 1u) ? s[i] : 0xff800000u;
+}
+
+// Row max over 32 scores (already masked, or all visible).
+__device__ __forceinline__ void chunk_max(const uint32_t (&s)[32], float& mx) {
+  float a = fmax3(__uint_as_float(s[0]), __uint_as_float(s[1]), __uint_as_float(s[2]));
+  float b = fmax3(__uint_as_float(s[3]), __uint_as_float(s[4]), __uint_as_float(s[5]));
+#pragma unroll
+  for (int i = 6; i + 3 < 32; i += 4) {
+    a = fmax3(a, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+    b = fmax3(b, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
+  }
+  mx = fmax3(mx, fmax3(a, b, __uint_as_float(s[30])), __uint_as_float(s[31]));
+}
+
+// P = exp2(s * scale_log2 - m) for 32 scores (masked ones are -inf and give 0) as 16 bf16
+// pairs; with ``emu`` (a fully visible chunk) every EXP_EMU_EVERY-th pair on the FMA pipe.
+template <bool EMU>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&s)[32], float sl2, float mu, float& sum,
+                                          uint32_t (&pk)[16]) {
+  const uint64_t scale = f2(sl2, sl2), shift = f2(-mu, -mu);
+  uint64_t acc = f2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint64_t x2 = ffma2(f2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), scale, shift);
+    float a, b;
+    if (EMU && i % EXP_EMU_EVERY == EXP_EMU_EVERY - 1) {
+      exp2_pair_fma(x2, a, b);
+    } else {
       float xa, xb;
-      f2_split(ffma2(f2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), scale, shift), xa, xb);
-      const float a = fast_exp2(xa), b = fast_exp2(xb);
-      acc = fadd2(acc, f2(a, b));
-      pk[i] = pack_bf16(a, b);
+      f2_split(x2, xa, xb);
+      a = fast_exp2(xa);
+      b = fast_exp2(xb);
     }
-    float s0, s1;
-    f2_split(acc, s0, s1);
-    sum += s0 + s1;
-  } else if (mw == 0u) {
+    acc = fadd2(acc, f2(a, b));
+    pk[i] = pack_bf16(a, b);
+  }
+  float s0, s1;
+  f2_split(acc, s0, s1);
+  sum += s0 + s1;
+}
+
+// One 32-column chunk of S: mask it unless fully visible; a fully masked chunk needs no work.
+__device__ __forceinline__ void chunk_prep(uint32_t (&s)[32], uint32_t mw, float& mx) {
+  if (mw == 0u) return;
+  if (mw != 0xffffffffu) mask_chunk(s, mw);
+  chunk_max(s, mx);
+}
+__device__ __forceinline__ void chunk_p(const uint32_t (&s)[32], uint32_t mw, float sl2, float mu, float& sum,
+                                        uint32_t (&pk)[16]) {
+  if (mw == 0u) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) pk[i] = 0u;
+  } else if (mw == 0xffffffffu) {
+    chunk_exp<true>(s, sl2, mu, sum, pk);
   } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float a = ((mw >> (2 * i)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s[2 * i]), sl2, -mu)) : 0.f;
-      const float b = ((mw >> (2 * i + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -mu)) : 0.f;
-      sum += a + b;
-      pk[i] = pack_bf16(a, b);
-    }
+    chunk_exp<false>(s, sl2, mu, sum, pk);
   }
 }
 
@@ -705,24 +749,22 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        // S is read in 32-column chunks through two register buffers, each load issued before
-        // the previous chunk is processed. Pass 1 (row max) walks chunks 3..0 so chunk 0 is still
-        // held for pass 2, which walks 0..3: P for chunk c overwrites S columns [16c, 16c + 16),
-        // all of which belong to chunks already consumed.
+        // S is read in 32-column chunks, two loads in flight per wait (tcgen05.wait::ld waits for
+        // every outstanding load): pass 1 takes chunks 3, 2 then 1, 0 for the row max and keeps
+        // chunks 1 and 0; pass 2 writes P0 and P1 from them (P chunk c covers S columns
+        // [16c, 16c + 16), already consumed), then reloads chunks 2 and 3 for P2 and P3.
         uint32_t x[32], y[32];
         float mx = -INFINITY;
         tmem_ld32(s_addr + 96, x);
-        tmem_wait_ld();
         tmem_ld32(s_addr + 64, y);
-        chunk_max(x, mw[3], mx);
         tmem_wait_ld();
+        chunk_prep(x, mw[3], mx);
+        chunk_prep(y, mw[2], mx);
         tmem_ld32(s_addr + 32, x);
-        chunk_max(y, mw[2], mx);
-        tmem_wait_ld();
         tmem_ld32(s_addr + 0, y);
-        chunk_max(x, mw[1], mx);
         tmem_wait_ld();
-        chunk_max(y, mw[0], mx);
+        chunk_prep(x, mw[1], mx);
+        chunk_prep(y, mw[0], mx);
         const float m_new = fmaxf(m, mx * sl2);
         bool rescale = false;
         float alpha = 1.f;
@@ -739,28 +781,21 @@ __global__ void __launch_bounds__(320, 1)
         float sum0 = 0.f, sum1 = 0.f;
         {
           uint32_t pk[16];
-          tmem_ld32(s_addr + 32, x);
-          chunk_exp(y, mw[0], sl2, mu, sum0, pk);
+          chunk_p(y, mw[0], sl2, mu, sum0, pk);
           tmem_st16(s_addr + 0, pk);
-          tmem_wait_ld();
-        }
-        {
-          uint32_t pk[16];
-          tmem_ld32(s_addr + 64, y);
-          chunk_exp(x, mw[1], sl2, mu, sum1, pk);
+          chunk_p(x, mw[1], sl2, mu, sum1, pk);
           tmem_st16(s_addr + 16, pk);
-          tmem_wait_ld();
         }
+        tmem_ld32(s_addr + 64, x);
+        tmem_ld32(s_addr + 96, y);
+        tmem_wait_ld();
         {
           uint32_t pk[16];
-          tmem_ld32(s_addr + 96, x);
-          chunk_exp(y, mw[2], sl2, mu, sum0, pk);
+          if (mw[2] != 0xffffffffu && mw[2]) mask_chunk(x, mw[2]);
+          chunk_p(x, mw[2], sl2, mu, sum0, pk);
           tmem_st16(s_addr + 32, pk);
-          tmem_wait_ld();
-        }
-        {
-          uint32_t pk[16];
-          chunk_exp(x, mw[3], sl2, mu, sum1, pk);
+          if (mw[3] != 0xffffffffu && mw[3]) mask_chunk(y, mw[3]);
+          chunk_p(y, mw[3], sl2, mu, sum1, pk);
           tmem_st16(s_addr + 48, pk);
         }
         l = l * alpha + (sum0 + sum1);
