@@ -115,3 +115,12 @@ def test_conv_and_scan_vs_oracle(cuda, hk, hv):
     # bf16 inputs of the scan (conv output) vs an fp32 oracle on the same pre-conv rows
     err = (got - want).abs().max().item() / want.abs().max().item()
     assert err < 2e-2, err
+
+
+def test_long_chunk_chain_vs_oracle(cuda):
+    """A 1500-token trunk (24 chunks of the WY-form scan, the state carried 23 times through
+    bf16 operands) plus branches and a chunk-aligned 64-token trunk, vs the fp64 token
+    recurrence: the chunked form must not drift over a long chain."""
+    got, want = _scan_case(cuda, 1, 2, [(1500, [40, 64]), (64, [1])], seed=3)
+    err = (got - want).abs().max().item() / want.abs().max().item()
+    assert err < 2e-2, err
