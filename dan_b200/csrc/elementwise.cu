@@ -43,6 +43,103 @@ __global__ void embed_kernel(const int64_t* ids, const __nv_bfloat16* table, int
 // mode 1 (zero-centred, fused.py:43-48): y = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))
 // With ``q8`` set, y is also quantised per row to e4m3 (fused.py:85-91):
 //   scale = max(amax |y|, 1e-12) / 448, q = e4m3(y / scale).
+// Wide rows (hidden-size norms): 128 threads per row, two rows per block, VPT 16-byte vectors
+// per thread, the sum of squares (and the e4m3 amax) reduced through shared memory. Small
+// per-thread state keeps many rows in flight per SM, so loads, arithmetic and stores of
+// different blocks overlap. Mode 0 writes w * bf16(x * inv) with one rounded bf16 product per
+// pair (the exact product of two bf16 values fits in fp32, so this equals the fp32 product
+// rounded to bf16); mode 1 bf16(x * inv * (1 + w)) in fp32.
+template <int VPT, bool Q8>
+__global__ void __launch_bounds__(256) rms_norm_wide_kernel(const __nv_bfloat16* x, int64_t x_outer, int64_t x_inner,
+                                                             int inner, const __nv_bfloat16* w, float eps, int mode,
+                                                             __nv_bfloat16* y, int64_t y_outer, int64_t y_inner,
+                                                             uint8_t* q8, int64_t ldq, float* q8_scale, int rows,
+                                                             int cols) {
+  __shared__ float red[2][4];
+  const int rg = threadIdx.x >> 7, t = threadIdx.x & 127, wg = t >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 2 + rg;
+  const bool live = r < rows;
+  const int rr = live ? r : 0;
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(rr / inner) * x_outer + static_cast<int64_t>(rr % inner) * x_inner;
+  __nv_bfloat16* yr = y ? y + static_cast<int64_t>(rr / inner) * y_outer + static_cast<int64_t>(rr % inner) * y_inner
+                        : nullptr;
+  const int nvec = cols / 8;
+  uint4 buf[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = t + 128 * i;
+    if (live && v < nvec) {
+      buf[i] = reinterpret_cast<const uint4*>(xr)[v];
+      const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&buf[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(e[k]);
+        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[rg][wg] = ss;
+  __syncthreads();
+  const float inv = rsqrtf((red[rg][0] + red[rg][1] + red[rg][2] + red[rg][3]) / cols + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = t + 128 * i;
+    if (live && v < nvec) {
+      __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&buf[i]);
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + v);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(e[k]);
+        if (mode == 0) {
+          e[k] = __hmul2(__floats2bfloat162_rn(f.x * inv, f.y * inv), w2[k]);
+        } else {
+          const float2 wf = __bfloat1622float2(w2[k]);
+          e[k] = __floats2bfloat162_rn(f.x * inv * (1.f + wf.x), f.y * inv * (1.f + wf.y));
+        }
+        if (Q8) {
+          const float2 o = __bfloat1622float2(e[k]);
+          amax = fmaxf(amax, fmaxf(fabsf(o.x), fabsf(o.y)));
+        }
+      }
+      if (yr) reinterpret_cast<uint4*>(yr)[v] = buf[i];
+    }
+  }
+  if (Q8) {
+    amax = warp_max(amax);
+    __syncthreads();  // every thread has read the sum of squares
+    if (lane == 0) red[rg][wg] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(red[rg][0], red[rg][1]), fmaxf(red[rg][2], red[rg][3]));
+    const float scale = fmaxf(amax, 1e-12f) / 448.f;
+    if (live) {
+      uint8_t* qr = q8 + static_cast<int64_t>(r) * ldq;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int v = t + 128 * i;
+        if (v < nvec) {
+          const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&buf[i]);
+          uint32_t lo = 0, hi = 0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const __nv_fp8_e4m3 c(__bfloat162float(e[k]) / scale);
+            const uint32_t b = *reinterpret_cast<const uint8_t*>(&c);
+            if (k < 4)
+              lo |= b << (8 * k);
+            else
+              hi |= b << (8 * (k - 4));
+          }
+          reinterpret_cast<uint2*>(qr)[v] = make_uint2(lo, hi);
+        }
+      }
+      if (t == 0) q8_scale[r] = scale;
+    }
+  }
+}
+
 // MAXV: 16-byte vectors per lane (a row holds at most 32 * MAXV * 8 elements); Q8: also
 // quantise the normalised row to e4m3 (the per-row amax is tracked only then).
 template <int MAXV, bool Q8>
@@ -333,6 +430,33 @@ DAN_API int dan_rms_norm(const void* x, int64_t x_outer, int64_t x_inner, int in
               "rms_norm: strides must be multiples of 8");
   DAN_REQUIRE(y || q8, "rms_norm: no output");
   if (!rows) return 0;
+  cudaStream_t s0 = static_cast<cudaStream_t>(stream);
+  if (cols >= 2048) {  // hidden-size rows: 128 threads per row
+    const int vpt = (cols / 8 + 127) / 128;
+    const dim3 g2((rows + 1) / 2);
+    const auto* xw = static_cast<const __nv_bfloat16*>(x);
+    const auto* ww = static_cast<const __nv_bfloat16*>(w);
+    auto* yw = static_cast<__nv_bfloat16*>(y);
+    auto* qw = static_cast<uint8_t*>(q8);
+#define DAN_WIDE(V)                                                                                                 \
+  do {                                                                                                              \
+    if (qw)                                                                                                         \
+      ew::rms_norm_wide_kernel<V, true><<<g2, 256, 0, s0>>>(xw, x_outer, x_inner, inner, ww, eps, mode, yw, y_outer, \
+                                                            y_inner, qw, ldq, q8_scale, rows, cols);                  \
+    else                                                                                                            \
+      ew::rms_norm_wide_kernel<V, false><<<g2, 256, 0, s0>>>(xw, x_outer, x_inner, inner, ww, eps, mode, yw,       \
+                                                             y_outer, y_inner, qw, ldq, q8_scale, rows, cols);      \
+  } while (0)
+    if (vpt <= 2)
+      DAN_WIDE(2);
+    else if (vpt <= 4)
+      DAN_WIDE(4);
+    else
+      DAN_WIDE(8);
+#undef DAN_WIDE
+    DAN_CUDA(cudaGetLastError());
+    return 0;
+  }
   const int warps = 8;
   const int per_lane = (cols / 8 + 31) / 32;
   const dim3 grid((rows + warps - 1) / warps), block(32 * warps);

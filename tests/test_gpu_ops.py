@@ -237,3 +237,28 @@ def test_kv_store(cuda):
     dst = torch.tensor([130, 131, 132], dtype=torch.int32, device=cuda)
     ops.kv_store(k, v, pk, pv, src, dst)
     assert torch.equal(pk[130:133], k[3:6]) and torch.equal(pv[130:133], v[3:6])
+
+
+@pytest.mark.parametrize("cols", [4096, 2560])
+def test_rms_norm_wide_rounding(cuda, cols):
+    """Hidden-size rows take the 128-threads-per-row kernel: outputs must follow the reference's
+    rounding points (mode 0: bf16(w * bf16(x * inv)); mode 1: bf16(x * inv * (1 + w)) in fp32,
+    fused.py:35-48) up to one-ulp flips where the sum-of-squares order moves x * inv across a
+    rounding boundary; the fused e4m3 output matches the quantisation of that bf16 row."""
+    g = torch.Generator(device=cuda).manual_seed(cols)
+    x = torch.randn(301, cols, device=cuda, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(cols, device=cuda, generator=g)).bfloat16()
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)
+    refs = {0: (w.float() * (xf * inv).bfloat16().float()).bfloat16(),
+            1: (xf * inv * (1 + w.float())).bfloat16()}
+    for mode, ref in refs.items():
+        y = ops.rms_norm(x, w, 1e-5, zero_centered=bool(mode))
+        diff = (y.float() - ref.float()).abs()
+        ulp = ref.float().abs().clamp(min=1e-30) * 2.0 ** -6  # two bf16 ulps
+        assert (diff <= ulp + 1e-30).all(), mode
+        assert (diff == 0).float().mean().item() > 0.99, mode
+    y = ops.rms_norm(x, w, 1e-5)
+    _, q8, sc = ops.rms_norm(x, w, 1e-5, fp8=True)
+    oq, osc = OF.quantize_rows(y.cpu())
+    assert torch.equal(q8.float().cpu(), oq) and torch.allclose(sc.cpu(), osc.flatten())
