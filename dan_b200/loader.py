@@ -39,9 +39,62 @@ def read_state(path):
     return state
 
 
-def load(name, device="cuda", dtype=torch.bfloat16, quantization=None):
+def broadcast_state(state, device, src=0, group=None, bucket_bytes=256 << 20):
+    """Send a state dict from rank ``src`` to every rank of ``group`` (NCCL over NVLink for
+    CUDA devices, gloo for CPU): names, shapes and dtypes first, then the tensors packed into
+    byte buckets of about ``bucket_bytes``, one broadcast per bucket. Ranks other than ``src``
+    pass ``state=None``; every rank returns the full state on ``device``."""
+    import torch.distributed as dist
+
+    rank = dist.get_rank(group)
+    meta = [[(k, tuple(v.shape), str(v.dtype).replace("torch.", "")) for k, v in state.items()]] if rank == src else [None]
+    dist.broadcast_object_list(meta, src=src, group=group)
+    out = {}
+    bucket = []
+
+    def flush():
+        if not bucket:
+            return
+        nbytes = sum(n for _, _, _, n in bucket)
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        if rank == src:
+            off = 0
+            for k, _, _, n in bucket:
+                buf[off:off + n].copy_(state[k].contiguous().view(-1).view(torch.uint8))
+                off += n
+        dist.broadcast(buf, src=src, group=group)
+        off = 0
+        for k, shape, dt, n in bucket:
+            out[k] = buf[off:off + n].view(dt).view(shape).clone()
+            off += n
+        bucket.clear()
+
+    total = 0
+    for k, shape, dname in meta[0]:
+        dt = getattr(torch, dname)
+        n = math.prod(shape) * torch.empty(0, dtype=dt).element_size()
+        bucket.append((k, shape, dt, n))
+        total += n
+        if total >= bucket_bytes:
+            flush()
+            total = 0
+    flush()
+    return out
+
+
+def load(name, device="cuda", dtype=torch.bfloat16, quantization=None, group=None):
+    """Build the model of a local Hugging Face directory on ``device``. With a process group of
+    several ranks, only rank 0 reads the checkpoint; the others receive it by broadcast."""
     if not isinstance(name, str):
         return name  # an already-built model
+    if group is not None:
+        import torch.distributed as dist
+
+        rank = dist.get_rank(group)
+        config = [read_config(name) if rank == 0 else None]
+        dist.broadcast_object_list(config, src=0, group=group)
+        state = broadcast_state(read_state(name) if rank == 0 else None, device, group=group)
+        return arch_for(config[0])(config[0], state, device, dtype, quantization)
     if not os.path.isdir(name):
         raise FileNotFoundError(f"{name!r} is not a local model directory (no network access)")
     config = read_config(name)
