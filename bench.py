@@ -11,9 +11,11 @@ and lengths are seeded synthetic data (no dataset or checkpoint is used).
 
 ``value`` is prefill tokens/s over all ranks with the batch already resident
 in HBM (device timing with CUDA events, max over ranks). ``e2e`` is the same
-metric through the public API ``Runner.read_many`` from host plans: packing,
-pinned host->device upload of ids / positions / tables, the forward, and the
-device->host copy of every question's logits and probabilities, every step.
+metric through the public API ``Runner.read_stream`` (``read_many`` per batch,
+with the next batch packed while the device runs the current one) from host
+plans: packing, pinned host->device upload of ids / positions / tables, the
+forward, and the device->host copy of every question's logits and
+probabilities, every step.
 Each rank runs an independent replica on its own batches (weak scaling, no
 collective on the data path).
 
@@ -286,8 +288,8 @@ def run_dan(args, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall = time.perf_counter()
     e0.record()
-    for plans in batches[args.warmup:]:
-        runner.read_many(plans)
+    for _ in runner.read_stream(batches[args.warmup:]):  # one batch queued while the next is packed
+        pass
     e1.record()
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall

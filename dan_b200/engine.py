@@ -7,6 +7,12 @@ thread (``runner.read_many``; ctypes launches release the GIL) and resolves its
 requests' futures; a failing batch fails only its own requests; the queue is
 capped (``Overloaded``).
 
+Batches are pipelined per replica: with a runner that has ``submit`` (queue the
+batch on the device, return a handle whose ``result()`` waits), up to
+``in_flight`` batches are queued at once, so the host collects and packs the
+next batch while the device computes the current one. A runner with only
+``read_many`` runs one batch at a time.
+
 Difference: ``runner`` may be a list of runners, one per GPU, each with its own
 prefix pool and its own queue. A plan whose static prefix was routed before goes
 to the same replica (prefix affinity: its cached K/V or recurrent state lives
@@ -29,6 +35,18 @@ class Overloaded(RuntimeError):
     pass
 
 
+class _Done:
+    """The handle of a batch a ``read_many``-only runner has already read."""
+
+    __slots__ = ("value",)
+
+    def __init__(self, value):
+        self.value = value
+
+    def result(self):
+        return self.value
+
+
 @dataclass
 class Stats:
     requests: int = 0
@@ -44,7 +62,7 @@ class Stats:
 
 class AsyncEngine:
     def __init__(self, planner, runner, max_batch_tokens=8192, max_wait_ms=2.0, max_queue=1024,
-                 steal_after_ms=20.0, max_homes=65536):
+                 steal_after_ms=20.0, max_homes=65536, in_flight=2):
         self.planner = planner
         self.runners = list(runner) if isinstance(runner, (list, tuple)) else [runner]
         self.runner = self.runners[0]  # dan's /metrics reads engine.runner.cache
@@ -56,7 +74,9 @@ class AsyncEngine:
         n = len(self.runners)
         self._queues = [deque() for _ in range(n)]  # (plan, future, enqueue time, cost)
         self._queued = [0] * n  # tokens waiting per replica
-        self._busy = [False] * n
+        self._busy = [0] * n  # per replica: batches being collected or in flight
+        self._busy_since = [0.0] * n
+        self.in_flight = max(1, int(in_flight))
         self._homes = OrderedDict()  # static-prefix key -> replica
         self._arrived = asyncio.Event()
         self.affinity_hits = 0
@@ -148,7 +168,16 @@ class AsyncEngine:
         return item
 
     async def _loop(self, replica):
+        slots, finishing = asyncio.Semaphore(self.in_flight), set()
+        try:
+            await self._serve(replica, slots, finishing)
+        finally:
+            for task in list(finishing):
+                task.cancel()
+
+    async def _serve(self, replica, slots, finishing):
         while True:
+            await slots.acquire()  # at most ``in_flight`` batches queued on this replica
             while True:
                 self._arrived.clear()
                 src = self._source(replica)
@@ -160,7 +189,7 @@ class AsyncEngine:
                     pass
             batch = [self._pop(replica, src)]
             budget = batch[0][3]
-            self._busy[replica] = True  # collecting a batch counts as load for routing and stealing
+            self._mark_busy(replica, +1)  # collecting a batch counts as load for routing and stealing
             deadline = time.perf_counter() + self.max_wait
             while budget < self.max_batch_tokens:
                 src = self._source(replica)
@@ -174,34 +203,68 @@ class AsyncEngine:
                     break
                 batch.append(self._pop(replica, src))
                 budget += batch[-1][3]
+            handed_off = False
             try:
-                await self._run(replica, batch, budget)
+                pending = await self._submit(replica, batch)
+                if pending is not None:
+                    task = asyncio.get_running_loop().create_task(
+                        self._finish(replica, batch, budget, pending, slots))
+                    finishing.add(task)
+                    task.add_done_callback(finishing.discard)
+                    handed_off = True
             finally:
-                self._busy[replica] = False
-                self._arrived.set()  # a replica that just went idle may now be stolen from
+                if not handed_off:
+                    slots.release()
+                    self._mark_busy(replica, -1)
+                    self._arrived.set()
 
-    async def _run(self, replica, batch, tokens):
-        plans = [item[0] for item in batch]
-        st = self.replica_stats[replica]
-        t = time.perf_counter()
-        try:
-            logits = await asyncio.to_thread(self.runners[replica].read_many, plans)
-        except Exception as e:  # noqa: BLE001 - fail this batch's requests, keep serving
-            self.stats.errors += len(batch)
-            st.errors += len(batch)
-            for item in batch:
-                if not item[1].done():
-                    item[1].set_exception(e)
-            return
-        dt = time.perf_counter() - t
-        for s in (self.stats, st):
-            s.batches += 1
-            s.tokens += tokens
-            s.busy_s += dt
-            s.plans += len(batch)
-        for item, lg in zip(batch, logits):
+    def _mark_busy(self, replica, d):
+        """Count a batch in (+1) or out (-1); busy seconds add up the time with any batch busy."""
+        now = time.perf_counter()
+        if d > 0 and self._busy[replica] == 0:
+            self._busy_since[replica] = now
+        self._busy[replica] += d
+        if d < 0 and self._busy[replica] == 0:
+            dt = now - self._busy_since[replica]
+            self.stats.busy_s += dt
+            self.replica_stats[replica].busy_s += dt
+
+    def _fail(self, replica, batch, e):
+        self.stats.errors += len(batch)
+        self.replica_stats[replica].errors += len(batch)
+        for item in batch:
             if not item[1].done():
-                item[1].set_result(lg)
+                item[1].set_exception(e)
+
+    async def _submit(self, replica, batch):
+        """Queue ``batch`` on the replica's device; None if that failed (its requests fail)."""
+        runner, plans = self.runners[replica], [item[0] for item in batch]
+        try:
+            if hasattr(runner, "submit"):
+                return await asyncio.to_thread(runner.submit, plans)
+            return _Done(await asyncio.to_thread(runner.read_many, plans))
+        except Exception as e:  # noqa: BLE001 - fail this batch's requests, keep serving
+            self._fail(replica, batch, e)
+            return None
+
+    async def _finish(self, replica, batch, tokens, pending, slots):
+        try:
+            try:
+                logits = pending.result() if isinstance(pending, _Done) else await asyncio.to_thread(pending.result)
+            except Exception as e:  # noqa: BLE001 - fail this batch's requests, keep serving
+                self._fail(replica, batch, e)
+                return
+            for s in (self.stats, self.replica_stats[replica]):
+                s.batches += 1
+                s.tokens += tokens
+                s.plans += len(batch)
+            for item, lg in zip(batch, logits):
+                if not item[1].done():
+                    item[1].set_result(lg)
+        finally:
+            slots.release()
+            self._mark_busy(replica, -1)
+            self._arrived.set()  # a replica that just went idle may now be stolen from
 
     def metrics(self):
         """Prometheus-style rows (dan/entrypoints/api_server.py:137-147) plus one set per replica."""

@@ -40,8 +40,8 @@ class LLM:
         flat = [p for g in groups for p in g]
         step = batch_size or len(flat) or 1
         reads = []
-        for i in range(0, len(flat), step):
-            reads += self.runner.read_many(flat[i:i + step])
+        for out in self.runner.read_stream(flat[i:i + step] for i in range(0, len(flat), step)):
+            reads += out
         out, k = [], 0
         for g in groups:
             out.append(combine(g, reads[k:k + len(g)]))

@@ -10,6 +10,8 @@ pages and computes only the rest of its prompt.
 segments, read rows, stores); ``forward`` uploads one batch, runs the model,
 and reads every question's label logits and probabilities with one fused
 readout kernel; ``read_many`` copies them to the host once per batch.
+``submit`` / ``read_stream`` keep a batch queued on the device while the host
+packs the next one.
 """
 import numpy as np
 import torch
@@ -128,20 +130,42 @@ class Runner:
         return self._split(plans, flat)
 
     @torch.inference_mode()
+    def submit(self, plans, probabilities=False):
+        """Queue one batch: pack, upload, forward and the copy of its results into pinned
+        host memory are all issued on the device's current stream without waiting for
+        it; ``PendingRead.result()`` waits. Batches submitted back to back run in order,
+        so the host packs the next batch while the device computes this one."""
+        with torch.cuda.device(self.device):
+            logits, probs, offsets = self.forward_flat(plans)
+            stream = torch.cuda.current_stream(self.device)
+            status = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            status.copy_(_lib.status_word(self.device), non_blocking=True)
+            if logits.numel():
+                host = torch.empty(2, logits.numel(), dtype=torch.float32, pin_memory=True)
+                host.copy_(torch.stack([logits, probs]), non_blocking=True)
+            else:
+                host = torch.zeros(2, 0)
+            done = torch.cuda.Event()
+            done.record(stream)
+        return PendingRead(self, plans, host, status, offsets, done, probabilities)
+
     def read_many(self, plans, probabilities=False):
         """Per plan, per branch: the logits of its label tokens (fp32, CPU), from one
         device-to-host copy per batch; with ``probabilities`` also the softmax of each.
         Runs on this runner's device whatever the calling thread's current device is."""
-        with torch.cuda.device(self.device):
-            logits, probs, offsets = self.forward_flat(plans)
-            both = torch.stack([logits, probs]).cpu() if logits.numel() else torch.zeros(2, 0)
-            _lib.check_status(self.device)
-        lg = [both[0, offsets[i]:offsets[i + 1]] for i in range(len(offsets) - 1)]
-        out = self._split(plans, lg)
-        if probabilities:
-            pr = [both[1, offsets[i]:offsets[i + 1]] for i in range(len(offsets) - 1)]
-            return out, self._split(plans, pr)
-        return out
+        return self.submit(plans, probabilities).result()
+
+    def read_stream(self, batches, probabilities=False):
+        """``read_many`` over an iterable of batches, yielding each batch's result in
+        order while the next batch is already queued on the device (one in flight)."""
+        pending = None
+        for plans in batches:
+            nxt = self.submit(plans, probabilities)
+            if pending is not None:
+                yield pending.result()
+            pending = nxt
+        if pending is not None:
+            yield pending.result()
 
     @staticmethod
     def _split(plans, flat):
@@ -154,3 +178,34 @@ class Runner:
 
     def read(self, plan):
         return self.read_many([plan])[0]
+
+
+class PendingRead:
+    """A submitted batch (``Runner.submit``): its results land in pinned host memory when
+    the device reaches them. ``result()`` waits for that point only (not for batches
+    queued after it), raises if a kernel of the device reported an error, and returns
+    what ``read_many`` returns."""
+
+    __slots__ = ("runner", "plans", "host", "status", "offsets", "done", "probabilities")
+
+    def __init__(self, runner, plans, host, status, offsets, done, probabilities):
+        self.runner, self.plans, self.host, self.status = runner, plans, host, status
+        self.offsets, self.done, self.probabilities = offsets, done, probabilities
+
+    def ready(self):
+        return self.done.query()
+
+    def result(self):
+        self.done.synchronize()
+        v = int(self.status[0])
+        if v:
+            with torch.cuda.device(self.runner.device):
+                _lib.status_word(self.runner.device).zero_()
+            raise RuntimeError(f"dan_b200 kernel error {v}: {_lib.STATUS_TEXT.get(v, 'unknown')}")
+        both, off, plans = self.host, self.offsets, self.plans
+        lg = [both[0, off[i]:off[i + 1]] for i in range(len(off) - 1)]
+        out = Runner._split(plans, lg)
+        if self.probabilities:
+            pr = [both[1, off[i]:off[i + 1]] for i in range(len(off) - 1)]
+            return out, Runner._split(plans, pr)
+        return out

@@ -207,3 +207,72 @@ def test_idle_replica_steals_a_backlog_from_a_busy_one():
     assert len(res) == 12 and all(isinstance(r, tuple) for r in res)
     assert runners[1].calls > 0 and eng.replica_stats[1].stolen > 0
     assert sum(rs.plans for rs in eng.replica_stats) == 12
+
+
+class PipelinedRunner(FakeRunner):
+    """A runner with the two-phase interface: ``submit`` returns at once and its handle's
+    ``result`` returns ``delay`` seconds after the previous batch's (a device that runs the
+    queued batches in order); records how many batches were outstanding at most."""
+
+    def __init__(self, fail_on=(), delay=0.0):
+        super().__init__(fail_on=fail_on, delay=delay)
+        self.outstanding = self.max_outstanding = 0
+        self.ready_at = 0.0
+
+    def submit(self, plans):
+        import time
+
+        with self.lock:
+            self.calls += 1
+            n = self.calls
+            self.outstanding += 1
+            self.max_outstanding = max(self.max_outstanding, self.outstanding)
+            self.ready_at = max(time.perf_counter(), self.ready_at) + self.delay
+            done_at = self.ready_at
+        value = FakeRunner(delay=0.0).read_many(plans)
+        runner = self
+
+        class Handle:
+            def result(self):
+                time.sleep(max(0.0, done_at - time.perf_counter()))
+                with runner.lock:
+                    runner.outstanding -= 1
+                if n in runner.fail_on:
+                    raise RuntimeError(f"injected failure on batch {n}")
+                return value
+
+        return Handle()
+
+
+@pytest.mark.parametrize("in_flight", [1, 2, 3])
+def test_pipelined_batches_stay_bounded_and_answer_like_solo_reads(in_flight):
+    """With a two-phase runner the engine queues up to ``in_flight`` batches at once (the host
+    packs the next batch while the device runs one); answers equal solo reads, a failing batch
+    fails only its own requests, and busy seconds count overlapping batches once."""
+    import time
+
+    runner = PipelinedRunner(fail_on={3}, delay=0.01)
+    eng = AsyncEngine(FakePlanner(), runner, max_batch_tokens=40, max_wait_ms=1, in_flight=in_flight)
+
+    async def main():
+        states = [f"p{i}" * 5 for i in range(24)]
+        t0 = time.perf_counter()
+        res = await asyncio.gather(*[eng.decide(s, QUESTIONS) for s in states], return_exceptions=True)
+        wall = time.perf_counter() - t0
+        await eng.stop()
+        return states, res, wall
+
+    states, res, wall = run(main())
+    assert 1 <= runner.max_outstanding <= in_flight
+    if in_flight > 1:
+        assert runner.max_outstanding == in_flight  # the 24 requests keep the pipeline full
+    failed = [r for r in res if isinstance(r, Exception)]
+    assert failed and all("injected failure on batch 3" in str(e) for e in failed)
+    assert eng.stats.errors == len(failed) and eng.stats.batches == runner.calls - 1
+    for s, r in zip(states, res):
+        if isinstance(r, Exception):
+            continue
+        plan = FakePlanner().plans(s, QUESTIONS)[0]
+        assert r[0] == readout.answers(plan, FakeRunner().read_many([plan])[0])
+    assert 0 < eng.stats.busy_s <= wall + 1e-3
+    assert runner.outstanding == 0

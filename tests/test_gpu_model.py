@@ -66,3 +66,21 @@ def test_tiny_llama_fp8_matches_fp8_oracle(cuda, tiny_dir):
         for p, w in zip(pp, ww):
             worst = max(worst, (p - torch.softmax(w.double(), 0).float()).abs().max().item())
     assert worst < 3e-2, worst
+
+
+def test_read_stream_matches_read_many(cuda, tiny_dir):
+    """``read_stream`` keeps one batch queued on the device while the host packs the next;
+    each batch's results are bit-identical to a lone ``read_many`` of that batch, and a
+    submitted batch's handle waits only for its own results."""
+    path, g = tiny_dir
+    runner = Runner(path, cuda, cache_bytes=0)
+    batches = [plans_from_json(b["plans"]) for b in g["batches"]] * 2
+    solo = [runner.read_many(p, probabilities=True) for p in batches]
+    streamed = list(runner.read_stream(batches, probabilities=True))
+    assert len(streamed) == len(solo)
+    for (lg_s, pr_s), (lg_a, pr_a) in zip(streamed, solo):
+        for a, b in zip(lg_s + pr_s, lg_a + pr_a):
+            assert len(a) == len(b) and all(torch.equal(x, y) for x, y in zip(a, b))
+    first, second = runner.submit(batches[0]), runner.submit(batches[1])
+    assert second.result() is not None and first.ready()  # in-order device queue
+    assert all(torch.equal(x, y) for x, y in zip(first.result()[0], solo[0][0][0]))
