@@ -393,7 +393,11 @@ struct PairCfg {
   static constexpr int CHUNKS = D / 64;
   static constexpr int Q_BYTES = CHUNKS * CHUNK;
   static constexpr int KV_BYTES = CHUNKS * CHUNK;
-  static constexpr int SMEM_USED = 2 * Q_BYTES + 2 * NS * KV_BYTES + 1024 + 512;
+  // Output staging: per softmax warp two 2 KB slots (32 rows x 32 bf16 columns each), written
+  // with the 64-byte swizzle and sent by TMA store.
+  static constexpr int SLOT_BYTES = 32 * 64;
+  static constexpr int SINK_BYTES = 8 * 2 * SLOT_BYTES;
+  static constexpr int SMEM_USED = 2 * Q_BYTES + 2 * NS * KV_BYTES + SINK_BYTES + 1024 + 512;
   static constexpr int SMEM = SMEM_USED < 120 * 1024 ? 120 * 1024 : SMEM_USED;
   static constexpr int THREADS = 320;
 };
@@ -530,7 +534,8 @@ template <int D>
 __global__ void __launch_bounds__(320, 1)
     tree_attention_pair_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                                const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tpk,
-                               const __grid_constant__ CUtensorMap tpv, Params p, int n_items) {
+                               const __grid_constant__ CUtensorMap tpv, const __grid_constant__ CUtensorMap to,
+                               Params p, int n_items) {
   using C = PairCfg<D>;
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
@@ -538,7 +543,8 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sq = smem;  // [2][Q_BYTES]
   uint8_t* sk = sq + 2 * C::Q_BYTES;
   uint8_t* sv = sk + NS * C::KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + NS * C::KV_BYTES);
+  uint8_t* sink = sv + NS * C::KV_BYTES;  // 1024-byte aligned: Q and K/V stages are multiples of 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sink + C::SINK_BYTES);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + 1;
   uint64_t* k_full = q_empty + 1;
@@ -715,6 +721,8 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t s_addr = tmem + lane_base + hsel * 128;
     const uint32_t o_addr = tmem + lane_base + 256 + hsel * D;
     const float sl2 = p.scale_log2;
+    uint8_t* slots = sink + (warp - 2) * 2 * C::SLOT_BYTES;
+    uint32_t sent = 0;  // output chunks this warp has sent by TMA store (slot = sent & 1)
     uint32_t gb = 0;
     bool ok = true;
     for (int kw = 0; ok; ++kw) {
@@ -824,17 +832,39 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
+        // A warp whose 32 rows all belong to the tile sends each 32-column chunk through a
+        // shared-memory slot by TMA store (whole lines, no per-row stores); the warp holding a
+        // segment's ragged last rows stores its valid rows directly.
+        const bool slab = (sub + 1) * 32 <= tile.nrows;
         __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
           uint32_t o[32];
           tmem_ld32(o_addr + c, o);
           tmem_wait_ld();
-          if (valid) {
-            uint32_t pkd[16];
+          uint32_t pkd[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          for (int i = 0; i < 16; ++i)
+            pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          if (slab) {
+            uint8_t* slot = slots + (sent & 1) * C::SLOT_BYTES;
+            if (lane == 0) bulk_wait_read<1>();  // the store sent from this slot two chunks ago has read it
+            __syncwarp();
+            // 64-byte swizzle: 16-byte unit u of row r sits at unit u ^ ((r >> 1) & 3)
+            uint4* d4 = reinterpret_cast<uint4*>(slot + lane * 64);
+            const int sw = (lane >> 1) & 3;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i ^ sw] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&to, slot, c, head, tile.row0 + sub * 32);
+              bulk_commit();
+            }
+            __syncwarp();
+            ++sent;
+          } else if (valid) {
             uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
             for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
@@ -846,6 +876,7 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) mbar_arrive(&o_free[hsel]);
       gb += nblk;
     }
+    if (lane == 0) bulk_wait_all();  // output stores done before the CTA's shared memory goes away
     tc_fence_before();
   }
   __syncwarp();
@@ -858,7 +889,7 @@ __global__ void __launch_bounds__(320, 1)
 
 template <int D>
 int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tpk,
-                const CUtensorMap& tpv, const Params& p, int n_tiles, cudaStream_t stream) {
+                const CUtensorMap& tpv, const CUtensorMap& to, const Params& p, int n_tiles, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     DAN_CUDA(cudaFuncSetAttribute(tree_attention_pair_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -867,8 +898,8 @@ int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
   }
   const int items = n_tiles * (p.n_heads / 2);
   const int grid = p.sched ? p.sched_ctas : (items < sm_count() ? items : sm_count());
-  tree_attention_pair_kernel<D><<<grid, PairCfg<D>::THREADS, PairCfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, p,
-                                                                                        items);
+  tree_attention_pair_kernel<D><<<grid, PairCfg<D>::THREADS, PairCfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, to,
+                                                                                        p, items);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }
@@ -879,6 +910,15 @@ static int rows_map(CUtensorMap* m, const void* base, int64_t row_stride, int64_
   uint64_t strides[2] = {static_cast<uint64_t>(head_stride) * 2, static_cast<uint64_t>(row_stride) * 2};
   uint32_t box[3] = {64, 1, 128};
   return make_tmap(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Output of the paired-head kernel: 32 columns x 1 head x 32 rows per store, 64-byte swizzle.
+static int out_map(CUtensorMap* m, const void* base, int64_t row_stride, int64_t head_stride, int heads, int rows,
+                   int d) {
+  uint64_t dims[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(heads), static_cast<uint64_t>(rows)};
+  uint64_t strides[2] = {static_cast<uint64_t>(head_stride) * 2, static_cast<uint64_t>(row_stride) * 2};
+  uint32_t box[3] = {32, 1, 32};
+  return make_tmap(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 }  // namespace attn
@@ -930,8 +970,12 @@ DAN_API int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, con
   p.sched_ctas = sched_ctas;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool paired = (n_heads / n_kv_heads) % 2 == 0 && head_dim <= 128;
-  if (paired) return head_dim == 64 ? attn::launch_pair<64>(tq, tk, tv, tpk, tpv, p, n_tiles, s)
-                                    : attn::launch_pair<128>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
+  if (paired) {
+    CUtensorMap to;
+    if ((rc = attn::out_map(&to, out, out_row, out_head, n_heads, n_rows, head_dim))) return rc;
+    return head_dim == 64 ? attn::launch_pair<64>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s)
+                          : attn::launch_pair<128>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s);
+  }
   switch (head_dim) {
     case 64:
       return attn::launch<64>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
