@@ -7,7 +7,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from dan_b200 import ops
+from dan_b200 import _lib, ops
 from oracle import fp8 as OF
 
 pytestmark = pytest.mark.gpu
@@ -237,6 +237,26 @@ def test_kv_store(cuda):
     dst = torch.tensor([130, 131, 132], dtype=torch.int32, device=cuda)
     ops.kv_store(k, v, pk, pv, src, dst)
     assert torch.equal(pk[130:133], k[3:6]) and torch.equal(pv[130:133], v[3:6])
+
+
+@pytest.mark.parametrize("rows,cols,heads", [(4001, 4096, 1), (2900, 8192, 1), (3000, 2560, 1), (1200, 2048, 3),
+                                             (5, 4096, 1)])
+def test_rms_norm_stream_rows(cuda, rows, cols, heads):
+    """Hidden-size rows (128 threads per row): thousands of rows, a strided [n, heads, cols] view
+    (rows r / heads, r % heads) and a handful of rows all give the reference's rounding."""
+    g = torch.Generator(device=cuda).manual_seed(rows + cols)
+    n = rows // heads
+    base = torch.randn(n, heads + 1, cols, device=cuda, generator=g).bfloat16()
+    x = base[:, :heads, :]  # rows of the view are not contiguous when heads > 1
+    w = (1 + 0.1 * torch.randn(cols, device=cuda, generator=g)).bfloat16()
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)
+    ref = (w.float() * (xf * inv).bfloat16().float()).bfloat16()
+    y = ops.rms_norm(x, w, 1e-6)
+    diff = (y.float() - ref.float()).abs()
+    assert (diff <= ref.float().abs() * 2.0 ** -6 + 1e-30).all()
+    assert (diff == 0).float().mean().item() > 0.99
+    _lib.check_status(cuda)
 
 
 @pytest.mark.parametrize("cols", [4096, 2560])
