@@ -241,7 +241,7 @@ def test_kv_store(cuda):
 
 @pytest.mark.parametrize("rows,cols,heads", [(4001, 4096, 1), (2900, 8192, 1), (3000, 2560, 1), (1200, 2048, 3),
                                              (5, 4096, 1)])
-def test_rms_norm_stream_rows(cuda, rows, cols, heads):
+def test_rms_norm_hidden_rows(cuda, rows, cols, heads):
     """Hidden-size rows (128 threads per row): thousands of rows, a strided [n, heads, cols] view
     (rows r / heads, r % heads) and a handful of rows all give the reference's rounding."""
     g = torch.Generator(device=cuda).manual_seed(rows + cols)
