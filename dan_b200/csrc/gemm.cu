@@ -113,6 +113,27 @@ struct PairWork {
   }
 };
 
+// e4m3 epilogues: scale the 32 accumulators of one chunk in place by a_scale[row] *
+// w_scale[col + i] (0 past n) before the element loop: eight 16-byte loads of the scales when
+// the chunk is whole and aligned (one uniform branch per chunk, none per element).
+__device__ __forceinline__ void scale_chunk(const Params& p, int col, float as, uint32_t (&r)[32]) {
+  if (col + 32 <= p.n && (reinterpret_cast<uintptr_t>(p.w_scale + col) & 15) == 0) {
+    const float4* w4 = reinterpret_cast<const float4*>(p.w_scale + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(w4 + j);
+      r[4 * j] = __float_as_uint(__uint_as_float(r[4 * j]) * (as * w.x));
+      r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) * (as * w.y));
+      r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) * (as * w.z));
+      r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) * (as * w.w));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      r[i] = __float_as_uint(__uint_as_float(r[i]) * (as * (col + i < p.n ? p.w_scale[col + i] : 0.f)));
+  }
+}
+
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <bool FP8>
@@ -248,6 +269,7 @@ __device__ __forceinline__ void residual_tma(Sink& o, const Params& p, uint32_t 
     }
     __syncwarp();
     tmem_wait_ld_regs(r);
+    if (FP8) scale_chunk(p, col, as, r);
     if (!mbar_wait(&o.bar[s], (o.phase >> s) & 1u)) report(p.status, kTimeoutFull);
     o.phase ^= 1u << s;
     uint4* slot = reinterpret_cast<uint4*>(o.stage + s * SLOT_BYTES + o.lane * 64);
@@ -259,10 +281,6 @@ __device__ __forceinline__ void residual_tma(Sink& o, const Params& p, uint32_t 
       for (int j = 0; j < 4; ++j) {
         const int c = 8 * g + 2 * j;
         float x0 = __uint_as_float(r[c]), x1 = __uint_as_float(r[c + 1]);
-        if (FP8) {
-          x0 *= as * (col + c < p.n ? p.w_scale[col + c] : 0.f);
-          x1 *= as * (col + c + 1 < p.n ? p.w_scale[col + c + 1] : 0.f);
-        }
         if (p.bias) {
           x0 += col + c < p.n ? __bfloat162float(p.bias[col + c]) : 0.f;
           x1 += col + c + 1 < p.n ? __bfloat162float(p.bias[col + c + 1]) : 0.f;
@@ -311,13 +329,13 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
       tmem_wait_ld();
       float v[32];
       const int gcol = tn * BN + c, ucol = tn * BN + BN / 2 + c;
+      if (FP8) {
+        scale_chunk(p, gcol, as, g);
+        scale_chunk(p, ucol, as, u);
+      }
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
-        if (FP8) {
-          gv *= as * (gcol + i < p.n ? p.w_scale[gcol + i] : 0.f);
-          uv *= as * (ucol + i < p.n ? p.w_scale[ucol + i] : 0.f);
-        }
         if (p.bias) {
           gv += gcol + i < p.n ? __bfloat162float(p.bias[gcol + i]) : 0.f;
           uv += ucol + i < p.n ? __bfloat162float(p.bias[ucol + i]) : 0.f;
@@ -333,33 +351,37 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
     // rounding points, bf16(bf16(a cos) + bf16(-b sin)) (llama.py:43-45); v heads: plain.
     const int hd = p.rope_hd, half = hd / 2;
     const int trow = row < p.m ? row : 0;
+    // Every head of the tile rotates by the same per-row angles: each 32-column slice of this
+    // row's cos / sin is loaded once and used for all the tile's heads.
+    const bool any_rot = tn * BN + hd <= p.rope_cols;
 #pragma unroll 1
-    for (int h0 = 0; h0 < BN; h0 += hd) {
-      const int hc = tn * BN + h0;
-      if (hc >= p.n) break;
+    for (int c = 0; c < half; c += 32) {
+      float ct[32], st[32];
+      if (any_rot) {  // 32 consecutive cos / sin of this row: 8 + 8 16-byte loads
+        const float4* c4 = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(trow) * half + c);
+        const float4* s4 = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(trow) * half + c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 cv = c4[i], sv = s4[i];
+          ct[4 * i] = cv.x, ct[4 * i + 1] = cv.y, ct[4 * i + 2] = cv.z, ct[4 * i + 3] = cv.w;
+          st[4 * i] = sv.x, st[4 * i + 1] = sv.y, st[4 * i + 2] = sv.z, st[4 * i + 3] = sv.w;
+        }
+      }
 #pragma unroll 1
-      for (int c = 0; c < half; c += 32) {
+      for (int h0 = 0; h0 < BN; h0 += hd) {
+        const int hc = tn * BN + h0;
+        if (hc >= p.n) break;
         uint32_t ra[32], rb[32];
         tmem_ld32(taddr + h0 + c, ra);
         tmem_ld32(taddr + h0 + half + c, rb);
         tmem_wait_ld();
         float va[32], vb[32];
         const bool rot = hc + hd <= p.rope_cols;
-        float ct[32], st[32];
-        if (rot) {  // 32 consecutive cos / sin of this row: 8 + 8 16-byte loads
-          const float4* c4 = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(trow) * half + c);
-          const float4* s4 = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(trow) * half + c);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 cv = c4[i], sv = s4[i];
-            ct[4 * i] = cv.x, ct[4 * i + 1] = cv.y, ct[4 * i + 2] = cv.z, ct[4 * i + 3] = cv.w;
-            st[4 * i] = sv.x, st[4 * i + 1] = sv.y, st[4 * i + 2] = sv.z, st[4 * i + 3] = sv.w;
-          }
-        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float a = __uint_as_float(ra[i]), b = __uint_as_float(rb[i]);
-          if (FP8) {
+          if (FP8) {  // per element here: the cos / sin held across the tile's heads leave no
+                      // registers for a chunk of scales
             a *= as * p.w_scale[hc + c + i];
             b *= as * p.w_scale[hc + half + c + i];
           }
@@ -396,11 +418,11 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
       uint32_t r[32];
       tmem_ld32(taddr + c, r);
       tmem_wait_ld();
+      if (FP8) scale_chunk(p, col, as, r);
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         float x = __uint_as_float(r[i]);
-        if (FP8) x *= as * (col + i < p.n ? p.w_scale[col + i] : 0.f);
         if (p.bias && col + i < p.n) x += __bfloat162float(p.bias[col + i]);
         v[i] = x;
       }
