@@ -20,6 +20,8 @@
 // chunk in the WY form on the tensor cores (see chunk_scan_kernel).
 #include "common.cuh"
 
+#include <type_traits>
+
 namespace dan {
 namespace delta {
 
@@ -732,6 +734,44 @@ __global__ void gated_rms_norm_kernel(const __nv_bfloat16* x, int64_t ldx, const
   }
 }
 
+// Vector form for dv = 4 V (V = 1, 2): lane l holds elements [4 V l, 4 V l + 4 V) of its (row,
+// head) in registers from one 8 V-byte load of x and of z, so x is read once.
+template <int V>
+__global__ void gated_rms_norm_vec_kernel(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* z, int64_t ldz,
+                                          const __nv_bfloat16* w, float eps, __nv_bfloat16* y, int64_t ldy, int rows,
+                                          int heads) {
+  using Vec = typename std::conditional<V == 1, uint2, uint4>::type;
+  constexpr int E = 4 * V, DV = 32 * E;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * heads) return;
+  const int r = gw / heads, h = gw % heads;
+  const int64_t off = h * DV + lane * E;
+  const Vec xv = *reinterpret_cast<const Vec*>(x + static_cast<int64_t>(r) * ldx + off);
+  const Vec zv = *reinterpret_cast<const Vec*>(z + static_cast<int64_t>(r) * ldz + off);
+  const Vec wv = *reinterpret_cast<const Vec*>(w + lane * E);
+  const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+  const __nv_bfloat16* ze = reinterpret_cast<const __nv_bfloat16*>(&zv);
+  const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    const float f = __bfloat162float(xe[i]);
+    ss += f * f;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / DV + eps);
+  Vec yv;
+  __nv_bfloat16* ye = reinterpret_cast<__nv_bfloat16*>(&yv);
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    const float t = bf16_round(__bfloat162float(we[i]) * bf16_round(__bfloat162float(xe[i]) * inv));
+    ye[i] = __float2bfloat16_rn(t * silu(__bfloat162float(ze[i])));
+  }
+  *reinterpret_cast<Vec*>(y + static_cast<int64_t>(r) * ldy + off) = yv;
+}
+
 }  // namespace delta
 }  // namespace dan
 
@@ -827,6 +867,22 @@ DAN_API int dan_gated_rms_norm(const void* x, int64_t ldx, const void* z, int64_
                                void* y, int64_t ldy, int rows, int heads, int dv, void* stream) {
   if (!rows) return 0;
   const int64_t warps = static_cast<int64_t>(rows) * heads;
+  const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if ((dv == 128 || dv == 256) && a16(x) && a16(z) && a16(w) && a16(y) && ldx % 8 == 0 && ldz % 8 == 0 &&
+      ldy % 8 == 0) {
+    const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dv == 128)
+      delta::gated_rms_norm_vec_kernel<1><<<grid, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(z), ldz,
+          static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
+    else
+      delta::gated_rms_norm_vec_kernel<2><<<grid, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(z), ldz,
+          static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
+    DAN_CUDA(cudaGetLastError());
+    return 0;
+  }
   delta::gated_rms_norm_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0,
                                  static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(z), ldz,

@@ -316,6 +316,28 @@ __global__ void sigmoid_gate_kernel(__nv_bfloat16* o, int64_t ldo, const __nv_bf
   o[static_cast<int64_t>(r) * ldo + c] = __float2bfloat16_rn(ov * (1.f / (1.f + __expf(-gv))));
 }
 
+// Vector form: one thread per 8 consecutive columns of a head (16-byte loads and store); used
+// when rows, heads and strides are 16-byte aligned.
+__global__ void sigmoid_gate_vec_kernel(__nv_bfloat16* o, int64_t ldo, const __nv_bfloat16* g, int64_t ldg,
+                                        int64_t g_head_stride, int head_dim, int rows, int cols) {
+  const int vcols = cols / 8;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(rows) * vcols) return;
+  const int r = static_cast<int>(idx / vcols), c = static_cast<int>(idx % vcols) * 8;
+  uint4* op = reinterpret_cast<uint4*>(o + static_cast<int64_t>(r) * ldo + c);
+  const uint4 gv = *reinterpret_cast<const uint4*>(g + static_cast<int64_t>(r) * ldg + (c / head_dim) * g_head_stride +
+                                                   c % head_dim);
+  uint4 ov = *op;
+  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 gf = __bfloat1622float2(g2[i]), of = __bfloat1622float2(o2[i]);
+    o2[i] = __floats2bfloat162_rn(of.x * (1.f / (1.f + __expf(-gf.x))), of.y * (1.f / (1.f + __expf(-gf.y))));
+  }
+  *op = ov;
+}
+
 // ---------------------------------------------------------------- prefix K/V page store
 // Copies rows src_rows[i] of k/v ([rows, heads, d] strided) to pool rows dst_rows[i].
 __global__ void kv_store_kernel(const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t ld_row, int64_t ld_head,
@@ -529,6 +551,17 @@ DAN_API int dan_rope(void* x, int64_t ld_row, int64_t ld_head, int heads, int he
 DAN_API int dan_sigmoid_gate(void* o, int64_t ldo, const void* g, int64_t ldg, int64_t g_head_stride, int head_dim,
                              int rows, int cols, void* stream) {
   if (!rows) return 0;
+  const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (a16(o) && a16(g) && cols % 8 == 0 && head_dim % 8 == 0 && ldo % 8 == 0 && ldg % 8 == 0 &&
+      g_head_stride % 8 == 0) {
+    const int64_t nv = static_cast<int64_t>(rows) * (cols / 8);
+    ew::sigmoid_gate_vec_kernel<<<static_cast<unsigned>((nv + 255) / 256), 256, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(g), ldg, g_head_stride, head_dim, rows,
+        cols);
+    DAN_CUDA(cudaGetLastError());
+    return 0;
+  }
   const int64_t n = static_cast<int64_t>(rows) * cols;
   ew::sigmoid_gate_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<__nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(g), ldg, g_head_stride, head_dim, rows,

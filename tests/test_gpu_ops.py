@@ -282,3 +282,42 @@ def test_rms_norm_wide_rounding(cuda, cols):
     _, q8, sc = ops.rms_norm(x, w, 1e-5, fp8=True)
     oq, osc = OF.quantize_rows(y.cpu())
     assert torch.equal(q8.float().cpu(), oq) and torch.allclose(sc.cpu(), osc.flatten())
+
+
+@pytest.mark.parametrize("aligned", [True, False])
+def test_sigmoid_gate(cuda, aligned):
+    """o *= sigmoid(gate) in place (fused.py:64-66), the gate read from a per-head [q | gate] layout
+    (strided rows and heads); the 16-byte path and, for an unaligned gate view, the scalar path."""
+    g = torch.Generator(device=cuda).manual_seed(7)
+    n, h, d = 777, 16, 256
+    proj = torch.randn(n, h, 2 * d + (0 if aligned else 1), device=cuda, generator=g).bfloat16()
+    gate = proj[:, :, d:2 * d] if aligned else proj[:, :, d + 1:2 * d + 1]
+    o = torch.randn(n, h * d, device=cuda, generator=g).bfloat16()
+    ref = (o.float() * torch.sigmoid(gate.reshape(n, h * d).float())).bfloat16()
+    ops.sigmoid_gate_(o, gate, d)
+    diff = (o.float() - ref.float()).abs()
+    assert (diff <= ref.float().abs() * 2.0 ** -7 + 1e-30).all()
+    assert (diff == 0).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("dv", [128, 256, 64])
+def test_gated_rms_norm(cuda, dv):
+    """y = bf16(bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) * silu(z)) per (row, head) (fused.py:51-56):
+    dv 128 / 256 take the vector kernel, 64 the per-element one; z is a strided view."""
+    g = torch.Generator(device=cuda).manual_seed(dv)
+    n, h = 1001, 8
+    x = torch.randn(n, h * dv, device=cuda, generator=g).bfloat16()
+    zbuf = torch.randn(n, 2 * h * dv, device=cuda, generator=g).bfloat16()
+    z = zbuf[:, h * dv:]
+    w = (1 + 0.1 * torch.randn(dv, device=cuda, generator=g)).bfloat16()
+    y = torch.empty_like(x)
+    _lib.call("dan_gated_rms_norm", _lib.ptr(x), x.stride(0), _lib.ptr(z), z.stride(0), _lib.ptr(w), 1e-6,
+              _lib.ptr(y), y.stride(0), n, h, dv, _lib.stream())
+    xf = x.float().view(n, h, dv)
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)
+    t = (w.float() * (xf * inv).bfloat16().float()).bfloat16().float()
+    zf = z.float().reshape(n, h, dv)
+    ref = (t * zf * torch.sigmoid(zf)).bfloat16().view(n, h * dv)
+    diff = (y.float() - ref.float()).abs()
+    assert (diff <= ref.float().abs() * 2.0 ** -6 + 1e-30).all()
+    assert (diff == 0).float().mean().item() > 0.98
