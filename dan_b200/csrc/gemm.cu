@@ -134,6 +134,23 @@ __device__ __forceinline__ void scale_chunk(const Params& p, int col, float as, 
   }
 }
 
+// e4m3: the tile's 256 weight scales, lane l holding columns l, l + 32, ... (loaded before the
+// epilogue waits for the accumulator, so their latency hides behind the main loop), and the
+// register of 32-column group k (uniform) for a broadcast by shuffle.
+__device__ __forceinline__ void load_tile_scales(const Params& p, int tn, int lane, float (&ws)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int col = tn * BN + 32 * j + lane;
+    ws[j] = col < p.n ? p.w_scale[col] : 0.f;
+  }
+}
+__device__ __forceinline__ float pick8(const float (&w)[8], int k) {
+  float r = w[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) r = k == j ? w[j] : r;
+  return r;
+}
+
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <bool FP8>
@@ -317,7 +334,8 @@ __device__ __forceinline__ void epilogue_prefetch(const Params& p, int row, int 
 // The fused epilogue of one 128-row x 256-column accumulator tile held in TMEM at ``taddr``
 // (this warp's lanes): ``row`` is this thread's output row, ``tn`` the tile's column block.
 template <bool FP8>
-__device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t taddr, int row, int tn) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t taddr, int row, int tn,
+                                              const float (&ws)[8]) {
   const int cols_out = p.epilogue == kSwiglu ? p.n / 2 : p.n;
   const float as = (FP8 && row < p.m) ? p.a_scale[row] : 1.f;
   if (p.epilogue == kSwiglu) {
@@ -377,13 +395,13 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
         tmem_wait_ld();
         float va[32], vb[32];
         const bool rot = hc + hd <= p.rope_cols;
+        const float wa = FP8 ? pick8(ws, (h0 + c) >> 5) : 0.f, wb = FP8 ? pick8(ws, (h0 + half + c) >> 5) : 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float a = __uint_as_float(ra[i]), b = __uint_as_float(rb[i]);
-          if (FP8) {  // per element here: the cos / sin held across the tile's heads leave no
-                      // registers for a chunk of scales
-            a *= as * p.w_scale[hc + c + i];
-            b *= as * p.w_scale[hc + half + c + i];
+          if (FP8) {  // scales by shuffle from the tile's prefetched scales
+            a *= as * __shfl_sync(0xffffffffu, wa, i);
+            b *= as * __shfl_sync(0xffffffffu, wb, i);
           }
           if (p.bias) {
             a += __bfloat162float(p.bias[hc + c + i]);
@@ -543,6 +561,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int tm = t % p.tiles_m, tn = t / p.tiles_m;
       epilogue_prefetch(p, tm * BM + r_in, tn);
+      float ws[8];
+      if (FP8) load_tile_scales(p, tn, lane, ws);
       if (!mbar_wait(&tfull[buf], acc_phase)) {
         report(p.status, kTimeoutMma);
         break;
@@ -551,7 +571,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = tm * BM + r_in;
       o.row0 = tm * BM + sub * 32;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
-      epilogue_tile<FP8>(p, o, taddr, row, tn);
+      epilogue_tile<FP8>(p, o, taddr, row, tn, ws);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -763,6 +783,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       int tm, tn;
       pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
       if (kb == 0) epilogue_prefetch(p, tm * 256 + static_cast<int>(rank) * 128 + r_in, tn);
+      float ws[8];
+      if (FP8 && kb == 0) load_tile_scales(p, tn, lane, ws);
       if (!mbar_wait(&tfull[buf], acc_phase)) {
         report(p.status, kTimeoutMma);
         break;
@@ -779,7 +801,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (ke < k_iters)  // head of a split tile: fold in the later pairs' partials first
           sk_gather_partials(p, taddr, pair, n_pairs, static_cast<int>(rank), r_in, sub, epoch,
                              (t - p.sk_first + 1) * k_iters);
-        epilogue_tile<FP8>(p, o, taddr, row, tn);
+        epilogue_tile<FP8>(p, o, taddr, row, tn, ws);
       }
       tc_fence_before();
       __syncwarp();
