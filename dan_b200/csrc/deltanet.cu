@@ -170,6 +170,8 @@ constexpr int CH = 64;
 constexpr int LDW = DK + 8;  // bf16 row stride of 128-wide tiles: 272 B, ldmatrix rows on distinct banks
 constexpr int LDN = CH + 8;  // bf16 row stride of 64-wide tiles
 constexpr int LDF = CH + 1;  // fp32 row stride of 64 x 64 tiles
+constexpr int LDT = CH + 4;  // fp32 row stride of T: 16-byte rows for the merges' vector loads
+constexpr int LDY = 36;      // fp32 row stride of the merges' 32-wide scratch
 
 // Scratch records, rows padded exactly as in shared memory so a chunk loads with a few bulk
 // copies: per (chunk, value head) -W [64][LDW], T'V as two 64-column halves [64][LDN], P
@@ -221,7 +223,7 @@ struct PrepSmem {
   __nv_bfloat16 kn[CH * LDW];  // k̂
   __nv_bfloat16 v[CH * LDW];   // v, later T'V
   float a[CH * LDF];           // A
-  float tf[CH * LDF];          // T
+  float tf[CH * LDT];          // T
   __nv_bfloat16 tb[CH * LDN];  // T diag(β) (fp32 merge scratch before that)
   __nv_bfloat16 tg[CH * LDN];  // T diag(βγ)
   __nv_bfloat16 pb[CH * LDN];  // P
@@ -304,7 +306,7 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
     *qp = make_uint2(pack_bf16(qa.x * nq, qa.y * nq), pack_bf16(qb.x * nq, qb.y * nq));
     *kp = make_uint2(pack_bf16(ka.x * nk, ka.y * nk), pack_bf16(kb.x * nk, kb.y * nk));
   }
-  for (int i = tid; i < CH * LDF; i += blockDim.x) sm.tf[i] = 0.f;
+  for (int i = tid; i < CH * LDT; i += blockDim.x) sm.tf[i] = 0.f;
   __syncthreads();
   if (owner) {
     copy_out(rk, sm.qn, TILE_W);
@@ -383,32 +385,34 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
 #pragma unroll
       for (int s2 = 0; s2 < t; ++s2) acc -= sm.a[(16 * d + t) * LDF + 16 * d + s2] * x[s2];
       x[t] = acc;
-      sm.tf[(16 * d + t) * LDF + 16 * d + j] = acc;
+      sm.tf[(16 * d + t) * LDT + 16 * d + j] = acc;
     }
   }
   __syncthreads();
-  float* ysc = reinterpret_cast<float*>(sm.tb);  // 32 x 33 fp32 scratch
+  float* ysc = reinterpret_cast<float*>(sm.tb);  // 32 x LDY fp32 scratch
+  // The merges read rows of T and of the scratch as 8- / 16-byte vectors (LDT, LDY: 16-byte
+  // rows); each output still accumulates over k in order.
   {  // level 1: T[d+1][d] = -T[d+1][d+1] A[d+1][d] T[d][d] for d = 0, 2
     const int q = tid >> 7, r = (tid >> 3) & 15, cc = (tid & 7) * 2, d = 2 * q;
     float y0 = 0.f, y1 = 0.f;
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
       const float av = sm.a[(16 * (d + 1) + r) * LDF + 16 * d + k];
-      y0 += av * sm.tf[(16 * d + k) * LDF + 16 * d + cc];
-      y1 += av * sm.tf[(16 * d + k) * LDF + 16 * d + cc + 1];
+      const float2 t2 = *reinterpret_cast<const float2*>(&sm.tf[(16 * d + k) * LDT + 16 * d + cc]);
+      y0 += av * t2.x;
+      y1 += av * t2.y;
     }
-    ysc[(q * 16 + r) * 33 + cc] = y0;
-    ysc[(q * 16 + r) * 33 + cc + 1] = y1;
+    *reinterpret_cast<float2*>(&ysc[(q * 16 + r) * LDY + cc]) = make_float2(y0, y1);
     __syncthreads();
     float x0 = 0.f, x1 = 0.f;
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-      const float tv = sm.tf[(16 * (d + 1) + r) * LDF + 16 * (d + 1) + k];
-      x0 -= tv * ysc[(q * 16 + k) * 33 + cc];
-      x1 -= tv * ysc[(q * 16 + k) * 33 + cc + 1];
+      const float tv = sm.tf[(16 * (d + 1) + r) * LDT + 16 * (d + 1) + k];
+      const float2 y2 = *reinterpret_cast<const float2*>(&ysc[(q * 16 + k) * LDY + cc]);
+      x0 -= tv * y2.x;
+      x1 -= tv * y2.y;
     }
-    sm.tf[(16 * (d + 1) + r) * LDF + 16 * d + cc] = x0;
-    sm.tf[(16 * (d + 1) + r) * LDF + 16 * d + cc + 1] = x1;
+    *reinterpret_cast<float2*>(&sm.tf[(16 * (d + 1) + r) * LDT + 16 * d + cc]) = make_float2(x0, x1);
   }
   __syncthreads();
   {  // level 2: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32]
@@ -416,25 +420,30 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
     float y[4] = {};
     for (int k = 0; k < 32; ++k) {
       const float av = sm.a[(32 + r) * LDF + k];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) y[e] += av * sm.tf[k * LDF + cq + e];
+      const float4 t4 = *reinterpret_cast<const float4*>(&sm.tf[k * LDT + cq]);
+      y[0] += av * t4.x;
+      y[1] += av * t4.y;
+      y[2] += av * t4.z;
+      y[3] += av * t4.w;
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) ysc[r * 33 + cq + e] = y[e];
+    *reinterpret_cast<float4*>(&ysc[r * LDY + cq]) = make_float4(y[0], y[1], y[2], y[3]);
     __syncthreads();
     float x[4] = {};
     for (int k = 0; k < 32; ++k) {
-      const float tv = sm.tf[(32 + r) * LDF + 32 + k];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) x[e] -= tv * ysc[k * 33 + cq + e];
+      const float tv = sm.tf[(32 + r) * LDT + 32 + k];
+      const float4 y4 = *reinterpret_cast<const float4*>(&ysc[k * LDY + cq]);
+      x[0] -= tv * y4.x;
+      x[1] -= tv * y4.y;
+      x[2] -= tv * y4.z;
+      x[3] -= tv * y4.w;
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) sm.tf[(32 + r) * LDF + cq + e] = x[e];
+    *reinterpret_cast<float4*>(&sm.tf[(32 + r) * LDT + cq]) = make_float4(x[0], x[1], x[2], x[3]);
   }
   __syncthreads();
   for (int e = tid; e < CH * CH / 2; e += blockDim.x) {  // T' = T diag(β) and T diag(βγ), bf16
     const int t = e >> 5, s2 = (e & 31) * 2;
-    const float t0 = sm.tf[t * LDF + s2] * sm.beta[s2], t1 = sm.tf[t * LDF + s2 + 1] * sm.beta[s2 + 1];
+    const float2 tt = *reinterpret_cast<const float2*>(&sm.tf[t * LDT + s2]);
+    const float t0 = tt.x * sm.beta[s2], t1 = tt.y * sm.beta[s2 + 1];
     st_bf2(&sm.tb[t * LDN + s2], t0, t1);
     st_bf2(&sm.tg[t * LDN + s2], t0 * sm.eg[s2], t1 * sm.eg[s2 + 1]);
   }
