@@ -361,11 +361,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int D>
 int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tpk,
            const CUtensorMap& tpv, const Params& p, int n_tiles, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    DAN_CUDA(cudaFuncSetAttribute(tree_attention_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  DAN_CUDA(smem_limit_once(tree_attention_kernel<D>, Cfg<D>::SMEM, configured));
   dim3 grid(p.n_heads, n_tiles);
   tree_attention_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, p);
   DAN_CUDA(cudaGetLastError());
@@ -890,12 +887,8 @@ __global__ void __launch_bounds__(320, 1)
 template <int D>
 int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tpk,
                 const CUtensorMap& tpv, const CUtensorMap& to, const Params& p, int n_tiles, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    DAN_CUDA(cudaFuncSetAttribute(tree_attention_pair_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  PairCfg<D>::SMEM));
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  DAN_CUDA(smem_limit_once(tree_attention_pair_kernel<D>, PairCfg<D>::SMEM, configured));
   const int items = n_tiles * (p.n_heads / 2);
   const int grid = p.sched ? p.sched_ctas : (items < sm_count() ? items : sm_count());
   tree_attention_pair_kernel<D><<<grid, PairCfg<D>::THREADS, PairCfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, to,

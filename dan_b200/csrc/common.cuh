@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -51,6 +52,21 @@ int fail(int code, const char* fmt, ...);
     if (e_ != cudaSuccess)                                                                    \
       return ::dan::fail(-5, "%s failed: %s", #call, cudaGetErrorString(e_));                 \
   } while (0)
+
+// Raise a kernel's dynamic shared-memory limit on the current device, once per (call site,
+// device): function attributes belong to each device's context, and one process may drive
+// several GPUs from several threads (one replica each). ``done`` holds a bit per device id.
+template <typename Kernel>
+cudaError_t smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // Tensor map: a 2-5 D tiled box of a strided global tensor, 128B swizzle.
 // dims/strides are innermost first; strides in bytes for dims 1.. (dim 0 is dense).

@@ -856,14 +856,9 @@ DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, in
   p.n_chunks = n_chunks;
   p.scratch = static_cast<uint8_t*>(scratch);
   p.status = status;
-  static bool configured = false;
-  if (!configured) {
-    DAN_CUDA(cudaFuncSetAttribute(delta::chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(sizeof(delta::PrepSmem))));
-    DAN_CUDA(cudaFuncSetAttribute(delta::chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(sizeof(delta::StateSmem))));
-    configured = true;
-  }
+  static std::atomic<uint64_t> prep_conf{0}, state_conf{0};
+  DAN_CUDA(smem_limit_once(delta::chunk_prep_kernel, static_cast<int>(sizeof(delta::PrepSmem)), prep_conf));
+  DAN_CUDA(smem_limit_once(delta::chunk_state_kernel, static_cast<int>(sizeof(delta::StateSmem)), state_conf));
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   delta::chunk_prep_kernel<<<dim3(n_chunks, hv), 256, sizeof(delta::PrepSmem), st>>>(p);
   DAN_CUDA(cudaGetLastError());

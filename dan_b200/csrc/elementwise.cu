@@ -593,11 +593,8 @@ DAN_API int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, 
   if (!n_questions) return 0;
   const size_t smem = (static_cast<size_t>(hidden) + max_labels) * sizeof(float);
   DAN_REQUIRE(smem <= 200 * 1024, "label_readout: hidden %d too large", hidden);
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    DAN_CUDA(cudaFuncSetAttribute(ew::readout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured = smem;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (smem > 48 * 1024) DAN_CUDA(smem_limit_once(ew::readout_kernel, 200 * 1024, configured));
   ew::readout_kernel<<<n_questions, 256, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(h), ldh, read_rows, static_cast<const __nv_bfloat16*>(norm_w), eps, mode,
       static_cast<const __nv_bfloat16*>(w_lm), ldw, vocab, label_ids, offsets, hidden, logits, probs, status);

@@ -1004,12 +1004,8 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
         pairs = max_pairs;
       }
     }
-    static bool pconf[2] = {false, false};
-    if (!pconf[FP8]) {
-      DAN_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    P_SMEM_BYTES));
-      pconf[FP8] = true;
-    }
+    static std::atomic<uint64_t> pconf{0};
+    DAN_CUDA(smem_limit_once(gemm_pair_kernel<FP8>, P_SMEM_BYTES, pconf));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(THREADS);
@@ -1028,11 +1024,8 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   constexpr int smem_bytes = SMEM_BYTES_BASE + SINK_BYTES;
-  static bool configured[2] = {false, false};
-  if (!configured[FP8]) {
-    DAN_CUDA(cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
-    configured[FP8] = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  DAN_CUDA(smem_limit_once(gemm_kernel<FP8>, smem_bytes, configured));
   gemm_kernel<FP8><<<grid, THREADS, smem_bytes, stream>>>(ta, tb, tc, tr, p);
   DAN_CUDA(cudaGetLastError());
   return 0;

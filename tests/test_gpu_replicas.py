@@ -1,0 +1,40 @@
+"""Several GPU replicas driven from one process (the engine's multi-replica mode): each
+device gets its own kernel attributes and status word, and two threads reading at once give
+the same answers as one replica alone. Needs two GPUs; skipped otherwise."""
+from concurrent.futures import ThreadPoolExecutor
+
+import pytest
+import torch
+from conftest import golden, plans_from_json
+
+from dan_b200.runner import Runner
+from oracle import weights
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tiny_dir(tmp_path_factory):
+    g = golden("tiny_llama.json")
+    path = tmp_path_factory.mktemp("tiny_llama_replicas")
+    weights.save_checkpoint(str(path), g["config"], weights.random_state(g["config"], g["seed"]))
+    return str(path), g
+
+
+def test_two_replicas_in_one_process(tiny_dir):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    path, g = tiny_dir
+    runners = [Runner(path, torch.device("cuda", i), cache_bytes=0) for i in (0, 1)]
+    batches = [plans_from_json(b["plans"]) for b in g["batches"]]
+    solo = [runners[0].read_many(p, probabilities=True) for p in batches]
+
+    def read_all(r):
+        return [r.read_many(p, probabilities=True) for p in batches]
+
+    with ThreadPoolExecutor(2) as ex:
+        both = list(ex.map(read_all, runners))
+    for outs in both:
+        for (lg, pr), (lg0, pr0) in zip(outs, solo):
+            for a, b in zip(lg + pr, lg0 + pr0):
+                assert all(torch.equal(x, y) for x, y in zip(a, b))
