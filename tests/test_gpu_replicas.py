@@ -38,3 +38,41 @@ def test_two_replicas_in_one_process(tiny_dir):
         for (lg, pr), (lg0, pr0) in zip(outs, solo):
             for a, b in zip(lg + pr, lg0 + pr0):
                 assert all(torch.equal(x, y) for x, y in zip(a, b))
+
+
+def test_engine_over_gpu_replicas(tiny_dir):
+    """dan's serving contract on the GPU: concurrent decides through ``AsyncEngine`` over one
+    runner per visible GPU (two batches in flight per replica) give the answers solo reads give."""
+    import asyncio
+
+    from test_engine import QUESTIONS, FakePlanner
+
+    from dan_b200 import readout
+    from dan_b200.engine import AsyncEngine
+
+    path, _ = tiny_dir
+    n = min(2, torch.cuda.device_count())
+    runners = [Runner(path, torch.device("cuda", i), cache_bytes=0) for i in range(n)]
+    eng = AsyncEngine(FakePlanner(), runners, max_batch_tokens=96, max_wait_ms=1)
+    states = [f"request {i} about billing " * (1 + i % 3) for i in range(24)]
+
+    async def main():
+        res = await asyncio.gather(*[eng.decide(s, QUESTIONS) for s in states])
+        await eng.stop()
+        return res
+
+    res = asyncio.run(main())
+    assert eng.stats.requests == len(states) and eng.stats.errors == 0 and eng.stats.batches > 1
+
+    def close(a, b):
+        if isinstance(a, dict):
+            return a.keys() == b.keys() and all(close(a[k], b[k]) for k in a)
+        if isinstance(a, float):
+            return abs(a - b) < 1e-5
+        return a == b
+
+    for s, (ans, tokens) in zip(states, res):
+        plans = FakePlanner().plans(s, QUESTIONS)
+        reads = runners[0].read_many(plans)
+        solo = readout.answers(plans[0], readout.combine(plans, reads), logits_canonical=True)
+        assert close(ans, solo) and tokens == AsyncEngine.cost(plans[0])
