@@ -13,6 +13,12 @@ batch on the device, return a handle whose ``result()`` waits), up to
 next batch while the device computes the current one. A runner with only
 ``read_many`` runs one batch at a time.
 
+Planning (the prompt planner's tokenisation, dan/prompt.py:70-123) runs on a
+pool of ``planner_threads`` threads (default 1) instead of the event loop, so
+one request's planning does not hold up the others' routing, batching and
+result delivery; with a thread-safe planner and a tokenizer that releases the
+GIL (Hugging Face fast tokenizers), more threads plan several requests at once.
+
 Difference: ``runner`` may be a list of runners, one per GPU, each with its own
 prefix pool and its own queue. A plan whose static prefix was routed before goes
 to the same replica (prefix affinity: its cached K/V or recurrent state lives
@@ -26,6 +32,7 @@ aggregates; ``replica_stats`` is per replica.
 import asyncio
 import time
 from collections import OrderedDict, deque
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 
 from .readout import answers, combine
@@ -62,7 +69,7 @@ class Stats:
 
 class AsyncEngine:
     def __init__(self, planner, runner, max_batch_tokens=8192, max_wait_ms=2.0, max_queue=1024,
-                 steal_after_ms=20.0, max_homes=65536, in_flight=2):
+                 steal_after_ms=20.0, max_homes=65536, in_flight=2, planner_threads=1):
         self.planner = planner
         self.runners = list(runner) if isinstance(runner, (list, tuple)) else [runner]
         self.runner = self.runners[0]  # dan's /metrics reads engine.runner.cache
@@ -77,6 +84,7 @@ class AsyncEngine:
         self._busy = [0] * n  # per replica: batches being collected or in flight
         self._busy_since = [0.0] * n
         self.in_flight = max(1, int(in_flight))
+        self._plan_pool = ThreadPoolExecutor(max(1, int(planner_threads)), thread_name_prefix="dan-plan")
         self._homes = OrderedDict()  # static-prefix key -> replica
         self._arrived = asyncio.Event()
         self.affinity_hits = 0
@@ -104,13 +112,14 @@ class AsyncEngine:
 
     async def decide(self, state, questions, profile=None):
         """Answers keyed by question id, and the input tokens the reads took (engine.py:55-72)."""
-        plans = self.planner.plans(state, questions, profile)
+        loop = asyncio.get_running_loop()
+        plans = await loop.run_in_executor(self._plan_pool, self.planner.plans, state, questions, profile)
         if not plans[0].branches:
             return answers(plans[0], []), 0
         if self.queued() + len(plans) > self.max_queue:
             raise Overloaded("dan is at capacity. Retry shortly.")
         self.start()
-        loop, t0 = asyncio.get_running_loop(), time.perf_counter()
+        t0 = time.perf_counter()
         futs = [loop.create_future() for _ in plans]
         for plan, fut in zip(plans, futs):
             r, cost = self.route(plan), self.cost(plan)

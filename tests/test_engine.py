@@ -276,3 +276,49 @@ def test_pipelined_batches_stay_bounded_and_answer_like_solo_reads(in_flight):
         assert r[0] == readout.answers(plan, FakeRunner().read_many([plan])[0])
     assert 0 < eng.stats.busy_s <= wall + 1e-3
     assert runner.outstanding == 0
+
+
+class SlowPlanner(FakePlanner):
+    """Planning that takes 50 ms outside the GIL (as a fast tokenizer's encode does)."""
+
+    def plans(self, state, questions, profile=None):
+        import time
+
+        time.sleep(0.05)
+        return super().plans(state, questions, profile)
+
+
+def test_planning_runs_off_the_event_loop():
+    """The engine plans on its planner pool: the event loop stays free while a request is being
+    planned (a ticker keeps running), and with a thread-safe planner several plan at once."""
+    import time
+
+    def measure(threads):
+        eng = AsyncEngine(SlowPlanner(), FakeRunner(), max_wait_ms=1, planner_threads=threads)
+        ticks = []
+
+        async def ticker(stop):
+            while not stop.is_set():
+                ticks.append(time.perf_counter())
+                await asyncio.sleep(0.005)
+
+        async def main():
+            stop = asyncio.Event()
+            tick = asyncio.create_task(ticker(stop))
+            t0 = time.perf_counter()
+            res = await asyncio.gather(*[eng.decide(f"state {i}", QUESTIONS) for i in range(8)])
+            dt = time.perf_counter() - t0
+            stop.set()
+            await tick
+            await eng.stop()
+            return res, dt
+
+        res, dt = run(main())
+        gaps = [b - a for a, b in zip(ticks, ticks[1:])]
+        return res, dt, max(gaps) if gaps else 0.0
+
+    res1, dt1, gap1 = measure(1)
+    res4, dt4, gap4 = measure(4)
+    assert len(res1) == len(res4) == 8 and [r[1] for r in res1] == [r[1] for r in res4]
+    assert gap1 < 0.045 and gap4 < 0.045  # the loop never waited out a 50 ms planning call
+    assert dt4 < 0.7 * dt1  # four planning threads overlap the 8 x 50 ms of planning
