@@ -74,8 +74,12 @@ struct Cfg {
   static constexpr int CHUNKS = D / 64;
   static constexpr int Q_BYTES = CHUNKS * CHUNK;
   static constexpr int KV_BYTES = CHUNKS * CHUNK;
+  // Output staging: per softmax warp two 2 KB slots (32 rows x 32 bf16 columns, 64-byte
+  // swizzle) sent by TMA store.
+  static constexpr int SLOT_BYTES = 32 * 64;
+  static constexpr int SINK_BYTES = 4 * 2 * SLOT_BYTES;
   // At least 120 KB so two CTAs never share an SM: each allocates all 512 TMEM columns.
-  static constexpr int SMEM_USED = Q_BYTES + 2 * NS * KV_BYTES + 1024 + 512;
+  static constexpr int SMEM_USED = Q_BYTES + 2 * NS * KV_BYTES + SINK_BYTES + 1024 + 512;
   static constexpr int SMEM = SMEM_USED < 120 * 1024 ? 120 * 1024 : SMEM_USED;
 };
 
@@ -89,7 +93,8 @@ template <int D>
 __global__ void __launch_bounds__(THREADS, 1)
     tree_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                           const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tpk,
-                          const __grid_constant__ CUtensorMap tpv, Params p) {
+                          const __grid_constant__ CUtensorMap tpv, const __grid_constant__ CUtensorMap to,
+                          Params p) {
   using C = Cfg<D>;
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
@@ -97,7 +102,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sq = smem;
   uint8_t* sk = sq + C::Q_BYTES;
   uint8_t* sv = sk + NS * C::KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + NS * C::KV_BYTES);
+  uint8_t* sink = sv + NS * C::KV_BYTES;  // 1024-byte aligned: Q and K/V stages are multiples of 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sink + C::SINK_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
   uint64_t* v_full = k_full + NS;
@@ -330,17 +336,37 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
+        // Whole 32-row slabs leave through two shared-memory slots by TMA store (as in the
+        // paired kernel); a segment's ragged last rows are stored per row.
+        const bool slab = (sub + 1) * 32 <= tile.nrows;
+        uint8_t* slots = sink + (warp - 2) * 2 * C::SLOT_BYTES;
         __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
           uint32_t o[32];
           tmem_ld32(tmem_o + lane_base + c, o);
           tmem_wait_ld();
-          if (valid) {
-            uint32_t pkd[16];
+          uint32_t pkd[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          for (int i = 0; i < 16; ++i)
+            pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          if (slab) {
+            uint8_t* slot = slots + ((c >> 5) & 1) * C::SLOT_BYTES;
+            if (lane == 0) bulk_wait_read<1>();  // the store sent from this slot two chunks ago has read it
+            __syncwarp();
+            uint4* d4 = reinterpret_cast<uint4*>(slot + lane * 64);
+            const int sw = (lane >> 1) & 3;  // 64-byte swizzle: unit u of row r at u ^ ((r >> 1) & 3)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i ^ sw] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&to, slot, c, head, tile.row0 + sub * 32);
+              bulk_commit();
+            }
+            __syncwarp();
+          } else if (valid) {
             uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
             for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
@@ -348,6 +374,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_all();  // output stores done before the CTA's shared memory goes away
     tc_fence_before();
   }
   __syncwarp();
@@ -360,11 +387,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 template <int D>
 int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tpk,
-           const CUtensorMap& tpv, const Params& p, int n_tiles, cudaStream_t stream) {
+           const CUtensorMap& tpv, const CUtensorMap& to, const Params& p, int n_tiles, cudaStream_t stream) {
   static std::atomic<uint64_t> configured{0};
   DAN_CUDA(smem_limit_once(tree_attention_kernel<D>, Cfg<D>::SMEM, configured));
   dim3 grid(p.n_heads, n_tiles);
-  tree_attention_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, p);
+  tree_attention_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, to, p);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }
@@ -963,18 +990,17 @@ DAN_API int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, con
   p.sched_ctas = sched_ctas;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool paired = (n_heads / n_kv_heads) % 2 == 0 && head_dim <= 128;
-  if (paired) {
-    CUtensorMap to;
-    if ((rc = attn::out_map(&to, out, out_row, out_head, n_heads, n_rows, head_dim))) return rc;
+  CUtensorMap to;
+  if ((rc = attn::out_map(&to, out, out_row, out_head, n_heads, n_rows, head_dim))) return rc;
+  if (paired)
     return head_dim == 64 ? attn::launch_pair<64>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s)
                           : attn::launch_pair<128>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s);
-  }
   switch (head_dim) {
     case 64:
-      return attn::launch<64>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
+      return attn::launch<64>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s);
     case 128:
-      return attn::launch<128>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
+      return attn::launch<128>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s);
     default:
-      return attn::launch<256>(tq, tk, tv, tpk, tpv, p, n_tiles, s);
+      return attn::launch<256>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s);
   }
 }

@@ -42,6 +42,14 @@ def test_long_segments_with_pages(cuda, d):
     torch.testing.assert_close(got, want, atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("h,hkv,d", [(9, 3, 64), (9, 3, 128), (8, 2, 256)])
+def test_single_head_kernel_long_segments(cuda, h, hkv, d):
+    """The single-head kernel (odd GQA ratio, or D = 256) on long paged segments: whole 32-row
+    slabs leave by TMA store, ragged ones per row."""
+    got, want = run_case(LONG, h, hkv, d, cuda, seed=3)
+    torch.testing.assert_close(got, want, atol=2e-2, rtol=2e-2)
+
+
 def test_llama3_heads_random_batch(cuda):
     import random
 
