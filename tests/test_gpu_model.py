@@ -84,3 +84,19 @@ def test_read_stream_matches_read_many(cuda, tiny_dir):
     first, second = runner.submit(batches[0]), runner.submit(batches[1])
     assert second.result() is not None and first.ready()  # in-order device queue
     assert all(torch.equal(x, y) for x, y in zip(first.result()[0], solo[0][0][0]))
+
+
+def test_submit_edges(cuda, tiny_dir):
+    """A batch whose plans ask nothing reads nothing (one empty list per plan), an empty stream
+    yields nothing, and such a batch between real ones does not disturb them."""
+    from dan_b200.plan import ReadPlan
+
+    path, g = tiny_dir
+    runner = Runner(path, cuda, cache_bytes=0)
+    empty = [ReadPlan([1, 2, 3], branches=[], static=0)]
+    assert runner.read_many(empty) == [[]]
+    assert list(runner.read_stream([])) == []
+    real = plans_from_json(g["batches"][0]["plans"])
+    outs = list(runner.read_stream([real, empty, real]))
+    assert outs[1] == [[]]
+    assert all(torch.equal(a, b) for pa, pb in zip(outs[0], outs[2]) for a, b in zip(pa, pb))
