@@ -61,6 +61,9 @@ struct Params {
   // Stream-K (pair kernel): tiles [sk_first, tiles) are split by K iteration across the pairs,
   // sk_iters iterations in all; 0 = every tile whole.
   int sk_first, sk_iters;
+  // Narrow tail (pair kernel, no stream-K): tiles [nt_first, sk_first) each run as nt_split
+  // items of BN / nt_split columns, so a ragged last wave spreads over more pairs; 1 = none.
+  int nt_first, nt_split;
   float* sk_part;     // [pairs][2][BN][128] fp32 partial accumulators, column-major per CTA
   uint32_t* sk_flag;  // [pairs][2][4] per-warp "partial written" flags (value = epoch + 1)
   uint32_t* sk_ctrl;  // [0] epoch, [1] CTAs finished in this launch
@@ -84,31 +87,54 @@ __device__ __forceinline__ void pair_tile(int t, int tiles_m, int tiles_n, int o
   tn = order == 0 ? b : a;
 }
 
-// The pair kernel's work list: whole tiles pair, pair + P, ... below sk_first, then this pair's
-// contiguous share [g, g1) of the stream-K iterations, cut at tile boundaries into segments
-// (t, kb, ke). A pair's share is contiguous, so only its first segment can start inside a
-// tile and only its last can stop inside one.
+// One unit of a pair's work: K iterations [kb, ke) of tile t, restricted to column slice ``sub``
+// of ``width`` columns (width BN: the whole tile).
+struct PairItem {
+  int t, kb, ke, sub, width;
+};
+
+// The pair kernel's work list: items pair, pair + P, ... of the data-parallel list (whole tiles
+// below nt_first, then nt_split narrow items per tile up to sk_first), then this pair's
+// contiguous share [g, g1) of the stream-K iterations, cut at tile boundaries into segments.
+// A pair's share is contiguous, so only its first segment can start inside a tile and only
+// its last can stop inside one.
 struct PairWork {
-  int next_dp, dp_end, n_pairs, k_iters, g, g1;
+  int next_dp, dp_items, dp_end, nt_first, ns, n_pairs, k_iters, g, g1;
   __device__ __forceinline__ PairWork(int pair, int P, const Params& p, int ki)
-      : next_dp(pair), dp_end(p.sk_first), n_pairs(P), k_iters(ki) {
+      : next_dp(pair),
+        dp_items(p.nt_first + (p.sk_first - p.nt_first) * p.nt_split),
+        dp_end(p.sk_first),
+        nt_first(p.nt_first),
+        ns(p.nt_split),
+        n_pairs(P),
+        k_iters(ki) {
     g = static_cast<int>(static_cast<long long>(pair) * p.sk_iters / P);
     g1 = static_cast<int>(static_cast<long long>(pair + 1) * p.sk_iters / P);
   }
-  __device__ __forceinline__ bool next(int& t, int& kb, int& ke) {
-    if (next_dp < dp_end) {
-      t = next_dp;
-      kb = 0;
-      ke = k_iters;
+  __device__ __forceinline__ bool next(PairItem& w) {
+    w.sub = 0;
+    w.width = BN;
+    if (next_dp < dp_items) {
+      const int it = next_dp;
       next_dp += n_pairs;
+      if (it < nt_first) {
+        w.t = it;
+      } else {
+        const int j = it - nt_first, q = j / ns;
+        w.t = nt_first + q;
+        w.sub = j - q * ns;
+        w.width = BN / ns;
+      }
+      w.kb = 0;
+      w.ke = k_iters;
       return true;
     }
     if (g >= g1) return false;
     const int tr = g / k_iters;
-    t = dp_end + tr;
-    kb = g - tr * k_iters;
-    ke = kb + (g1 - g) < k_iters ? kb + (g1 - g) : k_iters;
-    g += ke - kb;
+    w.t = dp_end + tr;
+    w.kb = g - tr * k_iters;
+    w.ke = w.kb + (g1 - g) < k_iters ? w.kb + (g1 - g) : k_iters;
+    g += w.ke - w.kb;
     return true;
   }
 };
@@ -265,9 +291,10 @@ __device__ __forceinline__ void sink_load_resid(Sink& o, uint32_t seq, int col) 
 // Residual epilogue through the sink: C = bf16(R + bf16(acc [+ bias])) chunk by chunk, the
 // next chunk's residual loading while this one is computed.
 template <bool FP8>
-__device__ __forceinline__ void residual_tma(Sink& o, const Params& p, uint32_t taddr, int col0, float as) {
+__device__ __forceinline__ void residual_tma(Sink& o, const Params& p, uint32_t taddr, int col0, int cols,
+                                             float as) {
   if (o.row0 >= p.m) return;
-  const int width = p.n - col0 < BN ? p.n - col0 : BN;
+  const int width = p.n - col0 < cols ? p.n - col0 : cols;
   const int nch = (width + 31) / 32;
   if (o.lane == 0) {
     bulk_wait_read<3>();
@@ -331,22 +358,26 @@ __device__ __forceinline__ void epilogue_prefetch(const Params& p, int row, int 
   }
 }
 
-// The fused epilogue of one 128-row x 256-column accumulator tile held in TMEM at ``taddr``
-// (this warp's lanes): ``row`` is this thread's output row, ``tn`` the tile's column block.
+// The fused epilogue of one 128-row accumulator held in TMEM at ``taddr`` (this warp's lanes):
+// ``row`` is this thread's output row, ``tn`` the tile's column block, and the accumulator
+// holds column slice ``sub`` of ``width`` columns of that block (width BN: the whole block).
+// A slice is contiguous, except for SwiGLU, where it is width / 2 gate columns followed by
+// the same width / 2 up columns (each CTA of the pair stages one half of W's rows).
 template <bool FP8>
-__device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t taddr, int row, int tn,
-                                              const float (&ws)[8]) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t taddr, int row, int tn, int sub,
+                                              int width, const float (&ws)[8]) {
   const int cols_out = p.epilogue == kSwiglu ? p.n / 2 : p.n;
   const float as = (FP8 && row < p.m) ? p.a_scale[row] : 1.f;
   if (p.epilogue == kSwiglu) {
+    const int half = width / 2, off = sub * half;
 #pragma unroll 1
-    for (int c = 0; c < BN / 2; c += 32) {
+    for (int c = 0; c < half; c += 32) {
       uint32_t g[32], u[32];
       tmem_ld32(taddr + c, g);
-      tmem_ld32(taddr + BN / 2 + c, u);
+      tmem_ld32(taddr + half + c, u);
       tmem_wait_ld();
       float v[32];
-      const int gcol = tn * BN + c, ucol = tn * BN + BN / 2 + c;
+      const int gcol = tn * BN + off + c, ucol = tn * BN + BN / 2 + off + c;
       if (FP8) {
         scale_chunk(p, gcol, as, g);
         scale_chunk(p, ucol, as, u);
@@ -362,16 +393,17 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
         uv = bf16_round(uv);
         v[i] = silu(gv) * uv;
       }
-      emit<FP8>(o, p, row, tn * (BN / 2) + c, cols_out, v);
+      emit<FP8>(o, p, row, tn * (BN / 2) + off + c, cols_out, v);
     }
   } else if (p.epilogue == kRope) {
     // q/k heads: rotate-half RoPE on the bf16-rounded projection with the reference's
     // rounding points, bf16(bf16(a cos) + bf16(-b sin)) (llama.py:43-45); v heads: plain.
-    const int hd = p.rope_hd, half = hd / 2;
+    // A slice holds whole heads (the host keeps width a multiple of the head size).
+    const int hd = p.rope_hd, half = hd / 2, base = sub * width;
     const int trow = row < p.m ? row : 0;
     // Every head of the tile rotates by the same per-row angles: each 32-column slice of this
     // row's cos / sin is loaded once and used for all the tile's heads.
-    const bool any_rot = tn * BN + hd <= p.rope_cols;
+    const bool any_rot = tn * BN + base + hd <= p.rope_cols;
 #pragma unroll 1
     for (int c = 0; c < half; c += 32) {
       float ct[32], st[32];
@@ -386,8 +418,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
         }
       }
 #pragma unroll 1
-      for (int h0 = 0; h0 < BN; h0 += hd) {
-        const int hc = tn * BN + h0;
+      for (int h0 = 0; h0 < width; h0 += hd) {
+        const int hc = tn * BN + base + h0;
         if (hc >= p.n) break;
         uint32_t ra[32], rb[32];
         tmem_ld32(taddr + h0 + c, ra);
@@ -395,7 +427,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
         tmem_wait_ld();
         float va[32], vb[32];
         const bool rot = hc + hd <= p.rope_cols;
-        const float wa = FP8 ? pick8(ws, (h0 + c) >> 5) : 0.f, wb = FP8 ? pick8(ws, (h0 + half + c) >> 5) : 0.f;
+        const float wa = FP8 ? pick8(ws, (base + h0 + c) >> 5) : 0.f;
+        const float wb = FP8 ? pick8(ws, (base + h0 + half + c) >> 5) : 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float a = __uint_as_float(ra[i]), b = __uint_as_float(rb[i]);
@@ -423,14 +456,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
       }
     }
   } else {
-    const int col0 = tn * BN;
+    const int col0 = tn * BN + sub * width;
     if (col0 >= p.n) return;
     if (o.tma && p.epilogue == kResidual) {
-      residual_tma<FP8>(o, p, taddr, col0, as);
+      residual_tma<FP8>(o, p, taddr, col0, width, as);
       return;
     }
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 0; c < width; c += 32) {
       const int col = col0 + c;
       if (col >= p.n) break;
       uint32_t r[32];
@@ -571,7 +604,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = tm * BM + r_in;
       o.row0 = tm * BM + sub * 32;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
-      epilogue_tile<FP8>(p, o, taddr, row, tn, ws);
+      epilogue_tile<FP8>(p, o, taddr, row, tn, 0, BN, ws);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -657,7 +690,8 @@ __device__ __forceinline__ void sk_gather_partials(const Params& p, uint32_t tad
 template <bool FP8>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                     const __grid_constant__ CUtensorMap tc, const __grid_constant__ CUtensorMap tr, Params p) {
+                     const __grid_constant__ CUtensorMap tbn, const __grid_constant__ CUtensorMap tc,
+                     const __grid_constant__ CUtensorMap tr, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
@@ -701,6 +735,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (elect_one()) {
       tma_prefetch_desc(&ta);
       tma_prefetch_desc(&tb);
+      if (p.nt_split > 1) tma_prefetch_desc(&tbn);
       int stage = 0;
       uint32_t phase = 0;
       // The operand every wave of tiles touches in full (A for m-fastest order, W for n-fastest)
@@ -708,19 +743,26 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t keep = l2_evict_last(), pass = l2_evict_normal();
       const uint64_t pol_a = p.order == 0 ? keep : pass, pol_b = p.order == 0 ? pass : keep;
       PairWork work(pair, n_pairs, p, k_iters);
-      int t, kb, ke;
-      while (work.next(t, kb, ke)) {
+      PairItem w;
+      while (work.next(w)) {
         int tm, tn;
-        pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
-        for (int ki = kb; ki < ke; ++ki) {
+        pair_tile(w.t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
+        // Each CTA stages width / 2 rows of W: for SwiGLU its own half of the block's gate or up
+        // rows, otherwise its half of the slice's contiguous rows (narrow items use ``tbn``,
+        // whose box is width / 2 rows).
+        const int bw = w.width / 2;
+        const int brow = p.epilogue == kSwiglu ? tn * BN + static_cast<int>(rank) * (BN / 2) + w.sub * bw
+                                               : tn * BN + w.sub * w.width + static_cast<int>(rank) * bw;
+        const CUtensorMap* mb = w.width == BN ? &tb : &tbn;
+        for (int ki = w.kb; ki < w.ke; ++ki) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             report(p.status, kTimeoutEmpty);
             goto done;
           }
           const uint32_t fb = map_shared(smem_u32(&full[stage]), 0);
-          if (rank == 0) mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * (P_A_BYTES + bw * KBYTES));
           tma_load_2d_pair_hint(sa + stage * P_A_BYTES, &ta, fb, ki * KELEM, tm * 256 + rank * 128, pol_a);
-          tma_load_2d_pair_hint(sb + stage * P_B_BYTES, &tb, fb, ki * KELEM, tn * BN + rank * 128, pol_b);
+          tma_load_2d_pair_hint(sb + stage * P_B_BYTES, mb, fb, ki * KELEM, brow, pol_b);
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -730,19 +772,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     if (rank == 0 && elect_one()) {
-      constexpr uint32_t idesc = FP8 ? idesc_e4m3(256, BN) : idesc_bf16(256, BN, false, false);
       int stage = 0, buf = 0;
       uint32_t phase = 0, acc_phase = 0;
       PairWork work(pair, n_pairs, p, k_iters);
-      int t, kb, ke;
-      while (work.next(t, kb, ke)) {
+      PairItem w;
+      while (work.next(w)) {
+        const uint32_t idesc = FP8 ? idesc_e4m3(256, w.width) : idesc_bf16(256, w.width, false, false);
+        const int kb = w.kb;
         if (!mbar_wait(&tempty[buf], acc_phase ^ 1)) {
           report(p.status, kTimeoutEmpty);
           goto done;
         }
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int ki = kb; ki < ke; ++ki) {
+        for (int ki = kb; ki < w.ke; ++ki) {
           if (!mbar_wait(&full[stage], phase)) {
             report(p.status, kTimeoutFull);
             goto done;
@@ -778,8 +821,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     const uint32_t epoch = p.sk_iters ? __ldcg(p.sk_ctrl) : 0u;
     PairWork work(pair, n_pairs, p, k_iters);
-    int t, kb, ke;
-    while (work.next(t, kb, ke)) {
+    PairItem w;
+    while (work.next(w)) {
+      const int t = w.t, kb = w.kb, ke = w.ke;
       int tm, tn;
       pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
       if (kb == 0) epilogue_prefetch(p, tm * 256 + static_cast<int>(rank) * 128 + r_in, tn);
@@ -801,7 +845,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (ke < k_iters)  // head of a split tile: fold in the later pairs' partials first
           sk_gather_partials(p, taddr, pair, n_pairs, static_cast<int>(rank), r_in, sub, epoch,
                              (t - p.sk_first + 1) * k_iters);
-        epilogue_tile<FP8>(p, o, taddr, row, tn, ws);
+        epilogue_tile<FP8>(p, o, taddr, row, tn, w.sub, w.width, ws);
       }
       tc_fence_before();
       __syncwarp();
@@ -1004,6 +1048,33 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
         pairs = max_pairs;
       }
     }
+    // Narrow tail: without stream-K, the tiles of a ragged last wave each run as s items of
+    // 256 / s columns (s = 2, 4 or 8, as many as the pairs can take at once), so that wave
+    // ends sooner instead of leaving most pairs idle. A narrow item still streams the tile's
+    // whole A slice, so it costs more than 1 / s of a tile, but several times less than one.
+    // SwiGLU items keep >= 32 gate and up columns; RoPE items keep whole heads.
+    p.nt_first = p.sk_first;
+    p.nt_split = 1;
+    CUtensorMap tbn = tb2;
+    if (p.sk_iters == 0) {
+      const int rem = tiles % max_pairs;
+      int s_max = 8;
+      if (p.epilogue == kSwiglu) s_max = 4;
+      if (p.epilogue == kRope) s_max = BN / p.rope_hd;
+      int s = 1;
+      while (2 * s <= s_max && rem * 2 * s <= max_pairs) s *= 2;
+      if (rem > 0 && s > 1) {
+        p.nt_first = tiles - rem;
+        p.nt_split = s;
+        uint64_t dims[2] = {static_cast<uint64_t>(p.k), static_cast<uint64_t>(p.n)};
+        uint64_t strides[1] = {static_cast<uint64_t>(ldw) * esize};
+        uint32_t box[2] = {kbox, static_cast<uint32_t>(BN / s / 2)};
+        int rc = make_tmap(&tbn, w, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+        const int items = p.nt_first + rem * s;
+        pairs = items < max_pairs ? items : max_pairs;
+      }
+    }
     static std::atomic<uint64_t> pconf{0};
     DAN_CUDA(smem_limit_once(gemm_pair_kernel<FP8>, P_SMEM_BYTES, pconf));
     cudaLaunchConfig_t cfg = {};
@@ -1018,7 +1089,7 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    DAN_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, ta, tb2, tc, tr, p));
+    DAN_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, ta, tb2, tbn, tc, tr, p));
     return 0;
   }
   const int tiles = p.tiles_m * p.tiles_n;

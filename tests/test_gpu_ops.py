@@ -105,6 +105,79 @@ def test_gemm_stream_k(cuda, m, n, k):
     assert rel_err(y1, x.float() @ w.float().T) < 1e-2
 
 
+def _narrow_split(m, n, k, epilogue, hd=0):
+    """Items per tile of the last, ragged wave of 256 x 256 tiles (the host rule of the pair
+    kernel): 1 when every tile runs whole."""
+    pairs = torch.cuda.get_device_properties(0).multi_processor_count // 2
+    tiles = -(-m // 256) * -(-n // 256)
+    if m < 256 or (k * 2 // 128 >= 128 and tiles % pairs and tiles * 100 < -(-tiles // pairs) * pairs * 95):
+        return 1  # single-CTA kernel, or the stream-K tail
+    s_max = 4 if epilogue == "swiglu" else (256 // hd if epilogue == "rope" else 8)
+    rem, s = tiles % pairs, 1
+    while 2 * s <= s_max and rem * 2 * s <= pairs:
+        s *= 2
+    return s if rem else 1
+
+
+# A ragged last wave of whole tiles runs as narrow column slices (256 / s columns, s = 2, 4, 8)
+# spread over the idle pairs. Shapes picked so each epilogue meets each slice width on a
+# 148-SM part: (7089, 4096) is the Llama-3-8B o projection (448 tiles, 4 left over -> 8 slices
+# of 32 columns), (7089, 6144) its q/k/v projection (6 left over, RoPE keeps 128-column heads),
+# 6600 columns make slices past n. The result must match fp32 and repeat bit for bit.
+@pytest.mark.parametrize("m,n,k,epilogue,split", [
+    (7089, 4096, 4096, "residual", 8),
+    (768, 6600, 512, "store", 8),
+    (512, 11008, 256, "residual", 4),
+    (7089, 6144, 1024, "rope", 2),
+    (300, 960, 512, "rope64", 4),
+    (256, 4096, 512, "swiglu", 4),
+    (768, 2560, 512, "swiglu", 2),
+    (7089, 4096, 2048, "e4m3", 8),
+])
+def test_gemm_narrow_tail(cuda, m, n, k, epilogue, split):
+    hd = {"rope": 128, "rope64": 64}.get(epilogue, 0)
+    kind = "rope" if hd else epilogue
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert _narrow_split(m, n, k, kind, hd) == split
+    g = torch.Generator(device=cuda).manual_seed(m + n + k)
+    x = torch.randn(m, k, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=cuda, generator=g) * 0.1).bfloat16()
+    ref = x.float() @ w.float().T
+    if kind == "residual":
+        r = torch.randn(m, n, device=cuda, generator=g).bfloat16()
+        want = r.float() + ref
+        r2 = r.clone()
+        ops.linear(x, w, residual=r)
+        ops.linear(x, w, residual=r2)
+        assert torch.equal(r, r2)
+        assert rel_err(r, want) < 1e-2
+    elif kind == "store":
+        y = ops.linear(x, w)
+        assert torch.equal(y, ops.linear(x, w))
+        assert rel_err(y, ref) < 1e-2
+    elif kind == "swiglu":
+        wg, wu = w[:n // 2], w[n // 2:]
+        y = ops.linear_swiglu(x, ops.interleave_gate_up(wg, wu))
+        want = F.silu(x.float() @ wg.float().T) * (x.float() @ wu.float().T)
+        assert rel_err(y, want) < 1e-2
+    elif kind == "rope":
+        pos = torch.randint(0, 3000, (m,), device=cuda, generator=g)
+        inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, dtype=torch.float32, device=cuda) / hd))
+        rot = n - 2 * hd if hd == 128 else n - 3 * hd  # v heads at the end stay unrotated
+        y = ops.linear_rope(x, w, ops.rope_table(pos, inv), rot, hd)
+        proj = ops.linear(x, w)
+        want = proj.float().clone()
+        want[:, :rot] = _rope_ref(proj[:, :rot].view(m, -1, hd), pos, inv, hd).reshape(m, -1)
+        assert rel_err(y, want) < 1e-2
+    else:
+        xq, xs = ops.quantize_e4m3(x)
+        wq, ws = ops.quantize_e4m3(w)
+        r = torch.randn(m, n, device=cuda, generator=g).bfloat16()
+        want = r.float() + (xq.float() * xs.view(-1, 1)) @ (wq.float() * ws.view(-1, 1)).T
+        ops.linear_e4m3(xq, xs, wq, ws, residual=r)
+        assert rel_err(r, want) < 1e-2
+
+
 def test_gemm_stream_k_epilogues(cuda):
     g = torch.Generator(device=cuda).manual_seed(9)
     m, k = 300, 8192
