@@ -10,7 +10,8 @@
 // loop of tile i+1. For M >= 256 a CTA-pair variant computes 256 x 256 tiles
 // in a grouped order that keeps the smaller operand's slice resident in L2,
 // and splits the last ragged wave of deep (>= 128 K iterations) tiles by K
-// across all pairs (stream-K, partial sums reduced in a fixed order).
+// across all pairs (stream-K, partial sums reduced in a fixed order); a ragged
+// last wave of shallower tiles runs as narrow column slices on the idle pairs.
 // Each epilogue warp stages 32 x 32 output chunks in shared memory and sends
 // them with TMA stores (the residual arrives by TMA load the same way).
 //
