@@ -419,6 +419,53 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// e4m3 codes of lo and hi (round to nearest even, saturating to +-448) in bits 0-7 and 8-15.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// a / s rounded to nearest fp32 without a division, given r = 1 / s rounded to nearest:
+// q0 = a r is within 1.5 ulp of a / s; one residual correction q1 = q0 + (a - s q0) r makes
+// it faithful (within 1 ulp), and then, by Markstein's theorem (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990;
+// restated in Muller et al., Handbook of Floating-Point Arithmetic, on division with an FMA),
+// the residual a - s q1 is exact in an FMA and q1 + (a - s q1) r rounds to a / s. Five FMA-pipe
+// operations where a division costs a reciprocal on the shared conversion unit plus a
+// refinement. It holds while the residuals do not underflow. In the e4m3 quantisers
+// s >= 1e-12 / 448 > 2^-49 and |a| <= 448 s, so every quotient whose code is not +-0
+// (|a / s| >= 2^-10) has |a| > 2^-59 and exact residuals; smaller quotients convert to +-0
+// whatever their last bits (checked against IEEE division on 3.2e9 such pairs). The quotient
+// of |a| takes a's sign at the end (rounding to nearest is symmetric), so that a zero or
+// underflowing quotient keeps its sign: a residual correction would turn -0 into +0.
+__device__ __forceinline__ float div_rn_fma(float a, float s, float r) {
+  const float m = fabsf(a);
+  const float q0 = m * r;
+  const float q1 = fmaf(fmaf(-s, q0, m), r, q0);
+  const float q = fmaf(fmaf(-s, q1, m), r, q1);
+  return __int_as_float(__float_as_int(q) | (__float_as_int(a) & static_cast<int>(0x80000000u)));
+}
+
+// e4m3 codes of the fp32 quotients a / s and b / s (each rounded to fp32 first, as an IEEE
+// division then a cast to float8_e4m3fn does), given r = 1 / s rounded to nearest; one
+// conversion for the pair.
+__device__ __forceinline__ uint32_t e4m3x2_div(float a, float b, float s, float r) {
+  return cvt_e4m3x2(div_rn_fma(a, s, r), div_rn_fma(b, s, r));
+}
+
+// Eight bf16 values (one 16-byte vector) to eight e4m3 codes of value / s, in order.
+__device__ __forceinline__ uint2 e4m3x8_div(const uint4& v, float s, float r) {
+  const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&v);
+  uint32_t c[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __bfloat1622float2(e[k]);
+    c[k] = e4m3x2_div(f.x, f.y, s, r);
+  }
+  return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+}
+
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 

@@ -219,6 +219,57 @@ def test_rms_norm_modes(cuda):
     assert torch.equal(buf[:, :128], before[:, :128]) and torch.equal(buf[:, 5 * 128:], before[:, 5 * 128:])
 
 
+def _e4m3_rows(cols, g):
+    """Rows that stress per-row e4m3 quantisation: spread-out magnitudes, exact ties (a row
+    max of 448 * 2^k makes the scale a power of two, so values at e4m3 midpoints divide
+    exactly onto them), signed zeros and values that round to zero."""
+    rows = [torch.randn(cols, generator=g) * 10.0 ** torch.empty(1).uniform_(-3, 3, generator=g)
+            for _ in range(24)]
+    mids = torch.tensor([1.0625, 1.1875, 0.0078125 * 1.5, 3.25, -1.0625, -13.0, 2.0 ** -10, 2.0 ** -9 * 1.5])
+    for k in (0, -3, 4):
+        r = mids[torch.randint(0, len(mids), (cols,), generator=g)] * 2.0 ** k
+        r[0] = 448.0 * 2.0 ** k
+        rows.append(r)
+    z = torch.zeros(cols)
+    z[1::2] = -0.0
+    z[3] = 1e-5
+    z[5] = -3e-6
+    rows.append(z)
+    return torch.stack(rows).bfloat16()
+
+
+def _e4m3_codes(x):
+    xf = x.float()
+    scale = xf.abs().amax(dim=-1, keepdim=True).clamp(min=1e-12) / 448.0
+    return (xf / scale).to(torch.float8_e4m3fn).view(torch.uint8), scale.flatten()
+
+
+# Codes bit for bit (signed zeros included) against the reference's (x / scale).to(e4m3)
+# on the CPU: the vector kernel (<= 8192 columns, 128 threads per row; <= 16384, 256), the
+# one-block-per-row kernel beyond that, and the product-with-bracket quotient's division
+# fallback on exact ties.
+@pytest.mark.parametrize("cols", [528, 2560, 4096, 9216, 14336, 16400])
+def test_quantize_e4m3_codes(cuda, cols):
+    g = torch.Generator().manual_seed(cols)
+    x = _e4m3_rows(cols, g)
+    q, s = ops.quantize_e4m3(x.to(cuda))
+    want_q, want_s = _e4m3_codes(x)
+    assert torch.equal(s.cpu(), want_s)
+    assert torch.equal(q.view(torch.uint8).cpu(), want_q)
+
+
+@pytest.mark.parametrize("cols", [1024, 2560, 4096])
+def test_rms_norm_fp8_codes(cuda, cols):
+    g = torch.Generator().manual_seed(cols)
+    x = _e4m3_rows(cols, g).to(cuda)
+    w = (1 + 0.1 * torch.randn(cols, generator=g)).bfloat16().to(cuda)
+    y = ops.rms_norm(x, w, 1e-6)
+    _, q8, sc = ops.rms_norm(x, w, 1e-6, fp8=True)
+    want_q, want_s = _e4m3_codes(y.cpu())
+    assert torch.equal(sc.cpu(), want_s)
+    assert torch.equal(q8.view(torch.uint8).cpu(), want_q)
+
+
 def test_rms_norm_fp8_fused(cuda):
     g = torch.Generator(device=cuda).manual_seed(5)
     x = torch.randn(64, 2560, device=cuda, generator=g).bfloat16()
