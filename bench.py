@@ -366,6 +366,21 @@ def run_dan(args, world, rank, local):
                                 "sample": f"oracle fp32, {SAMPLE_LAYERS} of 32 layers of Llama-3-8B over one "
                                           f"request ({ctok} tokens), time x{32 // SAMPLE_LAYERS}"}
     print(json.dumps(line), flush=True)
+    if args.breakdown:  # every entry point over the same batches again, to stderr
+        full = profiling.KernelTimer()
+        torch.cuda.synchronize()
+        with full:
+            for b in timed:
+                step_device(model, b)
+        rows = sorted(full.summary().items(), key=lambda kv: -kv[1]["ms_total"])
+        total = sum(v["ms_total"] for _, v in rows)
+        n = len(timed)
+        print(f"# configuration {cid}: device time per entry point over {n} steps (CUDA events around each "
+              f"launch; sum {total / n:.3f} ms/step)", file=sys.stderr)
+        for k, v in rows:
+            print(f"#   {k:44s} {v['launches'] / n:6.1f}/step {v['ms_total'] / n:8.3f} ms/step "
+                  f"{1000 * v['ms_total'] / max(v['launches'], 1):9.1f} us/launch {100 * v['ms_total'] / total:5.1f}%",
+                  file=sys.stderr)
 
 
 def main():
@@ -375,6 +390,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="dan", choices=["dan", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="after the JSON line, time every kernel entry point over the timed batches (stderr)")
     ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5],
                     help="3 (default): Llama-3-8B bf16; 4: Qwen3.5-4B-style hybrid; 5: Llama-3-8B FP8 + prefix pool")
     args = ap.parse_args()

@@ -194,10 +194,56 @@ __global__ void rms_norm_kernel(const __nv_bfloat16* x, int64_t x_outer, int64_t
 
 // ---------------------------------------------------------------- per-row e4m3
 // scale = max(amax |x|, 1e-12) / 448 ; q = e4m3(x / scale)   (fused.py:85-91, quant.py:26-33)
-// One block per row, the row read twice (amax, then codes; the second pass mostly from L2).
-// Measured against a row-in-registers single pass (persistent with the next row prefetched,
-// and not): this keeps 8 blocks per SM in flight, and the e4m3 conversions, on the shared
-// conversion unit, bound all of them.
+// Rows of up to TPR * VPT 16-byte vectors: TPR threads per row (128 or 256), 256 / TPR rows
+// per block; each thread issues its VPT loads of the row at once and keeps the row in
+// registers, so the row is read once and the amax, then the codes, come from registers.
+template <int VPT, int TPR>
+__global__ void __launch_bounds__(256) quant_rows_vec_kernel(const __nv_bfloat16* x, int64_t ldx, uint8_t* q,
+                                                             int64_t ldq, float* scale, int rows, int cols) {
+  constexpr int W = TPR / 32;  // warps per row
+  __shared__ float red[256 / TPR][W];
+  const int rg = threadIdx.x / TPR, t = threadIdx.x % TPR, wg = t >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (256 / TPR) + rg;
+  const bool live = r < rows;
+  const __nv_bfloat16* xr = x + static_cast<int64_t>(live ? r : 0) * ldx;
+  const int nvec = cols / 8;
+  uint4 buf[VPT];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = t + TPR * i;
+    if (live && v < nvec) buf[i] = reinterpret_cast<const uint4*>(xr)[v];
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = t + TPR * i;
+    if (live && v < nvec) {
+      const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&buf[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(e[k]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+  amax = warp_max(amax);
+  if (lane == 0) red[rg][wg] = amax;
+  __syncthreads();
+  amax = red[rg][0];
+#pragma unroll
+  for (int k = 1; k < W; ++k) amax = fmaxf(amax, red[rg][k]);
+  if (!live) return;
+  const float s = fmaxf(amax, 1e-12f) / 448.f, rcp = __frcp_rn(s);
+  uint8_t* qr = q + static_cast<int64_t>(r) * ldq;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = t + TPR * i;
+    if (v < nvec) reinterpret_cast<uint2*>(qr)[v] = e4m3x8_div(buf[i], s, rcp);
+  }
+  if (t == 0) scale[r] = s;
+}
+
+// Rows longer than 16384 columns: one block per row, the row read twice (amax, then codes).
 __global__ void quant_rows_kernel(const __nv_bfloat16* x, int64_t ldx, uint8_t* q, int64_t ldq, float* scale,
                                   int rows, int cols) {
   const int r = blockIdx.x;
@@ -487,7 +533,20 @@ DAN_API int dan_quantize_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* qb = static_cast<uint8_t*>(q);
-  ew::quant_rows_kernel<<<rows, 256, 0, st>>>(xb, ldx, qb, ldq, scale, rows, cols);
+  // Measured at M = 3400 (graph-timed): 14336 columns 28.8 us, 4096 columns 8.5 us (two-pass
+  // block-per-row kernel 37.3 / 10.5 us; HBM time 22 / 6.3 us).
+  const int nvec = cols / 8;
+  const dim3 g2((rows + 1) / 2);
+  if (nvec <= 128 * 2)
+    ew::quant_rows_vec_kernel<2, 128><<<g2, 256, 0, st>>>(xb, ldx, qb, ldq, scale, rows, cols);
+  else if (nvec <= 128 * 4)
+    ew::quant_rows_vec_kernel<4, 128><<<g2, 256, 0, st>>>(xb, ldx, qb, ldq, scale, rows, cols);
+  else if (nvec <= 128 * 8)
+    ew::quant_rows_vec_kernel<8, 128><<<g2, 256, 0, st>>>(xb, ldx, qb, ldq, scale, rows, cols);
+  else if (nvec <= 256 * 8)
+    ew::quant_rows_vec_kernel<8, 256><<<rows, 256, 0, st>>>(xb, ldx, qb, ldq, scale, rows, cols);
+  else
+    ew::quant_rows_kernel<<<rows, 256, 0, st>>>(xb, ldx, qb, ldq, scale, rows, cols);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }
