@@ -139,9 +139,63 @@ def norm(iters):
     return {"ms": ms, "gbs": 2 * x.numel() * 2 / ms / 1e6}
 
 
+def _graph_time(fn, n=20, reps=5):
+    """Device time of one ``fn`` call in ms, from ``reps`` replays of a CUDA graph holding ``n``
+    calls (for kernels shorter than the host's per-launch overhead; ``fn`` must not allocate)."""
+    fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(n):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / (n * reps)
+
+
+def quant(iters):
+    """Per-row e4m3 quantisation at configuration-5 sizes (3400 rows: the attention output,
+    4096 columns, and the SwiGLU output, 14336) and the e4m3-fused RMSNorm, graph-timed."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    cases = []
+    for name, m, k in (("quant_4096", 3400, 4096), ("quant_14336", 3400, 14336), ("norm_e4m3_4096", 3400, 4096)):
+        x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+        w = (1 + 0.1 * torch.randn(k, device=dev, generator=g)).bfloat16()
+        q = torch.empty(m, k, dtype=torch.float8_e4m3fn, device=dev)
+        sc = torch.empty(m, dtype=torch.float32, device=dev)
+        if name.startswith("quant"):
+            fn = (lambda x=x, q=q, sc=sc: ops.quantize_e4m3(x, out=q, scale=sc))
+        else:
+            fn = (lambda x=x, w=w, q=q, sc=sc, m=m, k=k: _lib.call(
+                "dan_rms_norm", _lib.ptr(x), x.stride(0), x.stride(0), 1, _lib.ptr(w), 1e-5, 0, None, 0, 0,
+                _lib.ptr(q), q.stride(0), _lib.ptr(sc), m, k, _lib.stream()))
+        cases.append((name, m, k, fn))
+    for _, _, _, fn in cases:  # one plain launch of each first (the launches a profiler picks up)
+        fn()
+    out = {}
+    for name, m, k, fn in cases:
+        ms = _graph_time(fn, n=max(iters, 2) * 5)
+        hbm = m * k * 3 + m * 4  # bf16 in, e4m3 out, scales
+        out[name] = {"rows": m, "cols": k, "us": 1000 * ms, "gbs": hbm / ms / 1e6}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "norm", "fp8peak"])
+    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "norm", "quant", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()
     res = globals()[a.case](max(a.iters, 2))
