@@ -337,15 +337,19 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
   }
   // ---- K K^T -> A and Q K^T -> P (warp: rows [16 tm, +16), columns [32 sh, +32))
   {
+    // 16-column blocks 2 sh + np past the warp's row block tm lie above the diagonal, where A
+    // and P are masked to zero: their products are skipped (warp-uniform).
     const int tm = warp & 3, sh = warp >> 2;
+    const int nb = tm - 2 * sh + 1;  // column blocks of this warp at or below the diagonal (<= 2)
     float G[4][4] = {}, Pq[4][4] = {};
 #pragma unroll 1
-    for (int kk = 0; kk < DK / 16; ++kk) {
+    for (int kk = 0; nb > 0 && kk < DK / 16; ++kk) {
       uint32_t ak[4], aq[4];
       ldsm4(ak, a_rows(sm.kn, LDW, 16 * tm, 16 * kk, lane));
       ldsm4(aq, a_rows(sm.qn, LDW, 16 * tm, 16 * kk, lane));
 #pragma unroll
       for (int np = 0; np < 2; ++np) {
+        if (np >= nb) break;
         uint32_t b[4];
         ldsm4(b, b_nrows(sm.kn, LDW, 32 * sh + 16 * np, 16 * kk, lane));
         mma16816(G[2 * np], ak, b[0], b[1]);
@@ -448,11 +452,12 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
     st_bf2(&sm.tg[t * LDN + s2], t0 * sm.eg[s2], t1 * sm.eg[s2 + 1]);
   }
   __syncthreads();
-  // ---- T'V and W = T diag(βγ) K (warp: rows [16 tm, +16), columns [64 tn, +64))
+  // ---- T'V and W = T diag(βγ) K (warp: rows [16 tm, +16), columns [64 tn, +64)); T is lower
+  // triangular, so row block tm only meets the key blocks kk <= tm.
   const int tm = warp & 3, tn = warp >> 2;
   float au[8][4] = {}, aw[8][4] = {};
 #pragma unroll 1
-  for (int kk = 0; kk < CH / 16; ++kk) {
+  for (int kk = 0; kk <= tm; ++kk) {
     uint32_t a1[4], a2[4];
     ldsm4(a1, a_rows(sm.tb, LDN, 16 * tm, 16 * kk, lane));
     ldsm4(a2, a_rows(sm.tg, LDN, 16 * tm, 16 * kk, lane));
