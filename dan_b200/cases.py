@@ -165,6 +165,29 @@ def _graph_time(fn, n=20, reps=5):
     return s.elapsed_time(e) / (n * reps)
 
 
+def conv(iters):
+    """Causal conv + SiLU of configuration-4 batches (8192 channels: q, k, v of 16 / 16 / 32
+    heads x 128), graph-timed, three seeded batches."""
+    from .qwen3_5 import RecurrentLayout
+
+    dev = torch.device("cuda")
+    out = {}
+    for seed in (0, 1, 2):
+        ids, pos, segs, reads, _ = _pack(4, seed)
+        n, c = len(ids), 8192
+        g = torch.Generator(device=dev).manual_seed(0)
+        pre = (torch.randn(n, c, device=dev, generator=g) * 0.5).bfloat16()
+        w = (torch.randn(c, 4, device=dev, generator=g) * 0.5).bfloat16()
+        rl = RecurrentLayout.build(segs, n, 3, dev)
+        y = torch.empty(n, c, dtype=torch.bfloat16, device=dev)
+        fn = (lambda pre=pre, w=w, rl=rl, y=y, n=n: _lib.call(
+            "dan_causal_conv", _lib.ptr(pre), c, None, 0, _lib.ptr(w), _lib.ptr(rl.prev), _lib.ptr(y), c, n, c,
+            _lib.stream()))
+        ms = _graph_time(fn, n=max(iters, 2) * 5)
+        out[f"batch{seed}"] = {"rows": n, "us": 1000 * ms, "gbs": 2 * n * c * 2 / ms / 1e6}
+    return out
+
+
 def quant(iters):
     """Per-row e4m3 quantisation at configuration-5 sizes (3400 rows: the attention output,
     4096 columns, and the SwiGLU output, 14336) and the e4m3-fused RMSNorm, graph-timed."""
@@ -195,7 +218,7 @@ def quant(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "norm", "quant", "fp8peak"])
+    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "norm", "quant", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()
     res = globals()[a.case](max(a.iters, 2))
