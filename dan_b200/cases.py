@@ -188,6 +188,24 @@ def conv(iters):
     return out
 
 
+def gnorm(iters):
+    """Gated RMSNorm of a configuration-4 batch (7189 rows x 32 value heads x 128), graph-timed."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    n, hv, dv = 7189, 32, 128
+    x = torch.randn(n, hv * dv, device=dev, generator=g).bfloat16()
+    zz = torch.randn(n, 2 * hv * dv, device=dev, generator=g).bfloat16()  # gate z strided inside a wider row
+    z = zz[:, hv * dv:]
+    w = (1 + 0.1 * torch.randn(dv, device=dev, generator=g)).bfloat16()
+    y = torch.empty(n, hv * dv, dtype=torch.bfloat16, device=dev)
+    fn = lambda: _lib.call("dan_gated_rms_norm", _lib.ptr(x), hv * dv, _lib.ptr(z), zz.stride(0), _lib.ptr(w), 1e-6,
+                           _lib.ptr(y), hv * dv, n, hv, dv, _lib.stream())
+    ms = _graph_time(fn, n=max(iters, 2) * 5)
+    fn()
+    torch.cuda.synchronize()
+    return {"rows": n, "us": 1000 * ms, "gbs": 3 * n * hv * dv * 2 / ms / 1e6, "sum": float(y.float().sum())}
+
+
 def quant(iters):
     """Per-row e4m3 quantisation at configuration-5 sizes (3400 rows: the attention output,
     4096 columns, and the SwiGLU output, 14336) and the e4m3-fused RMSNorm, graph-timed."""
@@ -218,7 +236,7 @@ def quant(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "norm", "quant", "fp8peak"])
+    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()
     res = globals()[a.case](max(a.iters, 2))

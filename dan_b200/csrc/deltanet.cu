@@ -49,6 +49,9 @@ __device__ __forceinline__ const __nv_bfloat16* code_row(int code, const __nv_bf
 // the row loop), 69.8 with the halo up front, 62.6 with eight channels and 8 rows at three
 // blocks per SM (spilling).
 constexpr int CONV_ROWS = 12, CONV_CPT = 4;
+// (row, head) items per warp of the gated norm at dv = 128; graph-timed on 7189 x 32 x 128:
+// 1 / 2 / 4 / 8 items = 49.2 / 44.6 / 49.1 / 58.8 us (one item per warp before: 48.0).
+constexpr int GNORM_ITEMS = 2;
 __global__ void __launch_bounds__(256, 4) causal_conv_kernel(const __nv_bfloat16* src, int64_t ld_src,
                                                           const __nv_bfloat16* hist, int64_t ld_hist,
                                                           const __nv_bfloat16* w, const int* prev,
@@ -762,41 +765,56 @@ __global__ void gated_rms_norm_kernel(const __nv_bfloat16* x, int64_t ldx, const
 }
 
 // Vector form for dv = 4 V (V = 1, 2): lane l holds elements [4 V l, 4 V l + 4 V) of its (row,
-// head) in registers from one 8 V-byte load of x and of z, so x is read once.
-template <int V>
-__global__ void gated_rms_norm_vec_kernel(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* z, int64_t ldz,
-                                          const __nv_bfloat16* w, float eps, __nv_bfloat16* y, int64_t ldy, int rows,
-                                          int heads) {
+// head) in registers from one 8 V-byte load of x and of z, so x is read once. A warp takes
+// ITEMS consecutive (row, head) items and issues all their loads before the first reduction,
+// so each warp keeps ITEMS x 16 V bytes per lane in flight (the SiLU's exponential and
+// reciprocal then overlap other warps' loads).
+template <int V, int ITEMS>
+__global__ void __launch_bounds__(256) gated_rms_norm_vec_kernel(const __nv_bfloat16* x, int64_t ldx,
+                                                                 const __nv_bfloat16* z, int64_t ldz,
+                                                                 const __nv_bfloat16* w, float eps, __nv_bfloat16* y,
+                                                                 int64_t ldy, int rows, int heads) {
   using Vec = typename std::conditional<V == 1, uint2, uint4>::type;
   constexpr int E = 4 * V, DV = 32 * E;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t total = static_cast<int64_t>(rows) * heads;
+  const int64_t gw0 = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * ITEMS;
   const int lane = threadIdx.x & 31;
-  if (gw >= rows * heads) return;
-  const int r = gw / heads, h = gw % heads;
-  const int64_t off = h * DV + lane * E;
-  const Vec xv = *reinterpret_cast<const Vec*>(x + static_cast<int64_t>(r) * ldx + off);
-  const Vec zv = *reinterpret_cast<const Vec*>(z + static_cast<int64_t>(r) * ldz + off);
+  if (gw0 >= total) return;
   const Vec wv = *reinterpret_cast<const Vec*>(w + lane * E);
-  const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
-  const __nv_bfloat16* ze = reinterpret_cast<const __nv_bfloat16*>(&zv);
+  Vec xv[ITEMS], zv[ITEMS];
+  int64_t yoff[ITEMS];
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) {
+    const int64_t gw = gw0 + k < total ? gw0 + k : total - 1;
+    const int64_t r = gw / heads, h = gw - r * heads;
+    const int64_t off = h * DV + lane * E;
+    xv[k] = *reinterpret_cast<const Vec*>(x + r * ldx + off);
+    zv[k] = *reinterpret_cast<const Vec*>(z + r * ldz + off);
+    yoff[k] = r * ldy + off;
+  }
   const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
-  float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < E; ++i) {
-    const float f = __bfloat162float(xe[i]);
-    ss += f * f;
+  for (int k = 0; k < ITEMS; ++k) {
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[k]);
+    const __nv_bfloat16* ze = reinterpret_cast<const __nv_bfloat16*>(&zv[k]);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float f = __bfloat162float(xe[i]);
+      ss += f * f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / DV + eps);
+    Vec yv;
+    __nv_bfloat16* ye = reinterpret_cast<__nv_bfloat16*>(&yv);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float t = bf16_round(__bfloat162float(we[i]) * bf16_round(__bfloat162float(xe[i]) * inv));
+      ye[i] = __float2bfloat16_rn(t * silu(__bfloat162float(ze[i])));
+    }
+    if (gw0 + k < total) *reinterpret_cast<Vec*>(y + yoff[k]) = yv;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / DV + eps);
-  Vec yv;
-  __nv_bfloat16* ye = reinterpret_cast<__nv_bfloat16*>(&yv);
-#pragma unroll
-  for (int i = 0; i < E; ++i) {
-    const float t = bf16_round(__bfloat162float(we[i]) * bf16_round(__bfloat162float(xe[i]) * inv));
-    ye[i] = __float2bfloat16_rn(t * silu(__bfloat162float(ze[i])));
-  }
-  *reinterpret_cast<Vec*>(y + static_cast<int64_t>(r) * ldy + off) = yv;
 }
 
 }  // namespace delta
@@ -892,14 +910,16 @@ DAN_API int dan_gated_rms_norm(const void* x, int64_t ldx, const void* z, int64_
   const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if ((dv == 128 || dv == 256) && a16(x) && a16(z) && a16(w) && a16(y) && ldx % 8 == 0 && ldz % 8 == 0 &&
       ldy % 8 == 0) {
-    const unsigned grid = static_cast<unsigned>((warps * 32 + 255) / 256);
+    constexpr int kItems128 = delta::GNORM_ITEMS, kItems256 = kItems128 > 1 ? kItems128 / 2 : 1;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (dv == 128)
-      delta::gated_rms_norm_vec_kernel<1><<<grid, 256, 0, s>>>(
+      delta::gated_rms_norm_vec_kernel<1, kItems128><<<static_cast<unsigned>((warps + 8 * kItems128 - 1) /
+                                                                             (8 * kItems128)), 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(z), ldz,
           static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
     else
-      delta::gated_rms_norm_vec_kernel<2><<<grid, 256, 0, s>>>(
+      delta::gated_rms_norm_vec_kernel<2, kItems256><<<static_cast<unsigned>((warps + 8 * kItems256 - 1) /
+                                                                             (8 * kItems256)), 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(z), ldz,
           static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
     DAN_CUDA(cudaGetLastError());
