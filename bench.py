@@ -251,8 +251,12 @@ def run_dan(args, world, rank, local):
     hbm, pk_burst, pk_sust, pk_kind = peaks()
     launches0 = profiling.total_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # Per-launch events of the roofline kernels, created before the timed region: creating them
+    # inside it cost ~1% (configuration 3) to ~3.5% (configuration 5) of the step; recording
+    # pre-created ones ~0% / ~1.4%.
     timer = profiling.KernelTimer({"dan_gemm_bf16", "dan_gemm_bf16_rope", "dan_gemm_e4m3", "dan_gemm_e4m3_rope",
                                    "dan_tree_attention", "dan_gated_delta_scan"})
+    timer.reserve(2 * 8 * cfg["num_hidden_layers"] * len(timed))
     with Clocks(local) as clocks:
         barrier(world, device)
         torch.cuda.synchronize()
@@ -367,8 +371,7 @@ def run_dan(args, world, rank, local):
                                           f"request ({ctok} tokens), time x{32 // SAMPLE_LAYERS}"}
     print(json.dumps(line), flush=True)
     if args.breakdown:  # every entry point over the same batches again, to stderr
-        full = profiling.KernelTimer()
-        torch.cuda.synchronize()
+        full = profiling.KernelTimer().reserve(2 * 16 * cfg["num_hidden_layers"] * len(timed))
         with full:
             for b in timed:
                 step_device(model, b)

@@ -77,7 +77,7 @@ def call(name, *args, work=0, key=None):
     fn = getattr(lib(), name)
     timer = profiling.active()
     if timer is not None and timer.wants(name):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s, e = timer.event(), timer.event()
         s.record()
         rc = fn(*args)
         e.record()

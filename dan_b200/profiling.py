@@ -15,6 +15,20 @@ class KernelTimer:
     def __init__(self, names=None):
         self.names = set(names) if names else None
         self.records = defaultdict(list)  # name -> [(start, end, work)]
+        self._pool = []
+
+    def reserve(self, n):
+        """Create ``n`` events ahead of the timed region (each recorded once, which makes CUDA
+        allocate it), so that timing a launch costs two event records and no event creation."""
+        for _ in range(n):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._pool.append(ev)
+        torch.cuda.synchronize()
+        return self
+
+    def event(self):
+        return self._pool.pop() if self._pool else torch.cuda.Event(enable_timing=True)
 
     def __enter__(self):
         global _timer
