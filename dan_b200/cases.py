@@ -132,11 +132,26 @@ def fp8peak(iters):
 
 
 def norm(iters):
+    """RMSNorm shapes of the benchmark configurations, graph-timed: the Llama-3-8B hidden norm
+    (4096), the Qwen3.5-4B hidden norm (2560, zero-centred) and its per-head q / k norms (16 heads
+    x 256 in place on a strided q/k/v buffer)."""
     dev = torch.device("cuda")
-    x = torch.randn(7089, 4096, device=dev).bfloat16()
-    w = torch.ones(4096, device=dev).bfloat16()
-    ms = _time(lambda: ops.rms_norm(x, w, 1e-5), iters)
-    return {"ms": ms, "gbs": 2 * x.numel() * 2 / ms / 1e6}
+    g = torch.Generator(device=dev).manual_seed(0)
+    out = {}
+    for name, n, cols, zc in (("hidden_4096", 7089, 4096, False), ("hidden_2560", 7189, 2560, True)):
+        x = torch.randn(n, cols, device=dev, generator=g).bfloat16()
+        w = (0.1 * torch.randn(cols, device=dev, generator=g)).bfloat16()
+        y = torch.empty_like(x)
+        ms = _graph_time(lambda x=x, w=w, y=y, zc=zc: ops.rms_norm(x, w, 1e-6, zero_centered=zc, out=y),
+                         n=max(iters, 2) * 5)
+        out[name] = {"us": 1000 * ms, "gbs": 2 * x.numel() * 2 / ms / 1e6}
+    n, heads, d = 7189, 16, 256
+    qkv = torch.randn(n, (heads + 2 * 4) * d * 2, device=dev, generator=g).bfloat16()
+    q = qkv[:, :heads * d * 2].view(n, heads, 2 * d)[:, :, :d]  # q interleaved with its gate (head stride 2 D)
+    w = (0.1 * torch.randn(d, device=dev, generator=g)).bfloat16()
+    ms = _graph_time(lambda: ops.rms_norm(q, w, 1e-6, zero_centered=True, out=q), n=max(iters, 2) * 5)
+    out["per_head_q_16x256"] = {"us": 1000 * ms, "gbs": 2 * n * heads * d * 2 / ms / 1e6}
+    return out
 
 
 def _graph_time(fn, n=20, reps=5):
