@@ -221,6 +221,30 @@ def gnorm(iters):
     return {"rows": n, "us": 1000 * ms, "gbs": 3 * n * hv * dv * 2 / ms / 1e6, "sum": float(y.float().sum())}
 
 
+def readout(iters):
+    """Fused label readout (final norm of each question's read row, label logits against a
+    Llama-3-sized vocabulary, softmax), graph-timed: 48 questions with 2-26 labels (configuration
+    3) and with 2-255 labels (configuration 5)."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    hidden, vocab, n = 4096, 128256, 7089
+    h = torch.randn(n, hidden, device=dev, generator=g).bfloat16()
+    nw = (1 + 0.1 * torch.randn(hidden, device=dev, generator=g)).bfloat16()
+    wlm = (0.02 * torch.randn(vocab, hidden, device=dev, generator=g)).bfloat16()
+    out = {}
+    for name, kmax in (("labels_2_26", 26), ("labels_2_255", 255)):
+        counts = torch.randint(2, kmax + 1, (48,), generator=torch.Generator().manual_seed(kmax))
+        off = torch.zeros(49, dtype=torch.int32)
+        off[1:] = torch.cumsum(counts, 0)
+        ids = torch.randint(0, vocab, (int(off[-1]),), dtype=torch.int32, device=dev, generator=g)
+        rows = torch.randint(0, n, (48,), dtype=torch.int32, device=dev, generator=g)
+        offd = off.to(dev)
+        ms = _graph_time(lambda rows=rows, ids=ids, offd=offd, kmax=kmax: ops.label_readout(
+            h, rows, nw, 1e-5, False, wlm, ids, offd, kmax), n=max(iters, 2) * 5)
+        out[name] = {"labels": int(off[-1]), "us": 1000 * ms, "label_gbs": int(off[-1]) * hidden * 2 / ms / 1e6}
+    return out
+
+
 def quant(iters):
     """Per-row e4m3 quantisation at configuration-5 sizes (3400 rows: the attention output,
     4096 columns, and the SwiGLU output, 14336) and the e4m3-fused RMSNorm, graph-timed."""
@@ -251,7 +275,7 @@ def quant(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "fp8peak"])
+    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "readout", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()
     res = globals()[a.case](max(a.iters, 2))

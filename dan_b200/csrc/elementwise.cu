@@ -413,11 +413,21 @@ __global__ void readout_kernel(const __nv_bfloat16* h, int64_t ldh, const int* r
     }
     const __nv_bfloat16* wr = wlm + id * ldw;
     float acc = 0.f;
-    for (int c = lane * 8; c < hidden; c += 256) {
-      const uint4 v = *reinterpret_cast<const uint4*>(wr + c);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+    // Four 16-byte loads of the label row in flight per lane before they are used (same
+    // accumulation order per lane as one at a time).
+    for (int c0 = lane * 8; c0 < hidden; c0 += 4 * 256) {
+      uint4 v[4];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) acc += __bfloat162float(e[t]) * sh[c + t];
+      for (int u = 0; u < 4; ++u)
+        if (c0 + 256 * u < hidden) v[u] = *reinterpret_cast<const uint4*>(wr + c0 + 256 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 256 * u;
+        if (c >= hidden) break;
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[u]);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc += __bfloat162float(e[t]) * sh[c + t];
+      }
     }
     acc = warp_sum(acc);
     if (lane == 0) lg[j - a] = acc;
@@ -623,7 +633,8 @@ DAN_API int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, 
   DAN_REQUIRE(smem <= 200 * 1024, "label_readout: hidden %d too large", hidden);
   static std::atomic<uint64_t> configured{0};
   if (smem > 48 * 1024) DAN_CUDA(smem_limit_once(ew::readout_kernel, 200 * 1024, configured));
-  ew::readout_kernel<<<n_questions, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+  // 16 warps per question: up to 255 labels (configuration 5) are 16 rows per warp, not 32.
+  ew::readout_kernel<<<n_questions, 512, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(h), ldh, read_rows, static_cast<const __nv_bfloat16*>(norm_w), eps, mode,
       static_cast<const __nv_bfloat16*>(w_lm), ldw, vocab, label_ids, offsets, hidden, logits, probs, status);
   DAN_CUDA(cudaGetLastError());
