@@ -245,6 +245,21 @@ def readout(iters):
     return out
 
 
+def gate(iters):
+    """Sigmoid output gate of the Qwen3.5-4B gated attention (7189 rows x 16 heads x 256, the
+    gate interleaved in the q/k/v projection at head stride 512), graph-timed."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    n, heads, d = 7189, 16, 256
+    o = torch.randn(n, heads * d, device=dev, generator=g).bfloat16()
+    qg = torch.randn(n, heads * 2 * d, device=dev, generator=g).bfloat16()
+    gate = qg[:, d:]  # head h's gate at columns [2 d h + d, 2 d h + 2 d)
+    fn = lambda: _lib.call("dan_sigmoid_gate", _lib.ptr(o), o.stride(0), _lib.ptr(gate), qg.stride(0), 2 * d, d, n,
+                           heads * d, _lib.stream())
+    ms = _graph_time(fn, n=max(iters, 2) * 5)
+    return {"us": 1000 * ms, "gbs": 3 * n * heads * d * 2 / ms / 1e6}
+
+
 def quant(iters):
     """Per-row e4m3 quantisation at configuration-5 sizes (3400 rows: the attention output,
     4096 columns, and the SwiGLU output, 14336) and the e4m3-fused RMSNorm, graph-timed."""
@@ -275,7 +290,7 @@ def quant(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "readout", "fp8peak"])
+    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "readout", "gate", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()
     res = globals()[a.case](max(a.iters, 2))
