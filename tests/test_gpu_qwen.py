@@ -124,3 +124,50 @@ def test_long_chunk_chain_vs_oracle(cuda):
     got, want = _scan_case(cuda, 1, 2, [(1500, [40, 64]), (64, [1])], seed=3)
     err = (got - want).abs().max().item() / want.abs().max().item()
     assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("rows,channels", [(1, 1032), (3, 512), (13, 1032), (25, 8192), (301, 1032)])
+def test_causal_conv_row_sources(cuda, rows, channels):
+    """dan_causal_conv against a float64 restatement of qwen3_5.py:218-220 row by row, at about
+    one bf16 step. Each row's three sources are drawn at random among the previous packed row
+    (taken from registers, including across the kernel's 12-row blocks), another packed row
+    (gathered), a zero row (code -1) and a history row (code -2 - i), with a channel count that
+    is not a multiple of the 1024 a block covers."""
+    gen = torch.Generator().manual_seed(rows * 7 + channels)
+    rng = random.Random(rows)
+    src = (torch.randn(rows, channels, generator=gen) * 0.7).bfloat16()
+    hist = (torch.randn(5, channels, generator=gen) * 0.7).bfloat16()
+    w = (torch.randn(channels, 4, generator=gen) * 0.5).bfloat16()
+    codes = torch.empty(rows, 3, dtype=torch.int32)
+    for r in range(rows):
+        for j in range(3):
+            kind = rng.random()
+            if kind < 0.6 and r - 1 - j >= 0:
+                codes[r, j] = r - 1 - j
+            elif kind < 0.75:
+                codes[r, j] = rng.randrange(rows)
+            elif kind < 0.9:
+                codes[r, j] = -1
+            else:
+                codes[r, j] = -2 - rng.randrange(5)
+
+    def row(code):
+        if code >= 0:
+            return src[code].double()
+        if code == -1:
+            return torch.zeros(channels, dtype=torch.float64)
+        return hist[-code - 2].double()
+
+    want = torch.empty(rows, channels, dtype=torch.float64)
+    wd = w.double()
+    for r in range(rows):
+        ext = [row(int(codes[r, 2])), row(int(codes[r, 1])), row(int(codes[r, 0])), src[r].double()]
+        acc = sum(wd[:, t] * ext[t] for t in range(4))
+        want[r] = torch.nn.functional.silu(acc)
+    src_d, hist_d, w_d, codes_d = src.to(cuda), hist.to(cuda), w.to(cuda), codes.to(cuda)
+    out = torch.empty(rows, channels, dtype=torch.bfloat16, device=cuda)
+    _lib.call("dan_causal_conv", _lib.ptr(src_d), channels, _lib.ptr(hist_d), channels, _lib.ptr(w_d),
+              _lib.ptr(codes_d), _lib.ptr(out), channels, rows, channels, _lib.stream())
+    got = out.double().cpu()
+    err = (got - want).abs() - (want.abs() * 2.0 ** -7 + 1e-5)
+    assert err.max().item() <= 0, (got - want).abs().max().item()
