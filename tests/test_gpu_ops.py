@@ -329,9 +329,12 @@ def test_gemm_rope_epilogue(cuda, d, heads, kv, fp8, k):
     assert rel_err(y, want) < 1e-2
 
 
-def test_embed_and_readout(cuda):
+# Hidden sizes of configurations 1, 4 and 3: the readout's label rows load 1024 elements per
+# warp step, so 576 and 2560 also take its remainder path.
+@pytest.mark.parametrize("hidden", [576, 2560, 4096])
+def test_embed_and_readout(cuda, hidden):
     g = torch.Generator(device=cuda).manual_seed(7)
-    vocab, hidden = 1000, 576
+    vocab = 1000
     table = torch.randn(vocab, hidden, device=cuda, generator=g).bfloat16()
     ids = torch.randint(0, vocab, (40,), device=cuda, generator=g)
     x = ops.embed(ids, table)
