@@ -19,10 +19,18 @@ probabilities, every step.
 Each rank runs an independent replica on its own batches (weak scaling, no
 collective on the data path).
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-oracle port, fp32, all host threads) on the same configuration and metric:
-each step is a bounded sample (a 1-layer slice of the model over one request,
-scaled to 32 layers).
+All ranks draw one seeded stream of batches and deal them so each rank times
+``steps`` batches with near-equal token totals; ``per_rank`` lists every
+rank's tokens and device time. ``attention_cfg2`` times the tree-attention
+kernel alone on a configuration-2 batch; ``cpu_baseline`` is dan's own CPU
+path on one of the timed batches (configuration 3, one GPU).
+
+``--impl reference`` runs dan itself: its unmodified ``Runner`` (fp32, all
+host threads, dense masked attention) from the offline install under
+baseline/_ref, on the same configuration-3 batches and metric. Each step reads
+one whole batch through a 1-layer Llama-3-8B-shaped checkpoint (full vocab);
+``ms_per_step`` is that measured time, and ``value`` counts the other 31
+layers at the hook-timed time of the one layer.
 """
 import argparse
 import json
@@ -131,58 +139,134 @@ def barrier(world, device):
         dist.barrier(device_ids=[device.index] if device.type == "cuda" else None)
 
 
-# ---------------------------------------------------------------------- CPU arm
-SAMPLE_LAYERS = 1
-_cpu_state = {}
+# ---------------------------------------------------------------------- reference arm
+# dan itself (its unmodified ``dan.runner.Runner``, fp32 on the host cores: the dense masked
+# attention path, attention.py:244-270) from the offline install under baseline/_ref.
+REF_SITE = os.path.join(ROOT, "baseline", "_ref")
+REF_LAYERS = 1  # decoder layers in the reference's checkpoint; the other 31 are counted from its time
+FULL_LAYERS = 32
 
 
-def cpu_sample(layers=SAMPLE_LAYERS, seed=0):
-    """The oracle (fp32 CPU restatement of the reference) over a ``layers``-layer slice of
-    Llama-3-8B on one configuration-3 request; returns (seconds, tokens, questions, threads)."""
-    from dan_b200 import synthetic
+def dan_reference():
+    """(dan.runner, None) from the offline install of the reference, or (None, why not)."""
+    if os.path.isdir(os.path.join(REF_SITE, "dan")) and REF_SITE not in sys.path:
+        sys.path.append(REF_SITE)
+    try:
+        import dan.runner as ref_runner
+    except Exception as e:  # noqa: BLE001 - any import failure makes the arm unavailable
+        return None, f"dan is not importable from baseline/_ref ({type(e).__name__}: {e})"
+    return ref_runner, None
+
+
+def reference_checkpoint(path, layers=REF_LAYERS, seed=0):
+    """A Llama-3-8B-shaped Hugging Face checkpoint with ``layers`` decoder layers and the full
+    128,256-token vocabulary, weights bf16 N(0, 0.02), seeded. The vocabulary matrix repeats one
+    seeded 8192-row block and lm_head is tied to it: writing and loading 2 x 1 GB of vocabulary
+    rows took most of a minute on a host, and the forward reads only the embedding rows of the
+    batch's tokens and the label rows, the same work tied or untied."""
+    from safetensors.torch import save_file
+
     from dan_b200.loader import llama3_8b_config
-    from oracle import llama as OL
-    from oracle import runner as OR
-    from oracle import weights as OW
 
-    torch.set_num_threads(os.cpu_count() or 1)
-    cfg = dict(llama3_8b_config(), num_hidden_layers=layers, vocab_size=1024)
-    if layers not in _cpu_state:
-        _cpu_state[layers] = OW.random_state(cfg, 0)
-    state = _cpu_state[layers]
-    import random
+    cfg = dict(llama3_8b_config(), num_hidden_layers=layers, architectures=["LlamaForCausalLM"],
+               tie_word_embeddings=True, torch_dtype="bfloat16", max_position_embeddings=131072,
+               hidden_act="silu", attention_bias=False, mlp_bias=False)
+    gen = torch.Generator().manual_seed(seed)
+    hd, inter, vocab = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    q, kv = cfg["num_attention_heads"] * cfg["head_dim"], cfg["num_key_value_heads"] * cfg["head_dim"]
 
-    plan = synthetic.request(3, random.Random(seed), 1024)
-    ids, pos, segs, reads, _ = OR.pack([plan])
-    t0 = time.perf_counter()
-    h = OL.hidden(state, cfg, ids, pos, segs)
-    for r, labels in reads:
-        OL.label_logits(state, h[r], labels)
-    dt = time.perf_counter() - t0
-    return dt, len(ids), len(reads), torch.get_num_threads()
+    def w(rows, cols):
+        return (torch.randn(rows, cols, generator=gen) * 0.02).bfloat16()
+
+    def vocab_rows():
+        blk = w(8192, hd)
+        return blk.repeat(-(-vocab // 8192), 1)[:vocab].contiguous()
+
+    state = {"model.embed_tokens.weight": vocab_rows(),
+             "model.norm.weight": (1 + 0.1 * torch.randn(hd, generator=gen)).bfloat16()}
+    for i in range(layers):
+        p = f"model.layers.{i}."
+        state.update({p + "input_layernorm.weight": (1 + 0.1 * torch.randn(hd, generator=gen)).bfloat16(),
+                      p + "post_attention_layernorm.weight": (1 + 0.1 * torch.randn(hd, generator=gen)).bfloat16(),
+                      p + "self_attn.q_proj.weight": w(q, hd), p + "self_attn.k_proj.weight": w(kv, hd),
+                      p + "self_attn.v_proj.weight": w(kv, hd), p + "self_attn.o_proj.weight": w(hd, q),
+                      p + "mlp.gate_proj.weight": w(inter, hd), p + "mlp.up_proj.weight": w(inter, hd),
+                      p + "mlp.down_proj.weight": w(hd, inter)})
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    save_file(state, os.path.join(path, "model.safetensors"))
+    return cfg
+
+
+class ReferenceRun:
+    """dan's ``Runner`` (fp32, CPU, all host threads) on a ``REF_LAYERS``-layer Llama-3-8B-shaped
+    checkpoint. ``step(plans)`` reads one packed batch through ``Runner.read_many`` and returns
+    (measured seconds, seconds scaled to 32 layers): the decoder layer is timed by forward hooks
+    (pre / post on ``model.model.layers[0]``) and the other 31 layers are counted at its time;
+    embedding, final norm, label logits and packing are measured once, as they run."""
+
+    def __init__(self, ref_runner):
+        import tempfile
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.threads = torch.get_num_threads()
+        shm = "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else None
+        with tempfile.TemporaryDirectory(dir=shm) as tmp:
+            reference_checkpoint(tmp)
+            self.runner = ref_runner.Runner(tmp, device="cpu", dtype=torch.float32, cache_bytes=0)
+        self.layer_s = []
+        layer = self.runner.model.model.layers[0]
+        layer.register_forward_pre_hook(lambda m, a: self.layer_s.append(-time.perf_counter()))
+        layer.register_forward_hook(lambda m, a, o: self.layer_s.append(self.layer_s.pop() + time.perf_counter()))
+
+    def step(self, plans):
+        self.layer_s.clear()
+        t0 = time.perf_counter()
+        self.runner.read_many(plans)
+        dt = time.perf_counter() - t0
+        layers = sum(self.layer_s)
+        return dt, dt + (FULL_LAYERS / REF_LAYERS - 1) * layers
+
+
+def plan_tokens(plans):
+    return sum(len(p.prefix) + sum(len(b.suffix) for b in p.branches) for p in plans)
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    full_layers = 32
-    vals, answers = [], []
-    for step in range(args.warmup + args.steps):
-        dt, tokens, questions, threads = cpu_sample(seed=step)
-        scale = full_layers / SAMPLE_LAYERS
-        if step >= args.warmup:
-            vals.append(tokens / (dt * scale))
-            answers.append(questions / (dt * scale))
-    v = statistics.median(vals)
+    from dan_b200 import synthetic
+
+    ref_runner, why = dan_reference()
+    if ref_runner is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    ref = ReferenceRun(ref_runner)
+    # the GPU arm's batches (rank 0's stream): warm-up batches first, then the timed ones
+    batches = synthetic.batches(3, args.warmup + args.steps + 1, seed=1000, vocab=128256)[1:]
+    measured, scaled, tokens, questions = [], [], 0, 0
+    for i, plans in enumerate(batches):
+        dt, full = ref.step(plans)
+        if i >= args.warmup:
+            measured.append(dt)
+            scaled.append(full)
+            tokens += plan_tokens(plans)
+            questions += sum(len(p.branches) for p in plans)
+    v = tokens / sum(scaled)
+    sample = (f"dan.runner.Runner (unmodified, fp32 CPU, dense masked attention) on a {REF_LAYERS}-layer "
+              f"Llama-3-8B-shaped checkpoint (vocab 128256, tied) over the GPU arm's configuration-3 batches; "
+              f"the layer's hook-timed seconds counted x{FULL_LAYERS // REF_LAYERS}")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * tokens / v,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(measured) / len(measured),
+            "ms_per_step_32_layers": 1000.0 * sum(scaled) / len(scaled),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "answers_per_s": statistics.median(answers),
-            "config": {"workload": "cfg3: Llama-3-8B packed prefill + label readout (1-layer slice x32, 1 request/step)",
-                       "global_batch": tokens, "seq_len": tokens, "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": f"oracle fp32, {SAMPLE_LAYERS} of 32 layers of Llama-3-8B over one "
-                                       f"request ({tokens} tokens), time x{32 // SAMPLE_LAYERS}"},
+            "answers_per_s": questions / sum(scaled),
+            "config": {"workload": WORKLOADS[3] + f" (dan's CPU path; {REF_LAYERS}-layer slice timed per step, "
+                                                  f"value counts 32 layers from the slice's layer time)",
+                       "global_batch": tokens // len(measured), "seq_len": 8192, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": ref.threads, "kind": "reference",
+                             "sample": sample},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -209,16 +293,118 @@ def prepare(runner, plans, use_cache=False):
 
 
 def step_device(model, b):
-    x = model.hidden(b["ids"], b["pos"], b["segs"])
+    x = model.residual(b["ids"], b["pos"], b["segs"])
     return model.readout(x, b["rows"], b["labels"], b["off"], b["max_labels"])
+
+
+def deal(batches, world, steps):
+    """Deal ``world * steps`` batches so every rank gets ``steps`` of them with token totals as
+    even as possible: largest first, each to the rank with the fewest tokens among those with
+    room (the engine's least-loaded dispatch). Each rank keeps its batches in draw order; with
+    one rank this is the batches as drawn."""
+    cost = [plan_tokens(p) for p in batches]
+    load, got = [0] * world, [[] for _ in range(world)]
+    for i in sorted(range(len(batches)), key=lambda i: -cost[i]):
+        r = min((r for r in range(world) if len(got[r]) < steps), key=lambda r: (load[r], r))
+        got[r].append(i)
+        load[r] += cost[i]
+    return [[batches[i] for i in sorted(g)] for g in got]
+
+
+def per_rank(values, world, rank, device):
+    """Every rank's ``values`` (a list of floats), gathered by one all-reduce: [world][len]."""
+    if world == 1:
+        return [list(values)]
+    import torch.distributed as dist
+
+    t = torch.zeros(world, len(values), dtype=torch.float64, device=device)
+    t[rank] = torch.tensor(values, dtype=torch.float64)
+    dist.all_reduce(t)
+    return t.tolist()
+
+
+def flush_l2(buf):
+    buf.add_(1)  # writes 256 MB: more than the 126 MB L2
+
+
+def attention_cfg2(device, hbm_peak, burst_peak, iters=10, seed=0):
+    """dan_tree_attention alone on one configuration-2 batch (<= 8192 tokens, Llama-3-8B heads
+    32 / 8 x 128, q / k / v ~ N(0, 1) bf16), timed per launch with CUDA events around the launch
+    and L2 flushed between launches. Useful work counts only the (query, key) pairs the tree mask
+    allows; the tile table's computed area (key blocks visited x 128 x 128) is reported beside it."""
+    from dan_b200 import synthetic
+    from dan_b200.attention import TreeLayout, tree_attention
+    from dan_b200.runner import Runner
+
+    r = Runner.__new__(Runner)
+    r.device, r.cache = device, None
+    ids, pos, segs, reads, _ = r.pack(synthetic.batch(2, seed=seed, vocab=128256), use_cache=False)
+    n, h, hkv, d = len(ids), 32, 8, 128
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(n, h, d, device=device, generator=g).bfloat16()
+    k = torch.randn(n, hkv, d, device=device, generator=g).bfloat16()
+    v = torch.randn(n, hkv, d, device=device, generator=g).bfloat16()
+    out = torch.empty_like(q)
+    lay = TreeLayout.build(segs, n, device)
+    buf = torch.empty(64 << 20, dtype=torch.float32, device=device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters + 3)]
+    for s, e in ev:
+        flush_l2(buf)
+        s.record()
+        tree_attention(q, k, v, lay, out=out)
+        e.record()
+    torch.cuda.synchronize()
+    ms = [s.elapsed_time(e) for s, e in ev[3:]]
+    med = statistics.median(ms)
+    tflops = 4 * h * d * lay.pairs / (med * 1e-3) / 1e12
+    computed = lay.blocks * 128 * 128
+    return {"bound": "tensor", "kernel": "dan_tree_attention", "workload": "cfg2a: one <=8192-token batch "
+            f"({n} tokens, {len(segs)} requests, {len(reads)} branches), 32/8 heads x 128, bf16",
+            "achieved": tflops, "peak": burst_peak, "unit": "TFLOP/s", "frac": tflops / burst_peak,
+            "peak_kind": "measured burst", "ms_median": med, "ms_min": min(ms), "launches": len(ms),
+            "useful_pairs": lay.pairs, "computed_pairs": computed, "useful_frac_of_computed": lay.pairs / computed,
+            "l2": "flushed (256 MB write) before every launch"}
+
+
+def fp8_library_peak(device, iters=5):
+    """The FP8 denominator, measured in this run: torch._scaled_mm (cuBLASLt) e4m3 8192^3 with
+    row-wise scales, bf16 out; the fastest of ``iters`` launches (burst), CUDA-event timed."""
+    n = 8192
+    a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+    sa, sb = torch.ones(n, 1, device=device), torch.ones(1, n, device=device)
+    best = None
+    for i in range(iters + 2):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+        e.record()
+        e.synchronize()
+        if i >= 2:
+            best = s.elapsed_time(e) if best is None else min(best, s.elapsed_time(e))
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def cpu_baseline_sample(plans):
+    """dan's own CPU path on one of the timed batches (the reference arm's measurement, bounded
+    to one batch): its line's ``cpu_baseline``; None with the reason when dan is unavailable."""
+    ref_runner, why = dan_reference()
+    if ref_runner is None:
+        return {"unavailable": why}
+    ref = ReferenceRun(ref_runner)
+    ref.step(plans)  # warm-up (thread pools, first-touch of the weights)
+    dt, full = ref.step(plans)
+    tokens = plan_tokens(plans)
+    return {"value": tokens / full, "unit": "tokens/s", "cores": ref.threads, "kind": "reference",
+            "sample": f"dan.runner.Runner (unmodified, fp32 CPU) on one timed batch ({tokens} tokens), "
+                      f"{REF_LAYERS}-layer Llama-3-8B-shaped checkpoint, layer time counted "
+                      f"x{FULL_LAYERS // REF_LAYERS}; measured {dt:.2f} s"}
 
 
 def run_dan(args, world, rank, local):
     from dan_b200 import profiling, synthetic
-    from dan_b200.loader import llama3_8b_config, random_model
+    from dan_b200.loader import llama3_8b_config, qwen35_4b_config, random_model
     from dan_b200.runner import Runner
-
-    from dan_b200.loader import qwen35_4b_config
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -227,25 +413,28 @@ def run_dan(args, world, rank, local):
     quant = "fp8" if cid == 5 else None
     model = random_model(cfg, seed=0, device=device, quantization=quant)
     runner = Runner(model, device, cache_bytes=(4 << 30) if cid == 5 else 0)
-    n = args.warmup + args.steps
-    batches = synthetic.batches(cid, n + 1, seed=1000 + rank, vocab=cfg["vocab_size"])
+    # One seeded request stream for all ranks: batch 0 warms the prefix pool (configuration 5),
+    # the next ``warmup`` batches are every rank's warm-up, and the following world x steps
+    # batches are dealt so each rank times ``steps`` of them with near-equal token totals.
+    drawn = synthetic.batches(cid, 1 + args.warmup + world * args.steps, seed=1000, vocab=cfg["vocab_size"])
     if cid == 5:  # the shared 1024-token prefix enters the prefix pool once, as in serving
-        runner.read_many(batches[0][:1])
-    batches = batches[1:]
-    prepared = [prepare(runner, p, use_cache=(cid == 5)) for p in batches]
+        runner.read_many(drawn[0][:1])
+    warm_plans = drawn[1:1 + args.warmup]
+    timed_plans = deal(drawn[1 + args.warmup:], world, args.steps)[rank]
+    use_cache = cid == 5
+    warm = [prepare(runner, p, use_cache=use_cache) for p in warm_plans]
+    timed = [prepare(runner, p, use_cache=use_cache) for p in timed_plans]
     torch.cuda.synchronize()
 
-    for b in prepared[:args.warmup]:
+    for b in warm:
         step_device(model, b)
     torch.cuda.synchronize()
-    timed = prepared[args.warmup:]
     tokens = sum(b["tokens"] for b in timed)
     questions = sum(b["questions"] for b in timed)
     # requests and prompt tokens as dan's usage counts them (cached prefix tokens included,
     # engine.py:74-76), over the same timed batches
-    requests = sum(len(p) for p in batches[args.warmup:])
-    prompt_tokens = sum(len(pl.prefix) + sum(len(br.suffix) for br in pl.branches)
-                        for p in batches[args.warmup:] for pl in p)
+    requests = sum(len(p) for p in timed_plans)
+    prompt_tokens = sum(plan_tokens(p) for p in timed_plans)
     pairs = sum(b["segs"].layout.pairs for b in timed)
 
     hbm, pk_burst, pk_sust, pk_kind = peaks()
@@ -271,58 +460,42 @@ def run_dan(args, world, rank, local):
     launches = profiling.total_launches() - launches0
     kern = timer.summary()
     kern["gemm"] = timer.total("gemm_")
-    ms_max = reduce(ms, "max", world, device)
-    tok_all = reduce(tokens, "sum", world, device)
-    q_all = reduce(questions, "sum", world, device)
-    req_all = reduce(requests, "sum", world, device)
-    prompt_all = reduce(prompt_tokens, "sum", world, device)
+    ranks = per_rank([tokens, ms, questions, requests, prompt_tokens], world, rank, device)
+    ms_max = max(r[1] for r in ranks)
+    tok_all, q_all, req_all, prompt_all = (sum(r[i] for r in ranks) for i in (0, 2, 3, 4))
 
-    # end to end through the public API: host plans -> read_many -> host logits
+    # end to end through the public API: host plans -> read_stream -> host logits
     h2d = d2h = 0
-    for plans in batches[args.warmup:]:
+    for plans in timed_plans:
         ids, pos, segs, reads, _ = runner.pack(plans, use_cache=False)
         nl = sum(len(l) for _, l in reads)
         h2d += 8 * len(ids) * 2 + 4 * (len(reads) + nl + len(reads) + 1)
         h2d += 4 * 12 * sum(-(-(s.end - s.start) // 128) for s in segs) + 4 * len(ids) + 4
         d2h += 2 * 4 * nl
-    for plans in batches[:1]:
-        runner.read_many(plans)
+    runner.read_many(warm_plans[0] if warm_plans else timed_plans[0])
     barrier(world, device)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall = time.perf_counter()
     e0.record()
-    for _ in runner.read_stream(batches[args.warmup:]):  # one batch queued while the next is packed
+    for _ in runner.read_stream(timed_plans):  # one batch queued while the next is packed
         pass
     e1.record()
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall
-    e2e_ms = reduce(max(e0.elapsed_time(e1), 1000 * t_wall), "max", world, device)
+    e2e_ranks = per_rank([max(e0.elapsed_time(e1), 1000 * t_wall)], world, rank, device)
+    e2e_ms = max(r[0] for r in e2e_ranks)
 
     if rank != 0:
         return
     g = kern.get("gemm", {})
-    attn_kind = f"{pk_kind} burst"  # attention stays bf16 in every configuration
-    if cid == 5:  # e4m3 GEMMs: the library's measured e4m3 burst rate is the denominator
-        try:
-            with open(os.path.join(ROOT, "profiles", "fp8_peak.md")) as f:
-                for line in f:
-                    if line.startswith("fp8_tflops_burst:"):
-                        pk_sust = float(line.split(":")[1])
-                        pk_kind = "measured fp8 (torch._scaled_mm burst, profiles/fp8_peak.md)"
-        except (OSError, ValueError):
-            pass
+    gemm_peak, gemm_kind = pk_sust, f"{pk_kind} bf16 sustained (kernels timed inside a long step)"
+    if cid == 5:  # e4m3 GEMMs: the library's e4m3 burst rate, measured now, is the denominator
+        gemm_peak = fp8_library_peak(device)
+        gemm_kind = "torch._scaled_mm e4m3 8192^3 burst, measured in this run"
     a = kern.get("dan_tree_attention", {})
     gemm_tflops = g["work_total"] / (g["ms_total"] * 1e-3) / 1e12 if g and g["ms_total"] else None
     attn_tflops = a["work_total"] / (a["ms_total"] * 1e-3) / 1e12 if a and a["ms_total"] else None
-    traffic = None  # DRAM bytes per GEMM launch from the committed ncu summary (configuration 3)
-    try:
-        with open(os.path.join(ROOT, "profiles", "gemm_bf16_cfg3_shapes.md")) as f:
-            for line in f:
-                if line.startswith("traffic_bytes_per_launch:") and cid == 3:
-                    traffic = int(line.split(":")[1])
-    except (OSError, ValueError):
-        pass
     line = {
         "metric": METRIC, "value": tok_all / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -333,16 +506,20 @@ def run_dan(args, world, rank, local):
         "config": {"workload": WORKLOADS[cid], "model": "qwen3.5-4b-style (random init)" if cid == 4 else
                    "llama-3-8b (random init)", "global_batch": int(tok_all / args.steps),
                    "seq_len": 8192, "parallelism": f"replicas x{world}",
+                   "batches": "one seeded stream; world x steps batches dealt largest-first to the least-loaded "
+                              "rank, steps per rank",
                    "l2": "weights (15 GB) streamed every step exceed the 126 MB L2"},
+        "per_rank": {"tokens": [int(r[0]) for r in ranks], "ms": [round(r[1], 3) for r in ranks],
+                     "tokens_per_s": [r[0] / (r[1] * 1e-3) for r in ranks],
+                     "e2e_ms": [round(r[0], 3) for r in e2e_ranks]},
         "roofline": {"bound": "tensor", "kernel": f"dan_gemm_{'e4m3' if cid == 5 else 'bf16'} (all decoder projections)",
-                     "achieved": gemm_tflops,
-                     "peak": pk_sust, "unit": "TFLOP/s", "frac": gemm_tflops / pk_sust if gemm_tflops else None,
-                     "peak_kind": pk_kind if cid == 5 else f"{pk_kind} sustained (kernel timed inside a long step)",
-                     "traffic": traffic, "share_of_step": g.get("ms_total", 0) / ms if g else None},
+                     "achieved": gemm_tflops, "peak": gemm_peak, "unit": "TFLOP/s",
+                     "frac": gemm_tflops / gemm_peak if gemm_tflops else None, "peak_kind": gemm_kind,
+                     "traffic": None, "share_of_step": g.get("ms_total", 0) / ms if g else None},
         "roofline_attention": {"bound": "tensor", "kernel": "dan_tree_attention", "achieved": attn_tflops,
                                "peak": pk_burst, "unit": "TFLOP/s",
                                "frac": attn_tflops / pk_burst if attn_tflops else None,
-                               "peak_kind": attn_kind, "useful_pairs_per_step": pairs / args.steps,
+                               "peak_kind": f"{pk_kind} burst", "useful_pairs_per_step": pairs / args.steps,
                                "share_of_step": a.get("ms_total", 0) / ms if a else None},
         "e2e": {"value": tok_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
@@ -363,12 +540,10 @@ def run_dan(args, world, rank, local):
                                  "unit": "GB/s", "frac": gbs / hbm if hbm else None, "peak_kind": "measured",
                                  "tflops": flops / (sc["ms_total"] * 1e-3) / 1e12,
                                  "share_of_step": sc["ms_total"] / ms}
+    if not args.no_attention_case:
+        line["attention_cfg2"] = attention_cfg2(device, hbm, pk_burst)
     if world == 1 and not args.no_cpu and cid == 3:
-        dt, ctok, cq, threads = cpu_sample()
-        v = ctok / (dt * 32 / SAMPLE_LAYERS)
-        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": f"oracle fp32, {SAMPLE_LAYERS} of 32 layers of Llama-3-8B over one "
-                                          f"request ({ctok} tokens), time x{32 // SAMPLE_LAYERS}"}
+        line["cpu_baseline"] = cpu_baseline_sample(timed_plans[0])
     print(json.dumps(line), flush=True)
     if args.breakdown:  # every entry point over the same batches again, to stderr
         full = profiling.KernelTimer().reserve(2 * 16 * cfg["num_hidden_layers"] * len(timed))
@@ -393,6 +568,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="dan", choices=["dan", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-attention-case", action="store_true", help="skip the configuration-2 attention timing")
     ap.add_argument("--breakdown", action="store_true",
                     help="after the JSON line, time every kernel entry point over the timed batches (stderr)")
     ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5],

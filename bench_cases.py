@@ -1,6 +1,6 @@
 """Small standalone kernel cases for profiling (``ncu``) and quick timing.
 
-    python -m dan_b200.cases gemm|attention|deltanet|norm [--iters N]
+    python bench_cases.py gemm|attention|deltanet|norm [--iters N]
 
 Each case builds seeded inputs with the shapes of a benchmark configuration,
 runs the kernel ``--iters`` times (4 by default) and prints one JSON line with
@@ -20,9 +20,9 @@ import json
 
 import torch
 
-from . import _lib, ops, synthetic
-from .attention import TreeLayout, tree_attention
-from .plan import Branch, ReadPlan  # noqa: F401  (re-exported for callers building cases)
+from dan_b200 import _lib, ops, synthetic
+from dan_b200.attention import TreeLayout, tree_attention
+from dan_b200.plan import Branch, ReadPlan  # noqa: F401  (re-exported for callers building cases)
 
 
 def _time(fn, iters):
@@ -38,7 +38,7 @@ def _time(fn, iters):
 
 
 def _pack(cfg, seed):
-    from .runner import Runner
+    from dan_b200.runner import Runner
 
     r = Runner.__new__(Runner)
     r.device, r.cache = torch.device("cuda"), None
@@ -82,7 +82,7 @@ def attention(iters):
 
 
 def deltanet(iters):
-    from .qwen3_5 import RecurrentLayout
+    from dan_b200.qwen3_5 import RecurrentLayout
 
     dev = torch.device("cuda")
     ids, pos, segs, reads, _ = _pack(4, 0)
@@ -183,7 +183,7 @@ def _graph_time(fn, n=20, reps=5):
 def conv(iters):
     """Causal conv + SiLU of configuration-4 batches (8192 channels: q, k, v of 16 / 16 / 32
     heads x 128), graph-timed, three seeded batches."""
-    from .qwen3_5 import RecurrentLayout
+    from dan_b200.qwen3_5 import RecurrentLayout
 
     dev = torch.device("cuda")
     out = {}

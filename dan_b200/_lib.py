@@ -21,6 +21,7 @@ SIGNATURES = {
     "dan_version": ([], ctypes.c_char_p),
     "dan_last_error": ([], ctypes.c_char_p),
     "dan_read_status": ([P, P, P], I32),
+    "dan_selftest_wait": ([I32, P, P, P], I32),
     "dan_gemm_bf16": ([P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
     "dan_gemm_bf16_noalloc": ([P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
     "dan_gemm_e4m3": ([P, I64, P, P, I64, P, P, I64, P, I64, P, I32, I32, I32, I32, P, P], I32),
@@ -43,6 +44,12 @@ SIGNATURES = {
                               F32, P, I64, P, P], I32),
     "dan_gated_delta_scratch_bytes": ([I32, I32, I32], I64),
     "dan_gated_rms_norm": ([P, I64, P, I64, P, F32, P, I64, I32, I32, I32, P], I32),
+    "dan_delta_rule_scan": ([P, P, P, I64, P, I64, P, I64, P, I32, P, P, I32, P, I64, P, I64, I32, I32, I32, I32, F32,
+                             P, I64, P, P], I32),
+    "dan_swiglu": ([P, I64, P, I64, P, I64, I32, I32, P], I32),
+    "dan_delta_gates": ([P, I64, P, I64, P, P, P, I64, P, I64, I32, I32, P], I32),
+    "dan_lse_merge": ([P, P, P, P, P, I64, I32, I32, I32, P], I32),
+    "dan_quantize_e4m3_tensor": ([P, I64, P, I64, P, I32, I32, P], I32),
 }
 
 _lib = None

@@ -15,7 +15,8 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, ops
+from .cache import PoolEntry
 
 BLOCK = 128  # query rows per tile, keys per block, tokens per pool page
 TILE_FIELDS = ("row0", "nrows", "seg_start", "past", "ppad", "split", "nblk_a", "blk_b0", "blk_b1", "page0", "q0v",
@@ -57,10 +58,12 @@ class Segment:
 
 class Batch(list):
     """The segments of one packed forward; caches the tile layout every attention
-    layer shares (``layout``) and the recurrent-layer layout (``recurrent``)."""
+    layer shares (``layout``), the recurrent-layer layout (``recurrent``) and the paging of
+    pasts given as tensors (``staged``)."""
 
     layout = None
     recurrent = None
+    staged = None
 
 
 def segment(start, branch, past=None, save=0, past_len=0, device="cpu"):
@@ -228,16 +231,65 @@ def tree_attention(q, k, v, layout, out=None, pool=None, layer=0, scale=None):
     return out
 
 
+class _StagedPasts:
+    """Cached prefixes given as dan's per-layer tensors, staged into 128-token pages for the
+    kernel: ``segments`` re-stated with page entries (the tile layout is built once per batch
+    from them) and one layer's staging pool at a time."""
+
+    def __init__(self, segments):
+        self.segments, page = Batch(), 0
+        for s in segments:
+            entry = None
+            if s.past_len:
+                npg = -(-s.past_len // BLOCK)
+                entry = PoolEntry(list(range(page, page + npg)), s.past_len, 0)
+                page += npg
+            self.segments.append(Segment(s.start, s.end, s.trunk, s.branches, entry, 0, {}, s.past_len,
+                                         s.branch_ids, s.device))
+        self.n_pages = page
+        self.layer, self.k, self.v = None, {}, {}
+
+    def stage(self, originals, layer, like):
+        """Copy every past's keys / values of ``layer`` ([Hkv, P, D] each) into the pages."""
+        if self.layer == layer:
+            return self
+        hkv, d = like.shape[0], like.shape[2]
+        pk = torch.empty(self.n_pages * BLOCK, hkv, d, dtype=like.dtype, device=like.device)
+        pv = torch.empty_like(pk)
+        for s, t in zip(originals, self.segments):
+            if not s.past_len:
+                continue
+            k, v = s.past[layer]
+            rows = torch.arange(s.past_len, dtype=torch.int32, device=like.device)
+            dst = torch.as_tensor(t.past.pages, dtype=torch.int32, device=like.device).repeat_interleave(BLOCK)
+            dst = (dst * BLOCK + torch.arange(BLOCK, dtype=torch.int32, device=like.device).repeat(len(t.past.pages)))
+            kt, vt = k.transpose(0, 1), v.transpose(0, 1)  # [P, Hkv, D] views
+            ops.kv_store(kt, vt, pk, pv, rows, dst[:s.past_len].contiguous())
+        self.layer, self.k, self.v = layer, {layer: pk}, {layer: pv}
+        return self
+
+
 def attend(q, k, v, segments, layer, scale=None, pool=None):
     """q: [H, N, D]; k, v: [Hkv, N, D] (rotary applied) -> [H, N, D] (attention.py:200-207).
 
-    Views of the packed [N, heads, D] projections are used in place (no copies).
-    Segments with ``save`` record their first ``save`` new tokens' k/v into
-    ``s.saved[layer]`` (as views; the pool stores them in pages)."""
+    Views of the packed [N, heads, D] projections are used in place (no copies). Segments
+    with ``save`` record copies of their first ``save`` new tokens' k/v in
+    ``s.saved[layer]`` as dan does. A segment's ``past`` is either a prefix-pool entry (read
+    in place from ``pool``) or dan's per-layer ``{layer: (k, v)}`` tensors [Hkv, past, D],
+    which are staged into pages once per layer."""
     for s in segments:
         if s.save:
-            s.saved[layer] = (k[:, s.start:s.start + s.save], v[:, s.start:s.start + s.save])
-    lay = layout_of(segments, q.shape[1], q.device)
+            s.saved[layer] = (k[:, s.start:s.start + s.save].clone(), v[:, s.start:s.start + s.save].clone())
+    segs = segments
+    if pool is None and any(s.past_len and not isinstance(s.past, PoolEntry) for s in segments):
+        staged = getattr(segments, "staged", None)
+        if staged is None:
+            staged = _StagedPasts(segments)
+            if isinstance(segments, Batch):
+                segments.staged = staged
+        pool = staged.stage(segments, layer, k)
+        segs = staged.segments
+    lay = layout_of(segs, q.shape[1], q.device)
     out = tree_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), lay, pool=pool, layer=layer,
                          scale=scale)
     return out.transpose(0, 1)

@@ -125,3 +125,40 @@ class PrefixPool:
         for e in list(self.entries.values()):
             self._free(e)
         self.entries.clear()
+
+
+class PrefixCache:
+    """dan's prefix cache contract (dan/cache.py:11-39) for callers that keep per-layer
+    ``{layer: (k, v)}`` tensors (``attend`` reads such pasts by staging them into pages):
+    exact-key entries, ``get`` counting ``hits`` / ``misses``, ``used`` bytes under
+    ``max_bytes`` with least-recently-used eviction, entries larger than the budget not kept.
+    ``Runner`` uses the paged ``PrefixPool`` above instead, which the kernels read in place."""
+
+    def __init__(self, max_bytes=2 << 30):
+        self.max_bytes = max_bytes
+        self.used = 0
+        self.hits = self.misses = 0
+        self._lru = OrderedDict()  # key -> (kv, nbytes), least recent first
+
+    def get(self, ids):
+        found = self._lru.get(tuple(ids))
+        if found is None:
+            self.misses += 1
+            return None
+        self.hits += 1
+        self._lru.move_to_end(tuple(ids))
+        return found[0]
+
+    def put(self, ids, kv):
+        key = tuple(ids)
+        nbytes = sum(t.numel() * t.element_size() for pair in kv.values() for t in pair)
+        if key in self._lru or nbytes > self.max_bytes:
+            return
+        while self._lru and self.used + nbytes > self.max_bytes:
+            self.used -= self._lru.popitem(last=False)[1][1]
+        self._lru[key] = (kv, nbytes)
+        self.used += nbytes
+
+    @property
+    def entries(self):
+        return self._lru

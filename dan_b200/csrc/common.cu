@@ -75,7 +75,31 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// Self-test of the bounded waits every pipelined kernel uses: one thread waits on something
+// that nothing completes (kind 0: an mbarrier phase no thread arrives on; kind 1: a global
+// flag no CTA sets), gives up after kWaitCycles (about a second), reports the timeout in the
+// status word exactly as the production kernels do, and returns: the context stays usable.
+__global__ void selftest_wait_kernel(int kind, const uint32_t* flag, int32_t* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  if (kind == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    if (!mbar_wait(&bar, 0)) report(status, kTimeoutFull);
+  } else {
+    if (!wait_flag(flag, 1u)) report(status, kTimeoutPartial);
+  }
+}
+
 }  // namespace dan
+
+DAN_API int dan_selftest_wait(int kind, const void* flag, int32_t* status, void* stream) {
+  DAN_REQUIRE(kind == 0 || (kind == 1 && flag != nullptr), "selftest_wait: kind 0, or kind 1 with a flag word");
+  dan::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      kind, static_cast<const uint32_t*>(flag), status);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
 
 DAN_API const char* dan_version(void) { return "dan_b200 0.1.0 (sm_100a)"; }
 

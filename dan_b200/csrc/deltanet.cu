@@ -147,8 +147,10 @@ struct ScanParams {
   const __nv_bfloat16* b;  // in_proj b / a columns, [rows, hv] with row stride ld_ba
   const __nv_bfloat16* a;
   int64_t ld_ba;
-  const float* a_log;    // [hv]
+  const float* a_log;    // [hv]; nullptr: the gates are given (b holds beta, g_given the log decay)
   const float* dt_bias;  // [hv]
+  const float* g_given;  // [rows, hv] fp32 log decay, row stride ld_g (when a_log is nullptr)
+  int64_t ld_g;
   const Seg* segs;
   const int* branches;
   float* state_pool;  // [slots, hv, dk, dv] of this layer (slot stride given)
@@ -260,7 +262,8 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
   const int per = p.hv / p.hk, kh = h / per;
   const bool owner = h % per == 0;  // writes this key head's q̂ and k̂
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const float a_neg = -__expf(p.a_log[h]), dtb = p.dt_bias[h];
+  const bool given = p.a_log == nullptr;
+  const float a_neg = given ? 0.f : -__expf(p.a_log[h]), dtb = given ? 0.f : p.dt_bias[h];
   uint8_t* rv = p.scratch + (static_cast<int64_t>(ci) * p.hv + h) * REC_V;
   uint8_t* rk = p.scratch + static_cast<int64_t>(p.n_chunks) * p.hv * REC_V + (static_cast<int64_t>(ci) * p.hk + kh) * REC_K;
   // ---- stage: raw q, k, v rows by cp.async (16 B per thread step, all in flight), gates; T cleared
@@ -286,8 +289,13 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
     float bb = 0.f, gg = 0.f;
     if (t < nt) {
       const int64_t row = row0 + t;
-      bb = 1.f / (1.f + __expf(-__bfloat162float(p.b[row * p.ld_ba + h])));
-      gg = a_neg * softplus(__bfloat162float(p.a[row * p.ld_ba + h]) + dtb);
+      if (given) {
+        bb = __bfloat162float(p.b[row * p.ld_ba + h]);
+        gg = p.g_given[row * p.ld_g + h];
+      } else {
+        bb = 1.f / (1.f + __expf(-__bfloat162float(p.b[row * p.ld_ba + h])));
+        gg = a_neg * softplus(__bfloat162float(p.a[row * p.ld_ba + h]) + dtb);
+      }
     }
     sm.beta[t] = bb;
     sm.graw[t] = gg;
@@ -850,35 +858,43 @@ DAN_API int64_t dan_gated_delta_scratch_bytes(int n_chunks, int hk, int hv) {
   return static_cast<int64_t>(n_chunks) * (hv * delta::REC_V + hk * delta::REC_K);
 }
 
-DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* b,
-                                 const void* a, int64_t ld_ba, const float* a_log, const float* dt_bias,
-                                 const int* segs, int n_segs, const int* branches, const int* chunks, int n_chunks,
-                                 float* state_pool, int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv,
-                                 int dk, int dv, float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status,
-                                 void* stream) {
+// Checks and launches of the two scan kernels (prep over all chunks, then the chains).
+static int scan_launch(const delta::ScanParams& p, int n_segs, int dk, int dv, int64_t scratch_bytes,
+                       void* stream) {
   DAN_REQUIRE(dk == delta::DK && dv == delta::DK, "gated_delta_scan: needs dk = dv = 128 (got %d, %d)", dk, dv);
-  DAN_REQUIRE(ld_qkv % 8 == 0 && ld_out % 8 == 0, "gated_delta_scan: strides must be multiples of 8");
-  DAN_REQUIRE(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(k) % 16 == 0 &&
-                  reinterpret_cast<uintptr_t>(v) % 16 == 0,
+  DAN_REQUIRE(p.ld_qkv % 8 == 0 && p.ld_out % 8 == 0, "gated_delta_scan: strides must be multiples of 8");
+  DAN_REQUIRE(reinterpret_cast<uintptr_t>(p.q) % 16 == 0 && reinterpret_cast<uintptr_t>(p.k) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(p.v) % 16 == 0,
               "gated_delta_scan: q, k, v must be 16-byte aligned (their rows are bulk-copied)");
-  DAN_REQUIRE(hk > 0 && hv % hk == 0, "gated_delta_scan: %d value heads not a multiple of %d key heads", hv, hk);
-  DAN_REQUIRE(n_segs < 65536 && n_chunks < (1 << 30), "gated_delta_scan: too many segments or chunks");
-  DAN_REQUIRE(scratch_bytes >= dan_gated_delta_scratch_bytes(n_chunks, hk, hv) &&
-                  reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
+  DAN_REQUIRE(p.hk > 0 && p.hv % p.hk == 0, "gated_delta_scan: %d value heads not a multiple of %d key heads", p.hv,
+              p.hk);
+  DAN_REQUIRE(n_segs < 65536 && p.n_chunks < (1 << 30), "gated_delta_scan: too many segments or chunks");
+  DAN_REQUIRE(scratch_bytes >= dan_gated_delta_scratch_bytes(p.n_chunks, p.hk, p.hv) &&
+                  reinterpret_cast<uintptr_t>(p.scratch) % 16 == 0,
               "gated_delta_scan: scratch needs %lld bytes, 16-byte aligned (got %lld)",
-              static_cast<long long>(dan_gated_delta_scratch_bytes(n_chunks, hk, hv)),
+              static_cast<long long>(dan_gated_delta_scratch_bytes(p.n_chunks, p.hk, p.hv)),
               static_cast<long long>(scratch_bytes));
-  if (!n_segs || !n_chunks) return 0;
+  if (!n_segs || !p.n_chunks) return 0;
+  static std::atomic<uint64_t> prep_conf{0}, state_conf{0};
+  DAN_CUDA(smem_limit_once(delta::chunk_prep_kernel, static_cast<int>(sizeof(delta::PrepSmem)), prep_conf));
+  DAN_CUDA(smem_limit_once(delta::chunk_state_kernel, static_cast<int>(sizeof(delta::StateSmem)), state_conf));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  delta::chunk_prep_kernel<<<dim3(p.n_chunks, p.hv), 256, sizeof(delta::PrepSmem), st>>>(p);
+  DAN_CUDA(cudaGetLastError());
+  delta::chunk_state_kernel<<<dim3(2 * p.hv, n_segs), 256, sizeof(delta::StateSmem), st>>>(p);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+static delta::ScanParams scan_params(const void* q, const void* k, const void* v, int64_t ld_qkv, const int* segs,
+                                     const int* branches, const int* chunks, int n_chunks, float* state_pool,
+                                     int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv, float q_scale,
+                                     void* scratch, int32_t* status) {
   delta::ScanParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k);
   p.v = static_cast<const __nv_bfloat16*>(v);
   p.ld_qkv = ld_qkv;
-  p.b = static_cast<const __nv_bfloat16*>(b);
-  p.a = static_cast<const __nv_bfloat16*>(a);
-  p.ld_ba = ld_ba;
-  p.a_log = a_log;
-  p.dt_bias = dt_bias;
   p.segs = reinterpret_cast<const delta::Seg*>(segs);
   p.branches = branches;
   p.state_pool = state_pool;
@@ -892,15 +908,39 @@ DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, in
   p.n_chunks = n_chunks;
   p.scratch = static_cast<uint8_t*>(scratch);
   p.status = status;
-  static std::atomic<uint64_t> prep_conf{0}, state_conf{0};
-  DAN_CUDA(smem_limit_once(delta::chunk_prep_kernel, static_cast<int>(sizeof(delta::PrepSmem)), prep_conf));
-  DAN_CUDA(smem_limit_once(delta::chunk_state_kernel, static_cast<int>(sizeof(delta::StateSmem)), state_conf));
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  delta::chunk_prep_kernel<<<dim3(n_chunks, hv), 256, sizeof(delta::PrepSmem), st>>>(p);
-  DAN_CUDA(cudaGetLastError());
-  delta::chunk_state_kernel<<<dim3(2 * hv, n_segs), 256, sizeof(delta::StateSmem), st>>>(p);
-  DAN_CUDA(cudaGetLastError());
-  return 0;
+  return p;
+}
+
+DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* b,
+                                 const void* a, int64_t ld_ba, const float* a_log, const float* dt_bias,
+                                 const int* segs, int n_segs, const int* branches, const int* chunks, int n_chunks,
+                                 float* state_pool, int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv,
+                                 int dk, int dv, float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status,
+                                 void* stream) {
+  DAN_REQUIRE(a_log != nullptr && dt_bias != nullptr, "gated_delta_scan: A_log and dt_bias are required");
+  delta::ScanParams p = scan_params(q, k, v, ld_qkv, segs, branches, chunks, n_chunks, state_pool, slot_stride, out,
+                                    ld_out, hk, hv, q_scale, scratch, status);
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.ld_ba = ld_ba;
+  p.a_log = a_log;
+  p.dt_bias = dt_bias;
+  return scan_launch(p, n_segs, dk, dv, scratch_bytes, stream);
+}
+
+DAN_API int dan_delta_rule_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* beta,
+                                int64_t ld_beta, const float* g, int64_t ld_g, const int* segs, int n_segs,
+                                const int* branches, const int* chunks, int n_chunks, float* state_pool,
+                                int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv, int dk, int dv,
+                                float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream) {
+  DAN_REQUIRE(beta != nullptr && g != nullptr, "delta_rule_scan: beta and g are required");
+  delta::ScanParams p = scan_params(q, k, v, ld_qkv, segs, branches, chunks, n_chunks, state_pool, slot_stride, out,
+                                    ld_out, hk, hv, q_scale, scratch, status);
+  p.b = static_cast<const __nv_bfloat16*>(beta);
+  p.ld_ba = ld_beta;
+  p.g_given = g;
+  p.ld_g = ld_g;
+  return scan_launch(p, n_segs, dk, dv, scratch_bytes, stream);
 }
 
 DAN_API int dan_gated_rms_norm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* w, float eps,

@@ -374,9 +374,9 @@ __global__ void kv_store_kernel(const __nv_bfloat16* k, const __nv_bfloat16* v, 
 // (llama.py:163-165), then the question's softmax (readout.py:13-17).
 __global__ void readout_kernel(const __nv_bfloat16* h, int64_t ldh, const int* read_rows, const __nv_bfloat16* nw,
                                float eps, int mode, const __nv_bfloat16* wlm, int64_t ldw, int64_t vocab,
-                               const int* label_ids, const int* offsets, int hidden, float* logits, float* probs,
-                               int32_t* status) {
-  extern __shared__ float sh[];  // [hidden] normed row, then [labels] logits
+                               const int* label_ids, const int* offsets, int hidden, int max_labels, float* logits,
+                               float* probs, int32_t* status) {
+  extern __shared__ float sh[];  // [hidden] normed row, then [max_labels] logits
   __shared__ float red[32];
   const int q = blockIdx.x;
   const int nwarps = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -397,13 +397,20 @@ __global__ void readout_kernel(const __nv_bfloat16* h, int64_t ldh, const int* r
   }
   __syncthreads();
   const float inv = red[0];
-  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
-    const float f = sh[c] * inv;
-    const float w = __bfloat162float(nw[c]);
-    sh[c] = bf16_round(mode == 0 ? w * bf16_round(f) : f * (1.f + w));
+  if (mode != 2) {  // mode 2: the row is already final-normed (label_logits on a hidden state)
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+      const float f = sh[c] * inv;
+      const float w = __bfloat162float(nw[c]);
+      sh[c] = bf16_round(mode == 0 ? w * bf16_round(f) : f * (1.f + w));
+    }
   }
   __syncthreads();
-  const int a = offsets[q], b = offsets[q + 1];
+  const int a = offsets[q];
+  int b = offsets[q + 1];
+  if (b < a || b - a > max_labels) {  // the logits slots hold max_labels values: clamp, report
+    if (threadIdx.x == 0) report(status, kBadIndex);
+    b = b < a ? a : a + max_labels;
+  }
   float* lg = sh + hidden;
   for (int j = a + warp; j < b; j += nwarps) {
     int64_t id = label_ids[j];
@@ -628,6 +635,7 @@ DAN_API int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, 
                               float* probs, int32_t* status, void* stream) {
   DAN_REQUIRE(hidden > 0 && hidden % 8 == 0 && ldw % 8 == 0, "label_readout: hidden/ldw must be multiples of 8");
   DAN_REQUIRE(max_labels >= 0 && max_labels <= 4096, "label_readout: at most 4096 labels per question");
+  DAN_REQUIRE(mode >= 0 && mode <= 2, "label_readout: unknown norm mode %d", mode);
   if (!n_questions) return 0;
   const size_t smem = (static_cast<size_t>(hidden) + max_labels) * sizeof(float);
   DAN_REQUIRE(smem <= 200 * 1024, "label_readout: hidden %d too large", hidden);
@@ -636,7 +644,8 @@ DAN_API int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, 
   // 16 warps per question: up to 255 labels (configuration 5) are 16 rows per warp, not 32.
   ew::readout_kernel<<<n_questions, 512, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(h), ldh, read_rows, static_cast<const __nv_bfloat16*>(norm_w), eps, mode,
-      static_cast<const __nv_bfloat16*>(w_lm), ldw, vocab, label_ids, offsets, hidden, logits, probs, status);
+      static_cast<const __nv_bfloat16*>(w_lm), ldw, vocab, label_ids, offsets, hidden, max_labels, logits, probs,
+      status);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }

@@ -35,7 +35,7 @@ from collections import OrderedDict, deque
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 
-from .readout import answers, combine
+from ._dan import answers, combine
 
 
 class Overloaded(RuntimeError):

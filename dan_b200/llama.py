@@ -55,6 +55,16 @@ def quantize_weight(w):
     return ops.quantize_e4m3(w.contiguous())
 
 
+def _label_logits(model, h, label_ids):
+    ids = torch.as_tensor(label_ids, dtype=torch.int32).reshape(-1).to(model.device)
+    hr = h.reshape(1, -1).to(torch.bfloat16).contiguous()
+    zero = torch.zeros(1, dtype=torch.int32, device=model.device)
+    off = torch.tensor([0, ids.numel()], dtype=torch.int32, device=model.device)
+    logits, _ = ops.label_readout(hr, zero, model.norm, model.eps, ops.NORM_NONE, model.lm_head, ids, off,
+                                  max(ids.numel(), 1))
+    return logits
+
+
 class Linear:
     """A decoder projection: bf16 weight, or e4m3 weight + per-row scale."""
 
@@ -150,9 +160,14 @@ class LlamaForReads:
             return None, (q8, sc)
         return ops.rms_norm(x, w, self.eps), None
 
-    def hidden(self, ids, positions, segments, saves=None):
-        """Residual-stream states [N, hidden] after the last layer, before the final
-        norm (the readout applies it to the read rows only; llama.py:152-161).
+    def hidden(self, ids, positions, segments):
+        """Final-normed hidden states [N, hidden] bf16 of a packed token sequence
+        (llama.py:152-161). The runner reads only the read rows, so it uses ``residual`` and
+        lets the readout kernel norm those rows."""
+        return ops.rms_norm(self.residual(ids, positions, segments), self.norm, self.eps)
+
+    def residual(self, ids, positions, segments, saves=None):
+        """Residual-stream states [N, hidden] after the last layer, before the final norm.
 
         ``saves``: optional (src_rows, dst_rows) int32 device tensors: after each
         layer's RoPE, those rows' k/v are stored into the prefix pool."""
@@ -186,12 +201,13 @@ class LlamaForReads:
 
     def readout(self, x, read_rows, label_ids, offsets, max_labels):
         """Final norm of the read rows, label logits in fp32 and per-question softmax."""
-        return ops.label_readout(x, read_rows, self.norm, self.eps, False, self.lm_head, label_ids, offsets,
+        return ops.label_readout(x, read_rows, self.norm, self.eps, ops.NORM_LLAMA, self.lm_head, label_ids, offsets,
                                  max_labels)
 
     def label_logits(self, h, label_ids):
-        """Logits of just ``label_ids`` for one final-normed hidden state (llama.py:163-165)."""
-        return self.lm_head[torch.as_tensor(label_ids, device=self.device)].float() @ h.float()
+        """fp32 logits of just ``label_ids`` for one final-normed hidden state h [hidden]
+        (llama.py:163-165), by the readout kernel with its norm off."""
+        return _label_logits(self, h, label_ids)
 
     def kv_layout(self):
         """(layers, kv heads, head dim) the prefix pool must hold for this model."""

@@ -9,7 +9,8 @@ plans works. All reads of all requests run in one packed forward per batch.
 """
 import torch
 
-from .readout import answers, combine
+from . import _dan
+from ._dan import answers, combine
 from .runner import Runner
 
 
@@ -17,10 +18,9 @@ class LLM:
     def __init__(self, model, planner=None, device="cuda", dtype=torch.bfloat16, quantization=None,
                  cache_bytes=2 << 30):
         if planner is None:  # dan installed alongside: build its planner from the model's tokenizer
-            from dan.prompt import Planner  # noqa: PLC0415
             from transformers import AutoTokenizer
 
-            planner = Planner(AutoTokenizer.from_pretrained(model))
+            planner = _dan.planner(AutoTokenizer.from_pretrained(model))
         self.planner = planner
         self.runner = Runner(model, device, dtype, cache_bytes=cache_bytes, quantization=quantization)
 

@@ -177,15 +177,19 @@ def kv_store(k, v, pool_k, pool_v, src_rows, dst_rows):
               k.shape[1], k.shape[2], _lib.stream())
 
 
-def label_readout(h, read_rows, norm_w, eps, zero_centered, w_lm, label_ids, offsets, max_labels):
-    """Per question: final norm of its read row, ``W_lm[labels] @ h`` in fp32 and the softmax
-    (llama.py:161-165, runner.py:73-74, readout.py:13-17). Returns (logits, probs), flat fp32."""
+NORM_LLAMA, NORM_ZERO_CENTERED, NORM_NONE = 0, 1, 2
+
+
+def label_readout(h, read_rows, norm_w, eps, norm_mode, w_lm, label_ids, offsets, max_labels):
+    """Per question: final norm of its read row (``norm_mode``: Llama, zero-centred, or none for
+    rows already normed), ``W_lm[labels] @ h`` in fp32 and the softmax (llama.py:161-165,
+    runner.py:73-74, readout.py:13-17). Returns (logits, probs), flat fp32."""
     nq = read_rows.numel()
     total = label_ids.numel()
     logits = torch.empty(total, dtype=torch.float32, device=h.device)
     probs = torch.empty(total, dtype=torch.float32, device=h.device)
     _lib.call("dan_label_readout", _lib.ptr(h), h.stride(0), _lib.ptr(read_rows), _lib.ptr(norm_w), float(eps),
-              1 if zero_centered else 0, _lib.ptr(w_lm), w_lm.stride(0), w_lm.shape[0], _lib.ptr(label_ids),
+              int(norm_mode), _lib.ptr(w_lm), w_lm.stride(0), w_lm.shape[0], _lib.ptr(label_ids),
               _lib.ptr(offsets), nq, h.shape[1], max_labels, _lib.ptr(logits), _lib.ptr(probs), _st(h),
               _lib.stream())
     return logits, probs

@@ -26,7 +26,7 @@ import torch
 
 from . import _lib, ops
 from .attention import layout_of, tree_attention
-from .llama import Linear
+from .llama import Linear, _label_logits
 
 PRE = "model.language_model."
 
@@ -43,6 +43,47 @@ def remap(name):
 
 
 CHUNK = 64  # tokens per chunk of the scan
+
+
+def delta_rule(q, k, v, g, beta, lengths, states, cu=None):
+    """Gated delta rule over packed sequences of ``lengths`` (qwen3_5.py:136-158): q, k [N, H,
+    128], v [N, H, 128] bf16 (q and k are l2-normalised and q scaled by 128^-0.5 inside, as
+    dan's kernels do), g [N, H] fp32 log decay, beta [N, H] bf16, ``states`` [S, H, 128, 128]
+    fp32 initial states, one per sequence. Returns (out [N, H, 128] bf16, final states fp32).
+    ``cu`` (dan's precomputed cumulative lengths) is accepted and not needed: each sequence is
+    one run of 64-token chunks of the chunked scan, its final state stored in place of a copy
+    of its initial one."""
+    n, h, dk = q.shape
+    dv = v.shape[-1]
+    lengths = [int(x) for x in lengths]
+    if sum(lengths) != n or len(lengths) != states.shape[0]:
+        raise ValueError(f"delta_rule: lengths {sum(lengths)} / {len(lengths)} do not match {n} rows / "
+                         f"{states.shape[0]} states")
+    for t in (q, k, v, beta):
+        if not (t.is_cuda and t.dtype == torch.bfloat16):
+            raise ValueError("delta_rule: q, k, v and beta must be bf16 CUDA tensors")
+    dev = q.device
+    final = states.to(torch.float32).contiguous().clone()
+    segs, chunks, start = [], [], 0
+    for i, length in enumerate(lengths):
+        segs.append((start, length, length, i, i, 0, 0, len(chunks)))
+        chunks += [(start + t0, min(CHUNK, length - t0)) for t0 in range(0, length, CHUNK)]
+        start += length
+    segs.sort(key=lambda r: -r[1])
+    up = lambda a, cols: torch.as_tensor(np.asarray(a, dtype=np.int32).reshape(-1, cols)).to(dev)  # noqa: E731
+    segs_t, chunks_t, br_t = up(segs, 8), up(chunks or [(0, 0)], 2), up([(0, 0, 0, 0)], 4)
+    qkv = torch.cat([q.reshape(n, -1), k.reshape(n, -1), v.reshape(n, -1)], 1)  # one row stride for all three
+    beta2 = beta.reshape(n, h).contiguous()
+    g2 = g.reshape(n, h).to(torch.float32).contiguous()
+    out = torch.empty(n, h, dv, dtype=torch.bfloat16, device=dev)
+    scratch = _lib.delta_scratch(len(chunks), h, h, dev)
+    kd = h * dk
+    _lib.call("dan_delta_rule_scan", _lib.ptr(qkv), _lib.ptr(qkv[:, kd:]), _lib.ptr(qkv[:, 2 * kd:]), qkv.stride(0),
+              _lib.ptr(beta2), beta2.stride(0), _lib.ptr(g2), g2.stride(0), _lib.ptr(segs_t), len(segs),
+              _lib.ptr(br_t), _lib.ptr(chunks_t), len(chunks), _lib.ptr(final), final.stride(0), _lib.ptr(out),
+              h * dv, h, h, dk, dv, float(dk ** -0.5), _lib.ptr(scratch), scratch.numel(),
+              _lib.ptr(_lib.status_word(dev)), _lib.stream())
+    return out, final
 
 
 @dataclass
@@ -196,7 +237,12 @@ class Qwen35ForReads:
         return lay
 
     # ------------------------------------------------------------------ forward
-    def hidden(self, ids, positions, segments, saves=None):
+    def hidden(self, ids, positions, segments):
+        """Final-normed (zero-centred) hidden states [N, hidden] bf16 (qwen3_5.py:410-417); the
+        runner uses ``residual`` and norms only the read rows in the readout kernel."""
+        return ops.rms_norm(self.residual(ids, positions, segments), self.norm, self.eps, zero_centered=True)
+
+    def residual(self, ids, positions, segments, saves=None):
         """Residual-stream states [N, hidden] after the last layer (before the final norm)."""
         n = ids.shape[0]
         x = ops.embed(ids, self.embed_tokens)
@@ -269,11 +315,12 @@ class Qwen35ForReads:
         ops.linear(ao, L["o"].w, residual=x)
 
     def readout(self, x, read_rows, label_ids, offsets, max_labels):
-        return ops.label_readout(x, read_rows, self.norm, self.eps, True, self.lm_head, label_ids, offsets,
-                                 max_labels)
+        return ops.label_readout(x, read_rows, self.norm, self.eps, ops.NORM_ZERO_CENTERED, self.lm_head, label_ids,
+                                 offsets, max_labels)
 
     def label_logits(self, h, label_ids):
-        return self.lm_head[torch.as_tensor(label_ids, device=self.device)].float() @ h.float()
+        """fp32 logits of ``label_ids`` for one final-normed hidden state (qwen3_5.py:419-420)."""
+        return _label_logits(self, h, label_ids)
 
     def linear_params(self):
         c, hd = self.config, self.config["hidden_size"]

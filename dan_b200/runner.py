@@ -113,7 +113,7 @@ class Runner:
             label_ids = _upload([x for l in labels for x in l], torch.int32, dev)
             off_t = _upload(offsets.astype(np.int32), torch.int32, dev)
             model = self.model
-            state = model.hidden(ids_t, pos_t, segs, saves)
+            state = model.residual(ids_t, pos_t, segs, saves)
             logits, probs = model.readout(state, read_rows, label_ids, off_t, max(len(l) for l in labels))
         except Exception:
             for _, _, entry in held:

@@ -11,7 +11,12 @@
  *   - callers own every buffer; the only allocation is the stream-K workspace of the GEMMs
  *     (dan_gemm_bf16 below), and dan_gemm_bf16_noalloc is the same GEMM without it.
  *
- * Each function names the reference (quangliz/dan) interface it replaces.
+ * Each function names the reference (quangliz/dan) interface it replaces, except
+ * dan_gemm_bf16_noalloc, which has no counterpart in the reference.
+ *
+ * The library caches per-device state (tensor-map encoder, SM counts, the stream-K workspace
+ * and the static scratch's address) for the life of the process: it must not outlive the
+ * device's primary context (no cudaDeviceReset between calls).
  */
 #ifndef DAN_B200_H
 #define DAN_B200_H
@@ -27,6 +32,12 @@ const char* dan_version(void);
 const char* dan_last_error(void);
 /* Copy *status_dev to *status_host, synchronise ``stream``, clear the device word if set. */
 int dan_read_status(int32_t* status_dev, int32_t* status_host, void* stream);
+/* Self-test of the kernels' bounded waits (dan's engine fails a batch whose forward raised,
+ * dan/engine.py:102-107; this checks the device side of that path): one thread waits on an
+ * mbarrier phase nothing completes (kind 0, reports 1 = kTimeoutFull) or on a device word
+ * ``flag`` that stays 0 (kind 1, reports 6 = kTimeoutPartial), gives up after about a second
+ * and returns, leaving the code in *status. */
+int dan_selftest_wait(int kind, const void* flag, int32_t* status, void* stream);
 
 /* Tree-masked attention over a packed batch, one launch for all segments and heads.
  * Replaces attend / _attend_varlen (dan/attention.py:200-241: three varlen flash calls,
@@ -59,12 +70,19 @@ int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, const void*
 int dan_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, const void* resid,
                   int64_t ldr, const void* bias, int m, int n, int k, int epilogue, int32_t* status, void* stream);
 
-/* dan_gemm_bf16 without any allocation: the stream-K partials live in a static device array of
- * the library (sized for up to 80 CTA pairs, i.e. 160 SMs; its address is looked up once per
- * device), so the call never allocates and can be captured in a CUDA graph from its first use.
- * Returns -22 (and allocates nothing) on a device with more SMs than the array covers. Calls on
- * one device share the array and must be stream-ordered with each other. Same arguments and
- * results as dan_gemm_bf16 (dan/models/llama.py:78,87,102). */
+/* dan_gemm_bf16 for callers that cannot allocate device memory: processes whose device memory is
+ * all handed out by their own allocator (a caching allocator or a memory plan made at start-up)
+ * and servers that must not make the device-synchronising cudaMalloc in the middle of a request.
+ * It has no counterpart in the reference. It allocates nothing: when a call takes the stream-K
+ * path (m >= 256, k at least 8192 bf16, a ragged last wave of 256 x 256 tiles) the partial tiles
+ * go to a static __device__ array of the library sized for at most 80 CTA pairs (about 21 MB,
+ * held by every device that loads the library until the process exits). Such a call on a device
+ * with more than 80 CTA pairs (160 SMs) returns -22; other shapes run on any device.
+ * The first call on a device looks up the array's address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture. All calls share the array
+ * and the kernel resets its per-tile counters itself, so each call starts from zeroed counters;
+ * calls that overlap on the GPU (different streams without ordering) race on the array.
+ * Same arguments and results as dan_gemm_bf16. */
 int dan_gemm_bf16_noalloc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
                           const void* resid, int64_t ldr, const void* bias, int m, int n, int k, int epilogue,
                           int32_t* status, void* stream);
@@ -124,7 +142,10 @@ int dan_kv_store(const void* k, const void* v, int64_t ld_row, int64_t ld_head, 
 
 /* Per question q: final RMSNorm of h[read_rows[q]], logits = W_lm[label_ids[off[q]:off[q+1]]] @ h
  * in fp32, and their softmax. Replaces the read-row gather + per-branch label_logits loop
- * (dan/runner.py:73-74, dan/models/llama.py:161-165) and readout.softmax (dan/readout.py:13-17). */
+ * (dan/runner.py:73-74, dan/models/llama.py:161-165) and readout.softmax (dan/readout.py:13-17).
+ * mode: 0 Llama norm, 1 zero-centred norm, 2 rows already normed (label_logits on a hidden
+ * state). A question with more than max_labels labels sets kBadIndex and keeps its first
+ * max_labels. */
 int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, const void* norm_w, float eps, int mode,
                       const void* w_lm, int64_t ldw, int64_t vocab, const int* label_ids, const int* offsets,
                       int n_questions, int hidden, int max_labels, float* logits, float* probs, int32_t* status,
@@ -158,6 +179,34 @@ int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld
 /* Bytes of scratch dan_gated_delta_scan needs for n_chunks chunks (45824 per chunk and value head
  * plus 34816 per chunk and key head). */
 int64_t dan_gated_delta_scratch_bytes(int n_chunks, int hk, int hv);
+/* dan_gated_delta_scan with the gates given instead of computed: beta [rows, hv] bf16 (row stride
+ * ld_beta) and the log decay g [rows, hv] fp32 (row stride ld_g); q and k still l2-normalised
+ * inside. Replaces delta_rule(q, k, v, g, beta, lengths, states) (dan/models/qwen3_5.py:136-158);
+ * tables, scratch and state pool as dan_gated_delta_scan. */
+int dan_delta_rule_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* beta, int64_t ld_beta,
+                        const float* g, int64_t ld_g, const int* segs, int n_segs, const int* branches,
+                        const int* chunks, int n_chunks, float* state_pool, int64_t slot_stride, void* out,
+                        int64_t ld_out, int hk, int hv, int dk, int dv, float q_scale, void* scratch,
+                        int64_t scratch_bytes, int32_t* status, void* stream);
+
+/* Stand-alone element-wise steps that the model path fuses elsewhere (dan/fused.py):
+ * out = bf16(bf16(silu(gate)) * up) (swiglu, fused.py:59-61); */
+int dan_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo, int rows, int cols,
+               void* stream);
+/* beta = bf16(sigmoid(b)), g = -exp(a_log) * softplus(a + dt_bias) fp32, per (row, head)
+ * (delta_gates, fused.py:79-82); */
+int dan_delta_gates(const void* b, int64_t ldb, const void* a, int64_t lda, const float* a_log, const float* dt_bias,
+                    void* beta, int64_t ldbeta, float* g, int64_t ldg, int rows, int heads, void* stream);
+/* exact merge of two attention results over disjoint key sets from their log-sum-exps;
+ * o [t_rows, heads, head_dim] bf16 with row stride ld_row, lse [heads, t_rows] fp32
+ * (lse_merge, fused.py:94-101); */
+int dan_lse_merge(const void* o_a, const float* lse_a, const void* o_b, const float* lse_b, void* out, int64_t ld_row,
+                  int t_rows, int heads, int head_dim, void* stream);
+/* e4m3 codes with one scale for the tensor, *scale = max(amax, 1e-12) / 448 (fp8_quantize with
+ * rowwise=False, fused.py:85-91; per-tensor FP8Linear, quant.py:26-33). */
+int dan_quantize_e4m3_tensor(const void* x, int64_t ldx, void* q, int64_t ldq, float* scale, int rows, int cols,
+                             void* stream);
+
 /* y = bf16(w * bf16(x_hat)) * silu(z) per (row, head) (gated_rms_norm, dan/fused.py:51-56). */
 int dan_gated_rms_norm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* w, float eps, void* y,
                        int64_t ldy, int rows, int heads, int dv, void* stream);

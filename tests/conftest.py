@@ -8,6 +8,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 sys.path.insert(0, ROOT)
 sys.path.insert(0, GOLDEN)
+# dan's own host code (answer formatting) is installed beside this package: the offline
+# install of the reference under baseline/_ref when present.
+_DAN = os.path.join(ROOT, "baseline", "_ref")
+if os.path.isdir(os.path.join(_DAN, "dan")):
+    sys.path.append(_DAN)
 
 
 def pytest_configure(config):

@@ -141,30 +141,6 @@ def dump_attention(dan):
                os.path.join(HERE, "attention_edges.pt"))
 
 
-def dump_readout(dan):
-    """dan/readout.py on seeded logits: answers (with rotations) and combine."""
-    from dan.readout import answers, combine
-    from dan.schema import Spec
-
-    rng = random.Random(21)
-    cases = []
-    for i in range(6):
-        specs = [Spec("yn", "noul", "", [("yes", ""), ("no", "")]),
-                 Spec("pick", "choice", "", [(c, "") for c in "abcde"[:rng.randint(2, 5)]]),
-                 Spec("rate", "score", "", [(str(j), "") for j in range(4)], legend=["l0", "l1", "l2", "l3"])]
-        perms = [[(j + r) % len(s.options) for j in range(len(s.options))]
-                 for s, r in zip(specs, (i % 2, i % 3, 0))]
-        logits = [[rng.gauss(0, 2) for _ in s.options] for s in specs]
-        plan = dan.prompt.ReadPlan([1], specs, [], [], {"forced": {"type": "noul", "noul": 1.0}},
-                                   ["pick", "forced", "yn", "rate"], 0, perms)
-        ans = answers(plan, logits)
-        comb = [c.tolist() for c in combine([plan, plan], [logits, logits])]
-        cases.append({"specs": [[s.key, s.type, [o[0] for o in s.options], s.legend] for s in specs],
-                      "perms": perms, "logits": logits, "answers": ans, "combine": comb})
-    with open(os.path.join(HERE, "readout.json"), "w") as f:
-        json.dump(cases, f)
-
-
 def run_model(dan, config, seed, batches, name, hf=True):
     from dan.reference import HFReference
     from dan.runner import Runner
@@ -205,7 +181,6 @@ def main():
                    "rows_mask2": branch_rows_mask(b2, 3).tolist()}, f)
     dump_pack(dan)
     dump_attention(dan)
-    dump_readout(dan)
 
     # configuration 1 (SmolLM2-135M shaped, tied embeddings) + a prefix-cache sequence
     cfg1 = weights.llama_config()

@@ -1,4 +1,5 @@
-"""The serving engine and answer readout on the CPU with fake replicas (no GPU).
+"""The serving engine on the CPU with fake replicas (no GPU); answers are formatted by dan's own
+readout module, installed beside this package.
 
 Mirrors the reference's serving tests (tests/test_api.py:51-68: concurrent decides are
 batched and give the same answers as solo reads) and its failure isolation
@@ -11,7 +12,7 @@ import threading
 import pytest
 import torch
 
-from dan_b200 import readout
+from dan.readout import answers
 from dan_b200.engine import AsyncEngine, Overloaded
 from dan_b200.plan import Branch, ReadPlan
 
@@ -73,7 +74,7 @@ def test_concurrent_decides_are_batched_and_match_solo_reads():
     assert eng.stats.batches < 12 and eng.stats.requests == 12
     for s, (ans, tokens) in zip(states, res):
         plan = FakePlanner().plans(s, QUESTIONS)[0]
-        solo = readout.answers(plan, FakeRunner().read_many([plan])[0])
+        solo = answers(plan, FakeRunner().read_many([plan])[0])
         assert ans == solo and tokens == AsyncEngine.cost(plan)
 
 
@@ -104,48 +105,6 @@ def test_overloaded_at_queue_cap():
             await eng.decide("x", QUESTIONS)
 
     run(main())
-
-
-def test_readout_shapes_and_rotation_inverse():
-    rng = random.Random(0)
-    spec = Spec("q", "choice", [("a", ""), ("b", ""), ("c", "")])
-    lg = [rng.gauss(0, 1) for _ in range(3)]
-    plan = ReadPlan([1], specs=[spec], branches=[], order=["q"], perms=[[1, 2, 0]])
-    ans = readout.answers(plan, [lg])["q"]
-    # shown position i held option perm[i]: canonical option o is read at position inv[o]
-    canon = [lg[2], lg[0], lg[1]]
-    want = readout.softmax(canon)
-    assert ans["choice"] == ["a", "b", "c"][max(range(3), key=want.__getitem__)]
-    assert all(abs(ans["probabilities"][k] - v) < 1e-6 for k, v in zip("abc", want))
-    assert 0 <= ans["confidence"] <= 1
-    # averaging over rotations in log space
-    plan2 = ReadPlan([1], specs=[spec], branches=[], order=["q"], perms=[[0, 1, 2]])
-    comb = readout.combine([plan, plan2], [[lg], [canon]])[0]
-    assert torch.allclose(comb, torch.log_softmax(torch.tensor(canon), 0), atol=1e-6)
-
-
-def test_readout_matches_reference_golden():
-    from conftest import golden
-
-    for case in golden("readout.json"):
-        specs = [Spec(k, t, [(o, "") for o in opts], legend) for k, t, opts, legend in case["specs"]]
-        plan = ReadPlan([1], specs=specs, branches=[], forced={"forced": {"type": "noul", "noul": 1.0}},
-                        order=["pick", "forced", "yn", "rate"], perms=case["perms"])
-        got = readout.answers(plan, case["logits"])
-        assert got.keys() == case["answers"].keys()
-        for k, want in case["answers"].items():
-            for f, v in want.items():
-                if isinstance(v, dict):
-                    assert v.keys() == got[k][f].keys()
-                    assert all(abs(got[k][f][x] - v[x]) < 1e-6 for x in v) if isinstance(next(iter(v.values())), float) \
-                        else got[k][f] == v
-                elif isinstance(v, float):
-                    assert abs(got[k][f] - v) < 1e-6
-                else:
-                    assert got[k][f] == v
-        comb = readout.combine([plan, plan], [case["logits"], case["logits"]])
-        for c, w in zip(comb, case["combine"]):
-            assert torch.allclose(c, torch.tensor(w), atol=1e-6)
 
 
 class PrefixPlanner(FakePlanner):
@@ -273,7 +232,7 @@ def test_pipelined_batches_stay_bounded_and_answer_like_solo_reads(in_flight):
         if isinstance(r, Exception):
             continue
         plan = FakePlanner().plans(s, QUESTIONS)[0]
-        assert r[0] == readout.answers(plan, FakeRunner().read_many([plan])[0])
+        assert r[0] == answers(plan, FakeRunner().read_many([plan])[0])
     assert 0 < eng.stats.busy_s <= wall + 1e-3
     assert runner.outstanding == 0
 

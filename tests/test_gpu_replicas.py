@@ -47,7 +47,7 @@ def test_engine_over_gpu_replicas(tiny_dir):
 
     from test_engine import QUESTIONS, FakePlanner
 
-    from dan_b200 import readout
+    from dan.readout import answers, combine
     from dan_b200.engine import AsyncEngine
 
     path, _ = tiny_dir
@@ -74,5 +74,5 @@ def test_engine_over_gpu_replicas(tiny_dir):
     for s, (ans, tokens) in zip(states, res):
         plans = FakePlanner().plans(s, QUESTIONS)
         reads = runners[0].read_many(plans)
-        solo = readout.answers(plans[0], readout.combine(plans, reads), logits_canonical=True)
+        solo = answers(plans[0], combine(plans, reads), logits_canonical=True)
         assert close(ans, solo) and tokens == AsyncEngine.cost(plans[0])

@@ -198,3 +198,29 @@ def test_recurrent_layout_chunks_follow_each_segments_runs():
                 c += 1
     assert sorted(seen) == list(range(rl.n_chunks))  # every chunk belongs to exactly one run
     assert recs[[r[1] for r in recs].index(300)][2] == 130
+
+
+def test_prefix_cache_contract():
+    """dan's PrefixCache contract (dan/cache.py:11-39): exact keys, hit / miss counters, bytes
+    used, least-recently-used eviction, entries larger than the budget not kept."""
+    from dan_b200.cache import PrefixCache
+
+    def kv(rows):
+        return {0: (torch.zeros(rows, 50, dtype=torch.bfloat16), torch.zeros(rows, 50, dtype=torch.bfloat16))}
+
+    c = PrefixCache(max_bytes=3000)
+    assert c.get([1, 2]) is None and c.misses == 1
+    big = kv(10)  # 2000 bytes
+    c.put([1, 2], big)
+    assert c.used == 2000 and c.get([1, 2]) is big and c.hits == 1
+    c.put([1, 2], big)  # already present: unchanged
+    assert c.used == 2000
+    c.put([3], kv(2))  # 400 bytes
+    assert c.used == 2400
+    c.get([1, 2])  # [3] is now the least recently used
+    c.put([4], kv(2))  # 2800: fits
+    c.put([5], kv(6))  # 1200 more: evicts [3], then [1, 2]
+    assert c.get([3]) is None and c.get([1, 2]) is None and c.get([4]) is not None and c.get([5]) is not None
+    assert c.used == 1600
+    c.put([6], kv(40))  # larger than the whole budget: not kept, nothing evicted
+    assert c.get([6]) is None and c.used == 1600
