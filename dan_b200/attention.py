@@ -254,8 +254,9 @@ class _StagedPasts:
         if self.layer == layer:
             return self
         hkv, d = like.shape[0], like.shape[2]
-        pk = torch.empty(self.n_pages * BLOCK, hkv, d, dtype=like.dtype, device=like.device)
-        pv = torch.empty_like(pk)
+        # zeroed: rows past each past's length are masked but still multiply into P V
+        pk = torch.zeros(self.n_pages * BLOCK, hkv, d, dtype=like.dtype, device=like.device)
+        pv = torch.zeros_like(pk)
         for s, t in zip(originals, self.segments):
             if not s.past_len:
                 continue

@@ -55,8 +55,11 @@ class PrefixPool:
             budget -= self.n_slots * self.slot_bytes
         self.n_pages = max(0, budget // self.page_bytes) if layers else 0
         dev = torch.device(device)
-        self.k = torch.empty(layers, self.n_pages * PAGE, kv_heads, head_dim, dtype=torch.bfloat16, device=dev)
-        self.v = torch.empty_like(self.k)
+        # Zeroed once: the kernel masks the rows of an entry's last page past its length, and a
+        # masked row still enters P V with weight 0, which must not meet a NaN bit pattern. Pages
+        # reused after eviction hold earlier entries' (finite) keys and values.
+        self.k = torch.zeros(layers, self.n_pages * PAGE, kv_heads, head_dim, dtype=torch.bfloat16, device=dev)
+        self.v = torch.zeros_like(self.k)
         if recurrent:  # layer-major, so one layer's slots are one contiguous block
             nl, kr, cd, hv, dk, dv = recurrent
             self.conv = torch.zeros(nl, self.n_slots, kr, cd, dtype=torch.bfloat16, device=dev)

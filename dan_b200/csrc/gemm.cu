@@ -65,9 +65,9 @@ struct Params {
   // Narrow tail (pair kernel, no stream-K): tiles [nt_first, sk_first) each run as nt_split
   // items of BN / nt_split columns, so a ragged last wave spreads over more pairs; 1 = none.
   int nt_first, nt_split;
-  float* sk_part;     // [pairs][2][BN][128] fp32 partial accumulators, column-major per CTA
-  uint32_t* sk_flag;  // [pairs][2][4] per-warp "partial written" flags (value = epoch + 1)
-  uint32_t* sk_ctrl;  // [0] epoch, [1] CTAs finished in this launch
+  float* sk_part;                 // [pairs][2 ranks][2 segments][BN][128] fp32 partials, column-major
+  unsigned long long* sk_cnt;     // [2 pairs][2 ranks][4 warps] arrivals per split tile: epoch << 32 | n
+  uint32_t* sk_ctrl;              // [0] epoch, [1] CTAs finished in this launch
   int tma_out;        // epilogue writes through the shared-memory sink and TMA stores
 };
 
@@ -637,15 +637,22 @@ constexpr int P_A_BYTES = 128 * KBYTES, P_B_BYTES = 128 * KBYTES;
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + SINK_BYTES + 1024 + 512;
 
-// Stream-K partials. Slot (pair, rank) holds one CTA's 128 x 256 fp32 accumulator stored
-// column-major ([col][row]) so a warp's 32 rows of one column are one 128-byte line.
-__device__ __forceinline__ float* sk_slot(const Params& p, int slot) {
-  return p.sk_part + static_cast<int64_t>(slot) * BN * 128;
+// Stream-K partials: one CTA's 128 x 256 fp32 accumulator of a split-tile segment, stored
+// column-major ([col][row]) so a warp's 32 rows of one column are one 128-byte line. Pair q has
+// two slots per CTA rank: the first segment of its share (which = 0) and the last (which = 1).
+__device__ __forceinline__ float* sk_slot(const Params& p, int q, int rank, int which) {
+  return p.sk_part + static_cast<int64_t>((q * 2 + rank) * 2 + which) * BN * 128;
 }
 
-__device__ __forceinline__ void sk_store_partial(const Params& p, uint32_t taddr, int slot, int r_in, int sub,
-                                                 int lane, uint32_t epoch) {
-  float* dst = sk_slot(p, slot) + r_in;
+// First stream-K iteration of pair q's share.
+__device__ __forceinline__ int sk_start(const Params& p, int q, int n_pairs) {
+  return static_cast<int>(static_cast<long long>(q) * p.sk_iters / n_pairs);
+}
+
+// This warp's 32 rows of its TMEM accumulator -> its slot (``dst`` already offset by the row).
+// Not inlined (nor sk_fold): inlined, their 32-value arrays pushed the pair kernel, already at
+// 255 registers, into spilling.
+__device__ __noinline__ void sk_store_partial(uint32_t taddr, float* dst) {
 #pragma unroll 1
   for (int c = 0; c < BN; c += 32) {
     uint32_t r[32];
@@ -654,36 +661,57 @@ __device__ __forceinline__ void sk_store_partial(const Params& p, uint32_t taddr
 #pragma unroll
     for (int i = 0; i < 32; ++i) __stcg(dst + (c + i) * 128, __uint_as_float(r[i]));
   }
-  __threadfence();
-  __syncwarp();
-  if (lane == 0) st_release_gpu(p.sk_flag + slot * 4 + sub, epoch + 1);
 }
 
-// Head of a split tile: add the partials of pairs pair+1, ... whose shares start inside the
-// tile (before iteration ``tile_end``), in pair order, into this warp's TMEM accumulator rows.
-__device__ __forceinline__ void sk_gather_partials(const Params& p, uint32_t taddr, int pair, int n_pairs, int rank,
-                                                   int r_in, int sub, uint32_t epoch, int tile_end) {
-  int q_end = pair + 1;
-  while (q_end < n_pairs && static_cast<int>(static_cast<long long>(q_end) * p.sk_iters / n_pairs) < tile_end)
-    ++q_end;
-  for (int q = pair + 1; q < q_end; ++q)
-    if (!wait_flag(p.sk_flag + (q * 2 + rank) * 4 + sub, epoch + 1)) report(p.status, kTimeoutPartial);
+// Count this warp's segment of a split tile in; true for the last of the tile's ``n`` segments
+// to arrive, which then folds every segment's partial and runs the epilogue. No warp waits for
+// another CTA, so the scheme needs no co-residency of the grid. The counter word is (launch
+// epoch << 32) | arrivals: a count left by an earlier launch that gave up on a bounded wait is
+// restarted, not added to. The CAS loop retries only on a concurrent arrival (at most n times).
+__device__ __forceinline__ bool sk_arrive(unsigned long long* cnt, uint32_t epoch, int n, int lane) {
+  __threadfence();  // the warp's partial is visible device-wide before it is counted
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(cnt), want;
+    for (;;) {
+      want = ((old >> 32) == epoch ? old : tag) + 1;
+      const unsigned long long seen = atomicCAS(cnt, old, want);
+      if (seen == old) break;
+      old = seen;
+    }
+    last = static_cast<int>(want & 0xffffffffull) == n;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) __threadfence();  // the other segments' partials are read after their counts
+  return last != 0;
+}
+
+// The last arriver of a split tile: the sum of segments qa..qb's partials in pair order (its
+// own from TMEM, the others from their slots), the same order whichever segment arrives last,
+// so results are deterministic; written back to this warp's TMEM rows for the epilogue.
+__device__ __noinline__ void sk_fold(const Params& p, uint32_t taddr, int self, int qa, int qb, int rank,
+                                        int tile_start, int n_pairs, int r_in) {
 #pragma unroll 1
   for (int c = 0; c < BN; c += 32) {
-    uint32_t r[32];
-    tmem_ld32(taddr + c, r);
-    tmem_wait_ld();
-    float acc[32];
+    uint32_t acc[32];
+#pragma unroll 1
+    for (int q = qa; q <= qb; ++q) {
+      uint32_t v[32];
+      if (q == self) {
+        tmem_ld32(taddr + c, v);
+        tmem_wait_ld();
+      } else {
+        const float* src = sk_slot(p, q, rank, sk_start(p, q, n_pairs) < tile_start ? 1 : 0) + r_in;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(r[i]);
-    for (int q = pair + 1; q < q_end; ++q) {
-      const float* src = sk_slot(p, q * 2 + rank) + r_in;
+        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__ldcg(src + (c + i) * 128));
+      }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc[i] += __ldcg(src + (c + i) * 128);
+      for (int i = 0; i < 32; ++i)
+        acc[i] = q == qa ? v[i] : __float_as_uint(__uint_as_float(acc[i]) + __uint_as_float(v[i]));
     }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(acc[i]);
-    tmem_st32(taddr + c, r);
+    tmem_st32(taddr + c, acc);
   }
   tmem_wait_st();
 }
@@ -827,9 +855,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int t = w.t, kb = w.kb, ke = w.ke;
       int tm, tn;
       pair_tile(t, tiles_m, p.tiles_n, p.order, p.group, tm, tn);
-      if (kb == 0) epilogue_prefetch(p, tm * 256 + static_cast<int>(rank) * 128 + r_in, tn);
+      const bool split = kb > 0 || ke < k_iters;
+      if (!split) epilogue_prefetch(p, tm * 256 + static_cast<int>(rank) * 128 + r_in, tn);
       float ws[8];
-      if (FP8 && kb == 0) load_tile_scales(p, tn, lane, ws);
+      if (FP8 && !split) load_tile_scales(p, tn, lane, ws);
       if (!mbar_wait(&tfull[buf], acc_phase)) {
         report(p.status, kTimeoutMma);
         break;
@@ -838,16 +867,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = tm * 256 + static_cast<int>(rank) * 128 + r_in;
       o.row0 = tm * 256 + static_cast<int>(rank) * 128 + sub * 32;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
-      const int slot = pair * 2 + static_cast<int>(rank);
-      if (kb > 0) {
-        // Tail of a split tile: park the partial sum for the pair that owns the tile's head.
-        sk_store_partial(p, taddr, slot, r_in, sub, lane, epoch);
-      } else {
-        if (ke < k_iters)  // head of a split tile: fold in the later pairs' partials first
-          sk_gather_partials(p, taddr, pair, n_pairs, static_cast<int>(rank), r_in, sub, epoch,
-                             (t - p.sk_first + 1) * k_iters);
-        epilogue_tile<FP8>(p, o, taddr, row, tn, w.sub, w.width, ws);
+      bool last = true;  // this warp writes the tile (always, unless the tile is split)
+      if (split) {
+        // Segments qa..qb of pairs' shares cover this tile; each parks its partial and counts
+        // in, and the last to arrive folds them all and writes the tile.
+        const int tr = t - p.sk_first, tile_start = tr * k_iters, tile_end = tile_start + k_iters;
+        int qa = pair, qb = pair;
+        while (sk_start(p, qa, n_pairs) > tile_start) --qa;
+        while (qb + 1 < n_pairs && sk_start(p, qb + 1, n_pairs) < tile_end) ++qb;
+        const int which = sk_start(p, pair, n_pairs) < tile_start ? 1 : 0;
+        sk_store_partial(taddr, sk_slot(p, pair, static_cast<int>(rank), which) + r_in);
+        last = sk_arrive(p.sk_cnt + (tr * 2 + static_cast<int>(rank)) * 4 + sub, epoch, qb - qa + 1, lane);
+        if (last) {
+          if (FP8) load_tile_scales(p, tn, lane, ws);
+          sk_fold(p, taddr, pair, qa, qb, static_cast<int>(rank), tile_start, n_pairs, r_in);
+        }
       }
+      if (last) epilogue_tile<FP8>(p, o, taddr, row, tn, w.sub, w.width, ws);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(buf ? te1 : te0);
@@ -865,7 +901,7 @@ done:
     tmem_dealloc_pair(tmem, 512);
   }
   if (p.sk_iters && threadIdx.x == 0) {
-    // The last CTA out advances the epoch, so the next launch's flags never match this one's.
+    // The last CTA out advances the epoch, so the next launch's arrival counts never match this one's.
     __threadfence();
     if (atomicAdd(p.sk_ctrl + 1, 1u) == gridDim.x - 1) {
       p.sk_ctrl[1] = 0;
@@ -879,9 +915,17 @@ done:
 // Allocated on first use (cudaMalloc) and kept for the life of the process.
 struct Workspace {
   float* part;
-  uint32_t* flag;
+  unsigned long long* cnt;
   uint32_t* ctrl;
 };
+
+// Partials: two segment slots per (pair, CTA rank), 128 x 256 fp32 each. Counters: one per
+// (split tile, CTA rank, epilogue warp), at most 2 x pairs split tiles; then the two control
+// words (epoch, CTAs finished).
+constexpr size_t sk_part_bytes(int pairs) { return static_cast<size_t>(pairs) * 2 * 2 * BN * 128 * sizeof(float); }
+constexpr size_t sk_cnt_bytes(int pairs) {
+  return static_cast<size_t>(pairs) * 2 * 2 * 4 * sizeof(unsigned long long) + 2 * sizeof(uint32_t);
+}
 
 static Workspace* workspace(cudaStream_t stream, int pairs) {
   static std::mutex mu;
@@ -895,29 +939,27 @@ static Workspace* workspace(cudaStream_t stream, int pairs) {
   auto it = all.find({dev, stream});
   if (it != all.end()) return &it->second;
   Workspace w{};
-  const size_t part_bytes = static_cast<size_t>(pairs) * 2 * BN * 128 * sizeof(float);
-  const size_t flag_bytes = static_cast<size_t>(pairs) * 2 * 4 * sizeof(uint32_t) + 2 * sizeof(uint32_t);
+  const size_t part_bytes = sk_part_bytes(pairs), cnt_bytes = sk_cnt_bytes(pairs);
   void* a = nullptr;
   void* b = nullptr;
-  if (cudaMalloc(&a, part_bytes) != cudaSuccess || cudaMalloc(&b, flag_bytes) != cudaSuccess ||
-      cudaMemset(b, 0, flag_bytes) != cudaSuccess) {
+  if (cudaMalloc(&a, part_bytes) != cudaSuccess || cudaMalloc(&b, cnt_bytes) != cudaSuccess ||
+      cudaMemset(b, 0, cnt_bytes) != cudaSuccess) {
     if (a) cudaFree(a);
     if (b) cudaFree(b);
-    set_error("stream-K workspace allocation of %zu bytes failed", part_bytes + flag_bytes);
+    set_error("stream-K workspace allocation of %zu bytes failed", part_bytes + cnt_bytes);
     return nullptr;
   }
   w.part = static_cast<float*>(a);
-  w.flag = static_cast<uint32_t*>(b);
-  w.ctrl = w.flag + static_cast<size_t>(pairs) * 2 * 4;
+  w.cnt = static_cast<unsigned long long*>(b);
+  w.ctrl = reinterpret_cast<uint32_t*>(w.cnt + static_cast<size_t>(pairs) * 2 * 2 * 4);
   return &(all[{dev, stream}] = w);
 }
 
 // Allocation-free stream-K scratch for dan_gemm_bf16_noalloc: one static device array per
 // device (zero at module load), laid out like a Workspace for up to kStaticPairs CTA pairs.
 constexpr int kStaticPairs = 80;
-constexpr size_t kStaticPartBytes = static_cast<size_t>(kStaticPairs) * 2 * BN * 128 * sizeof(float);
-constexpr size_t kStaticFlagWords = static_cast<size_t>(kStaticPairs) * 2 * 4 + 2;
-static __device__ __align__(256) unsigned char g_sk_scratch[kStaticPartBytes + kStaticFlagWords * sizeof(uint32_t)];
+constexpr size_t kStaticPartBytes = sk_part_bytes(kStaticPairs);
+static __device__ __align__(256) unsigned char g_sk_scratch[kStaticPartBytes + sk_cnt_bytes(kStaticPairs)];
 
 // The static scratch of the current device as a Workspace (its address looked up once per
 // device with cudaGetSymbolAddress); nullptr with the error text set if it is unavailable.
@@ -939,8 +981,8 @@ static const Workspace* static_workspace() {
   }
   Workspace w{};
   w.part = static_cast<float*>(base);
-  w.flag = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(base) + kStaticPartBytes);
-  w.ctrl = w.flag + static_cast<size_t>(kStaticPairs) * 2 * 4;
+  w.cnt = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(base) + kStaticPartBytes);
+  w.ctrl = reinterpret_cast<uint32_t*>(w.cnt + static_cast<size_t>(kStaticPairs) * 2 * 2 * 4);
   return &(all[dev] = w);
 }
 
@@ -1044,7 +1086,7 @@ int launch(const void* a, int64_t lda, const void* w, int64_t ldw, Params p, cud
         p.sk_first = first;
         p.sk_iters = static_cast<int>(iters);
         p.sk_part = ws->part;
-        p.sk_flag = ws->flag;
+        p.sk_cnt = ws->cnt;
         p.sk_ctrl = ws->ctrl;
         pairs = max_pairs;
       }

@@ -91,15 +91,19 @@ def pack(plans, cache=None, use_cache=True):
     return ids, pos, segs, reads, stores
 
 
-def read_many(state, config, plans, cache=None, fp8=False):
+def read_many(state, config, plans, cache=None, fp8=False, bf16=False):
     """Per plan, per branch: fp32 label logits (runner.py:66-82); ``fp8``: decoder linears
-    through the FP8 restatement (Llama family only)."""
+    through the FP8 restatement (Llama family only); ``bf16``: the reference's bf16 path
+    (``Runner(dtype=torch.bfloat16)``, the dtype of its GPU and FP8 paths)."""
     arch = qwen3_5 if config["model_type"].startswith("qwen3_5") else llama
     ids, pos, segs, reads, stores = pack(plans, cache)
     flat = []
     if reads:
-        h = arch.hidden(state, config, ids, pos, segs, fp8=True) if fp8 else arch.hidden(state, config, ids, pos, segs)
-        flat = [arch.label_logits(state, h[r], labels) for r, labels in reads]
+        kw = {"bf16": True} if bf16 else {}
+        if fp8:
+            kw["fp8"] = True
+        h = arch.hidden(state, config, ids, pos, segs, **kw)
+        flat = [arch.label_logits(state, h[r], labels, bf16=bf16) for r, labels in reads]
         for static, seg in stores:
             cache.put(static, seg["saved"])
     out, k = [], 0

@@ -22,6 +22,12 @@ Fixtures:
   gated attention layer) whose trunks exceed one 64-token delta-rule chunk.
 - ``tree_mask.json``: ``tree_mask`` / ``branch_rows_mask`` rows
   (tests/test_runner.py:16-22).
+- ``fullsize.json``: ``Runner.read_many`` label logits in fp32 and in bf16 (the reference's
+  GPU dtype, here on the CPU) for a 2-layer Llama-3-8B-shaped slice on one configuration-3
+  batch and a 4-layer Qwen3.5-4B-shaped slice on one configuration-4 batch.
+
+The model fixtures also hold the bf16 runner's logits (``runner_bf16``), which pin the
+oracle's bf16 rounding mode.
 """
 import argparse
 import json
@@ -39,6 +45,7 @@ sys.path.insert(0, ROOT)
 from dan_b200 import synthetic  # noqa: E402
 from oracle import weights  # noqa: E402
 
+SHM = "/dev/shm" if os.path.isdir("/dev/shm") else None  # checkpoints of GBs: write to memory
 EDGE_SHAPES = [(40, [5, 9, 1], 0), (7, [30], 12), (1, [3, 3, 3, 3, 3, 3], 0), (64, [], 0), (13, [17, 2], 20)]
 
 
@@ -145,21 +152,64 @@ def run_model(dan, config, seed, batches, name, hf=True):
     from dan.reference import HFReference
     from dan.runner import Runner
 
-    with tempfile.TemporaryDirectory() as tmp:
+    with tempfile.TemporaryDirectory(dir=SHM) as tmp:
         weights.save_checkpoint(tmp, config, weights.random_state(config, seed))
         runner = Runner(tmp, "cpu", torch.float32)
+        runner16 = Runner(tmp, "cpu", torch.bfloat16)  # the reference's bf16 path (its GPU dtype)
         ref = HFReference(tmp) if hf else None
         recs = []
         for bname, plans in batches:
             rp = ref_plans(dan.prompt, plans)
             got = runner.read_many(rp)
+            got16 = runner16.read_many(ref_plans(dan.prompt, plans))
             rec = {"name": bname, "plans": [plan_json(p) for p in plans],
-                   "runner": [[x.tolist() for x in per] for per in got], "hits": runner.cache.hits}
+                   "runner": [[x.tolist() for x in per] for per in got], "hits": runner.cache.hits,
+                   "runner_bf16": [[x.tolist() for x in per] for per in got16]}
             if ref is not None:
                 rec["hf"] = [[x.tolist() for x in ref.read(p)] for p in rp]
             recs.append(rec)
     with open(os.path.join(HERE, name), "w") as f:
         json.dump({"config": config, "seed": seed, "batches": recs}, f)
+
+
+def plans_digest(plans):
+    """A short hash of a batch's plans (the tests regenerate them from the same seed)."""
+    import hashlib
+
+    return hashlib.sha256(json.dumps([plan_json(p) for p in plans]).encode()).hexdigest()[:16]
+
+
+def fullsize_cases():
+    """(name, config, weight seed, plans) of the full-shape slices: 2 Llama-3-8B-shaped layers on
+    one configuration-3 batch, and 4 Qwen3.5-4B-shaped layers (3 Gated DeltaNet + 1 gated
+    attention) on one configuration-4 batch; vocabulary tied to lm_head."""
+    from dan_b200.loader import llama3_8b_config, qwen35_4b_config
+
+    c3 = dict(llama3_8b_config(), num_hidden_layers=2, tie_word_embeddings=True, architectures=["LlamaForCausalLM"],
+              torch_dtype="float32", hidden_act="silu", max_position_embeddings=131072)
+    c4 = dict(qwen35_4b_config(), num_hidden_layers=4, tie_word_embeddings=True, architectures=["Qwen3_5ForCausalLM"],
+              torch_dtype="float32", hidden_act="silu", max_position_embeddings=32768, attention_bias=False)
+    c4["layer_types"] = c4["layer_types"][:4]
+    return [("cfg3_llama3_8b_2layers", c3, 8, synthetic.batch(3, seed=21, vocab=c3["vocab_size"])),
+            ("cfg4_qwen35_4b_4layers", c4, 9, synthetic.batch(4, seed=22, vocab=c4["vocab_size"]))]
+
+
+def dump_fullsize(dan):
+    """The reference's own fp32 and bf16 label logits on the full-shape slices (CPU)."""
+    from dan.runner import Runner
+
+    out = {}
+    for name, config, seed, plans in fullsize_cases():
+        with tempfile.TemporaryDirectory(dir=SHM) as tmp:
+            weights.save_checkpoint(tmp, config, weights.random_state(config, seed))
+            rec = {"seed": seed, "digest": plans_digest(plans)}
+            for key, dtype in (("runner", torch.float32), ("runner_bf16", torch.bfloat16)):
+                runner = Runner(tmp, "cpu", dtype, cache_bytes=0)
+                rec[key] = [[x.tolist() for x in per] for per in runner.read_many(ref_plans(dan.prompt, plans))]
+                del runner
+        out[name] = rec
+    with open(os.path.join(HERE, "fullsize.json"), "w") as f:
+        json.dump(out, f)
 
 
 def main():
@@ -198,6 +248,7 @@ def main():
     hp = small_plans(rng, cfgh["vocab_size"], 3, trunk=(70, 150), nb=(1, 3), blen=(3, 9), static=(20, 60))
     hx = small_plans(rng, cfgh["vocab_size"], 1, trunk=(70, 150), nb=(1, 3), blen=(3, 9), static=(20, 60))
     run_model(dan, cfgh, 0, [("cold", hp), ("warm", hp), ("mixed", [hp[2], hx[0], hp[0]])], "tiny_hybrid.json")
+    dump_fullsize(dan)
 
 
 if __name__ == "__main__":

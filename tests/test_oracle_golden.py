@@ -82,3 +82,34 @@ def test_useful_pairs_matches_mask_count():
     segs = [{"start": 0, "end": 10, "branch": [0] * 4 + [1] * 3 + [2] * 3,
              "past": (torch.zeros(1, 5, 2), torch.zeros(1, 5, 2))}]
     assert OA.useful_pairs(segs) == int(OA.segment_mask(segs[0]["branch"], 5).sum())
+
+
+def _probs_gap(a, b):
+    worst = 0.0
+    for pa, pb in zip(a, b):
+        for x, y in zip(pa, pb):
+            px = torch.softmax(torch.as_tensor(x).double(), 0)
+            worst = max(worst, (px - torch.softmax(torch.as_tensor(y).double(), 0)).abs().max().item())
+    return worst
+
+
+def _bf16_golden(name):
+    """The oracle's bf16 mode against the reference run in bf16 (``runner_bf16``): both round to
+    bf16 at the same module boundaries, so they land within the reference's own bf16-vs-fp32
+    distance of each other (attention and matmul accumulation orders still differ)."""
+    g = golden(name)
+    cfg, state = g["config"], weights.random_state(g["config"], g["seed"])
+    cache = OR.PrefixCache()
+    for b in g["batches"]:
+        got = OR.read_many(state, cfg, plans_from_json(b["plans"]), cache, bf16=True)
+        own_gap = _probs_gap(b["runner_bf16"], b["runner"])
+        assert _probs_gap(got, b["runner_bf16"]) <= max(own_gap, 1e-3), b["name"]
+        assert _probs_gap(got, b["runner"]) <= 2 * own_gap + 1e-3, b["name"]
+
+
+def test_tiny_llama_bf16_mode_golden():
+    _bf16_golden("tiny_llama.json")
+
+
+def test_tiny_hybrid_bf16_mode_golden():
+    _bf16_golden("tiny_hybrid.json")
