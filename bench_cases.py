@@ -14,6 +14,8 @@ are larger than L2 where the configuration's are.
 - deltanet: causal conv + gated delta scan of one configuration-4 batch
   (Qwen3.5-4B-style: 16 key / 32 value heads x 128).
 - norm: RMSNorm of [7089, 4096].
+- gemm8: the four projections in e4m3 at M = 3400 (configuration 5).
+- readout, gate, gnorm, conv, quant, kvstore: the HBM-bound kernels at benchmark sizes.
 """
 import argparse
 import json
@@ -288,9 +290,51 @@ def quant(iters):
     return out
 
 
+def gemm8(iters):
+    """The four Llama-3-8B decoder projections in e4m3 at configuration 5's batch size (M = 3400
+    new tokens): q/k/v + RoPE, o + residual, gate/up + SwiGLU, down + residual, CUDA-event timed."""
+    dev = torch.device("cuda")
+    m = 3400
+    g = torch.Generator(device=dev).manual_seed(0)
+    pos = torch.arange(m, device=dev)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, dtype=torch.float32, device=dev) / 128))
+    table = ops.rope_table(pos, inv)
+    out = {}
+    for name, n, k in (("qkv_rope", 6144, 4096), ("o_residual", 4096, 4096), ("gate_up_swiglu", 28672, 4096),
+                       ("down_residual", 4096, 14336)):
+        xq, xs = ops.quantize_e4m3(torch.randn(m, k, device=dev, generator=g).bfloat16())
+        wq, ws = ops.quantize_e4m3((torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16())
+        r = torch.randn(m, n, device=dev, generator=g).bfloat16()
+        fn = {"qkv_rope": lambda: ops.linear_e4m3_rope(xq, xs, wq, ws, table, 5120, 128),
+              "o_residual": lambda: ops.linear_e4m3(xq, xs, wq, ws, residual=r),
+              "gate_up_swiglu": lambda: ops.linear_e4m3(xq, xs, wq, ws, swiglu=True),
+              "down_residual": lambda: ops.linear_e4m3(xq, xs, wq, ws, residual=r)}[name]
+        ms = _time(fn, iters)
+        out[name] = {"m": m, "n": n, "k": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e12 * 1e3}
+    return out
+
+
+def kvstore(iters):
+    """Prefix K/V page stores of one configuration-5 save: 1024 rows of 8 kv heads x 128 (k and v,
+    read in place from the fused q/k/v projection at row stride 6144) into pool pages, graph-timed."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    n, hkv, d = 1024, 8, 128
+    qkv = torch.randn(n, 6144, device=dev, generator=g).bfloat16()
+    k = qkv[:, 4096:5120].view(n, hkv, d)
+    v = qkv[:, 5120:].view(n, hkv, d)
+    pool_k = torch.zeros(64 * 128, hkv, d, dtype=torch.bfloat16, device=dev)
+    pool_v = torch.zeros_like(pool_k)
+    src = torch.arange(n, dtype=torch.int32, device=dev)
+    dst = torch.randperm(64 * 128, device=dev, generator=g)[:n].to(torch.int32)
+    ms = _graph_time(lambda: ops.kv_store(k, v, pool_k, pool_v, src, dst), n=max(iters, 2) * 5)
+    return {"rows": n, "us": 1000 * ms, "gbs": 2 * 2 * n * hkv * d * 2 / ms / 1e6}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "readout", "gate", "fp8peak"])
+    ap.add_argument("case", choices=["gemm", "gemm8", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "readout",
+                                     "gate", "kvstore", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()
     res = globals()[a.case](max(a.iters, 2))

@@ -536,18 +536,19 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&s)[32], float sl2, fl
   sum += s0 + s1;
 }
 
-// One 32-column chunk of S: mask it unless fully visible; a fully masked chunk needs no work.
-__device__ __forceinline__ void chunk_prep(uint32_t (&s)[32], uint32_t mw, float& mx) {
-  if (mw == 0u) return;
-  if (mw != 0xffffffffu) mask_chunk(s, mw);
+// Warp-uniform forms (``cls``: 0 no lane sees a key of the chunk, 1 mixed, 2 every lane sees
+// every key).
+__device__ __forceinline__ void chunk_prep_u(uint32_t (&s)[32], uint32_t mw, uint32_t cls, float& mx) {
+  if (cls == 0u) return;
+  if (cls == 1u) mask_chunk(s, mw);
   chunk_max(s, mx);
 }
-__device__ __forceinline__ void chunk_p(const uint32_t (&s)[32], uint32_t mw, float sl2, float mu, float& sum,
-                                        uint32_t (&pk)[16]) {
-  if (mw == 0u) {
+__device__ __forceinline__ void chunk_p_u(const uint32_t (&s)[32], uint32_t cls, float sl2, float mu, float& sum,
+                                          uint32_t (&pk)[16]) {
+  if (cls == 0u) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) pk[i] = 0u;
-  } else if (mw == 0xffffffffu) {
+  } else if (cls == 2u) {
     chunk_exp<true>(s, sl2, mu, sum, pk);
   } else {
     chunk_exp<false>(s, sl2, mu, sum, pk);
@@ -785,18 +786,35 @@ __global__ void __launch_bounds__(320, 1)
         // every outstanding load): pass 1 takes chunks 3, 2 then 1, 0 for the row max and keeps
         // chunks 1 and 0; pass 2 writes P0 and P1 from them (P chunk c covers S columns
         // [16c, 16c + 16), already consumed), then reloads chunks 2 and 3 for P2 and P3.
+        // Each chunk takes one of three warp-uniform paths: no lane sees any of its keys (P = 0),
+        // every lane sees every key (no mask; some exponentials on the FMA pipe), or mixed (scores
+        // masked to -inf per lane, MUFU exponentials); branching on each row's own mask word had
+        // serialised up to three paths per chunk within a warp (+1.3% on a configuration-2 batch).
+        // Measured and not kept: the whole row in registers with one TMEM round trip (twelve
+        // warps, setmaxnreg moving registers to the softmax warpgroups): no change.
+        uint32_t cls = 0;  // 2 bits per chunk: 0 none visible, 1 mixed, 2 all visible
+        if (full) {
+          cls = 0xaau;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const bool all = __all_sync(0xffffffffu, mw[c] == 0xffffffffu);
+            const bool any = __any_sync(0xffffffffu, mw[c] != 0u);
+            cls |= (all ? 2u : (any ? 1u : 0u)) << (2 * c);
+          }
+        }
         uint32_t x[32], y[32];
         float mx = -INFINITY;
         tmem_ld32(s_addr + 96, x);
         tmem_ld32(s_addr + 64, y);
         tmem_wait_ld();
-        chunk_prep(x, mw[3], mx);
-        chunk_prep(y, mw[2], mx);
+        chunk_prep_u(x, mw[3], (cls >> 6) & 3u, mx);
+        chunk_prep_u(y, mw[2], (cls >> 4) & 3u, mx);
         tmem_ld32(s_addr + 32, x);
         tmem_ld32(s_addr + 0, y);
         tmem_wait_ld();
-        chunk_prep(x, mw[1], mx);
-        chunk_prep(y, mw[0], mx);
+        chunk_prep_u(x, mw[1], (cls >> 2) & 3u, mx);
+        chunk_prep_u(y, mw[0], cls & 3u, mx);
         const float m_new = fmaxf(m, mx * sl2);
         bool rescale = false;
         float alpha = 1.f;
@@ -813,9 +831,9 @@ __global__ void __launch_bounds__(320, 1)
         float sum0 = 0.f, sum1 = 0.f;
         {
           uint32_t pk[16];
-          chunk_p(y, mw[0], sl2, mu, sum0, pk);
+          chunk_p_u(y, cls & 3u, sl2, mu, sum0, pk);
           tmem_st16(s_addr + 0, pk);
-          chunk_p(x, mw[1], sl2, mu, sum1, pk);
+          chunk_p_u(x, (cls >> 2) & 3u, sl2, mu, sum1, pk);
           tmem_st16(s_addr + 16, pk);
         }
         tmem_ld32(s_addr + 64, x);
@@ -823,11 +841,11 @@ __global__ void __launch_bounds__(320, 1)
         tmem_wait_ld();
         {
           uint32_t pk[16];
-          if (mw[2] != 0xffffffffu && mw[2]) mask_chunk(x, mw[2]);
-          chunk_p(x, mw[2], sl2, mu, sum0, pk);
+          if (((cls >> 4) & 3u) == 1u) mask_chunk(x, mw[2]);
+          chunk_p_u(x, (cls >> 4) & 3u, sl2, mu, sum0, pk);
           tmem_st16(s_addr + 32, pk);
-          if (mw[3] != 0xffffffffu && mw[3]) mask_chunk(y, mw[3]);
-          chunk_p(y, mw[3], sl2, mu, sum1, pk);
+          if (((cls >> 6) & 3u) == 1u) mask_chunk(y, mw[3]);
+          chunk_p_u(y, (cls >> 6) & 3u, sl2, mu, sum1, pk);
           tmem_st16(s_addr + 48, pk);
         }
         l = l * alpha + (sum0 + sum1);
