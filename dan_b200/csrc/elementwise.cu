@@ -368,17 +368,50 @@ __global__ void kv_store_kernel(const __nv_bfloat16* k, const __nv_bfloat16* v, 
 }
 
 // ---------------------------------------------------------------- label readout
-// One CTA per question: final norm of its read row (the norm is row-wise, so
-// norming only the read rows equals norming all rows then gathering,
-// llama.py:161 + runner.py:73), logits = W_lm[label_ids] @ h in fp32
-// (llama.py:163-165), then the question's softmax (readout.py:13-17).
-__global__ void readout_kernel(const __nv_bfloat16* h, int64_t ldh, const int* read_rows, const __nv_bfloat16* nw,
-                               float eps, int mode, const __nv_bfloat16* wlm, int64_t ldw, int64_t vocab,
-                               const int* label_ids, const int* offsets, int hidden, int max_labels, float* logits,
-                               float* probs, int32_t* status) {
-  extern __shared__ float sh[];  // [hidden] normed row, then [max_labels] logits
+// One thread-block cluster of C CTAs per question (C = 1..8, from the launch's largest label
+// count): every CTA norms the question's read row (the norm is row-wise, so norming only the
+// read rows equals norming all rows then gathering, llama.py:161 + runner.py:73), computes the
+// logits W_lm[label] . h in fp32 (llama.py:163-165) of its contiguous share of the labels (one
+// label row per warp at a time, the whole 8 KB row's loads in flight), and the question's
+// softmax (readout.py:13-17) is combined across the cluster through distributed shared memory:
+// each CTA publishes its (max, sum of exp) and reads its peers'. One CTA per question had left
+// most SMs idle (24-48 questions per batch) and each warp's label rows in flight one 2 KB slice
+// at a time (0.28 / 0.65 TB/s of label bytes on configuration-3 / -5 label counts under ncu).
+constexpr int kReadoutThreads = 512;
+
+__device__ __forceinline__ float dot_row(const __nv_bfloat16* wr, const float* sh, int hidden, int lane) {
+  float acc = 0.f;
+  // 16 x 16 bytes per lane in flight per round: a 4096-wide row in one round.
+  for (int c0 = lane * 8; c0 < hidden; c0 += 16 * 256) {
+    uint4 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      if (c0 + 256 * u < hidden) v[u] = __ldcs(reinterpret_cast<const uint4*>(wr + c0 + 256 * u));
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int c = c0 + 256 * u;
+      if (c >= hidden) break;
+      const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&v[u]);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __bfloat1622float2(e[t]);
+        acc = fmaf(f.x, sh[c + 2 * t], acc);
+        acc = fmaf(f.y, sh[c + 2 * t + 1], acc);
+      }
+    }
+  }
+  return warp_sum(acc);
+}
+
+__global__ void __launch_bounds__(kReadoutThreads) readout_kernel(
+    const __nv_bfloat16* h, int64_t ldh, const int* read_rows, const __nv_bfloat16* nw, float eps, int mode,
+    const __nv_bfloat16* wlm, int64_t ldw, int64_t vocab, const int* label_ids, const int* offsets, int hidden,
+    int max_labels, float* logits, float* probs, int32_t* status) {
+  extern __shared__ float sh[];  // [hidden] normed row, then this CTA's share of the logits
   __shared__ float red[32];
-  const int q = blockIdx.x;
+  __shared__ float stat[2];  // this CTA's (max, sum of exp(logit - max)) for its peers
+  const int q = blockIdx.y;
+  const int crank = static_cast<int>(cluster_rank()), csize = static_cast<int>(gridDim.x);
   const int nwarps = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const __nv_bfloat16* x = h + static_cast<int64_t>(read_rows[q]) * ldh;
   float ss = 0.f;
@@ -407,51 +440,52 @@ __global__ void readout_kernel(const __nv_bfloat16* h, int64_t ldh, const int* r
   __syncthreads();
   const int a = offsets[q];
   int b = offsets[q + 1];
-  if (b < a || b - a > max_labels) {  // the logits slots hold max_labels values: clamp, report
-    if (threadIdx.x == 0) report(status, kBadIndex);
+  if (b < a || b - a > max_labels) {  // the output slots hold max_labels values: clamp, report
+    if (threadIdx.x == 0 && crank == 0) report(status, kBadIndex);
     b = b < a ? a : a + max_labels;
   }
+  const int per = (b - a + csize - 1) / csize;
+  const int lo = min(b, a + crank * per), hi = min(b, lo + per);
   float* lg = sh + hidden;
-  for (int j = a + warp; j < b; j += nwarps) {
+  for (int j = lo + warp; j < hi; j += nwarps) {
     int64_t id = label_ids[j];
     if (id < 0 || id >= vocab) {
       report(status, kBadIndex);
       id = 0;
     }
-    const __nv_bfloat16* wr = wlm + id * ldw;
-    float acc = 0.f;
-    // Four 16-byte loads of the label row in flight per lane before they are used (same
-    // accumulation order per lane as one at a time).
-    for (int c0 = lane * 8; c0 < hidden; c0 += 4 * 256) {
-      uint4 v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (c0 + 256 * u < hidden) v[u] = *reinterpret_cast<const uint4*>(wr + c0 + 256 * u);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = c0 + 256 * u;
-        if (c >= hidden) break;
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[u]);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) acc += __bfloat162float(e[t]) * sh[c + t];
-      }
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) lg[j - a] = acc;
+    const float acc = dot_row(wlm + id * ldw, sh, hidden, lane);
+    if (lane == 0) lg[j - lo] = acc;
   }
   __syncthreads();
   if (warp == 0) {
     float mx = -INFINITY;
-    for (int j = lane; j < b - a; j += 32) mx = fmaxf(mx, lg[j]);
+    for (int j = lane; j < hi - lo; j += 32) mx = fmaxf(mx, lg[j]);
     mx = warp_max(mx);
     float z = 0.f;
-    for (int j = lane; j < b - a; j += 32) z += expf(lg[j] - mx);
+    for (int j = lane; j < hi - lo; j += 32) z += expf(lg[j] - mx);
     z = warp_sum(z);
-    for (int j = lane; j < b - a; j += 32) {
-      logits[a + j] = lg[j];
-      probs[a + j] = expf(lg[j] - mx) / z;
+    if (lane == 0) {
+      stat[0] = mx;
+      stat[1] = z;
     }
   }
+  cluster_sync();  // every CTA's (max, sum) is published
+  if (warp == 0) {
+    float m = -INFINITY, z = 0.f;
+    if (lane < csize) {
+      const uint32_t base = map_shared(smem_u32(stat), static_cast<uint32_t>(lane));
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(m) : "r"(base));
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(z) : "r"(base + 4));
+    }
+    const float big = warp_max(m);
+    float part = (z > 0.f) ? z * expf(m - big) : 0.f;
+    part = warp_sum(part);
+    for (int j = lane; j < hi - lo; j += 32) {
+      logits[lo + j] = lg[j];
+      probs[lo + j] = expf(lg[j] - big) / part;
+    }
+  }
+  cluster_sync();  // peers keep their shared memory until every CTA has read it
 }
 
 }  // namespace ew
@@ -636,16 +670,31 @@ DAN_API int dan_label_readout(const void* h, int64_t ldh, const int* read_rows, 
   DAN_REQUIRE(hidden > 0 && hidden % 8 == 0 && ldw % 8 == 0, "label_readout: hidden/ldw must be multiples of 8");
   DAN_REQUIRE(max_labels >= 0 && max_labels <= 4096, "label_readout: at most 4096 labels per question");
   DAN_REQUIRE(mode >= 0 && mode <= 2, "label_readout: unknown norm mode %d", mode);
+  DAN_REQUIRE(n_questions >= 0 && n_questions < 65536, "label_readout: %d questions", n_questions);
   if (!n_questions) return 0;
-  const size_t smem = (static_cast<size_t>(hidden) + max_labels) * sizeof(float);
+  // Cluster size: about 16 labels per CTA (one per warp), at most the portable 8.
+  int csize = (max_labels + 15) / 16;
+  csize = csize < 1 ? 1 : (csize > 8 ? 8 : csize);
+  const int per = (max_labels + csize - 1) / csize;
+  const size_t smem = (static_cast<size_t>(hidden) + (per > 0 ? per : 1)) * sizeof(float);
   DAN_REQUIRE(smem <= 200 * 1024, "label_readout: hidden %d too large", hidden);
   static std::atomic<uint64_t> configured{0};
   if (smem > 48 * 1024) DAN_CUDA(smem_limit_once(ew::readout_kernel, 200 * 1024, configured));
-  // 16 warps per question: up to 255 labels (configuration 5) are 16 rows per warp, not 32.
-  ew::readout_kernel<<<n_questions, 512, smem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(h), ldh, read_rows, static_cast<const __nv_bfloat16*>(norm_w), eps, mode,
-      static_cast<const __nv_bfloat16*>(w_lm), ldw, vocab, label_ids, offsets, hidden, max_labels, logits, probs,
-      status);
-  DAN_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(csize), static_cast<unsigned>(n_questions), 1);
+  cfg.blockDim = dim3(ew::kReadoutThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DAN_CUDA(cudaLaunchKernelEx(&cfg, ew::readout_kernel, static_cast<const __nv_bfloat16*>(h), ldh, read_rows,
+                              static_cast<const __nv_bfloat16*>(norm_w), eps, mode,
+                              static_cast<const __nv_bfloat16*>(w_lm), ldw, vocab, label_ids, offsets, hidden,
+                              max_labels, logits, probs, status));
   return 0;
 }
