@@ -791,7 +791,11 @@ __global__ void __launch_bounds__(320, 1)
         // masked to -inf per lane, MUFU exponentials); branching on each row's own mask word had
         // serialised up to three paths per chunk within a warp (+1.3% on a configuration-2 batch).
         // Measured and not kept: the whole row in registers with one TMEM round trip (twelve
-        // warps, setmaxnreg moving registers to the softmax warpgroups): no change.
+        // warps, setmaxnreg moving registers to the softmax warpgroups): no change; each row split
+        // over two warps (sixteen softmax warps of 64 key columns, the row max exchanged through
+        // shared memory per block, 96 registers): 12% slower. Skipping the exponentials of half
+        // the columns (a timing probe, wrong results) made the kernel 22% faster: the softmax
+        // warps' instruction stream, not one warp's latency, sets the block period.
         uint32_t cls = 0;  // 2 bits per chunk: 0 none visible, 1 mixed, 2 all visible
         if (full) {
           cls = 0xaau;
