@@ -13,8 +13,9 @@ batch on the device, return a handle whose ``result()`` waits), up to
 next batch while the device computes the current one. A runner with only
 ``read_many`` runs one batch at a time.
 
-Planning (the prompt planner's tokenisation, dan/prompt.py:70-123) runs on a
-pool of ``planner_threads`` threads (default 1) instead of the event loop, so
+Planning (the prompt planner's tokenisation, dan/prompt.py:70-123; with
+``dan_b200.planner.CachedPlanner`` the chat template is rendered once, not per
+prompt) runs on a pool of ``planner_threads`` threads (default 1) instead of the event loop, so
 one request's planning does not hold up the others' routing, batching and
 result delivery; with a thread-safe planner and a tokenizer that releases the
 GIL (Hugging Face fast tokenizers), more threads plan several requests at once.

@@ -3,24 +3,25 @@
     llm = LLM("/models/Llama-3-8B-Instruct", planner=dan.prompt.Planner(tokenizer))
     llm.decide("I was charged twice", {"intent": {"type": "choice", "criteria": {"refund": None, "other": None}}})
 
-The planner (tokenizer-bound prompt planning) is dan's own and outside this
-package; any object with ``plans(state, questions, profile)`` returning read
+The planner (tokenizer-bound prompt planning) is dan's own; by default it runs with the
+template cache of ``dan_b200.planner.CachedPlanner`` (same plans, the chat template rendered
+once instead of per prompt); any object with ``plans(state, questions, profile)`` returning read
 plans works. All reads of all requests run in one packed forward per batch.
 """
 import torch
 
-from . import _dan
 from ._dan import answers, combine
+from .planner import CachedPlanner
 from .runner import Runner
 
 
 class LLM:
     def __init__(self, model, planner=None, device="cuda", dtype=torch.bfloat16, quantization=None,
                  cache_bytes=2 << 30):
-        if planner is None:  # dan installed alongside: build its planner from the model's tokenizer
+        if planner is None:  # dan installed alongside: its planner, with the template cache
             from transformers import AutoTokenizer
 
-            planner = _dan.planner(AutoTokenizer.from_pretrained(model))
+            planner = CachedPlanner(AutoTokenizer.from_pretrained(model))
         self.planner = planner
         self.runner = Runner(model, device, dtype, cache_bytes=cache_bytes, quantization=quantization)
 
