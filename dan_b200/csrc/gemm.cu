@@ -283,6 +283,31 @@ __device__ __forceinline__ void emit(Sink& o, const Params& p, int row, int col,
   }
 }
 
+// Write 32 packed bf16 values (16 pairs) of one row: through the sink, or direct stores.
+__device__ __forceinline__ void emit_packed(Sink& o, const Params& p, int row, int col, int cols_out,
+                                            const uint32_t (&pk)[16]) {
+  if (o.tma) {
+    sink_put(o, col, pk);
+    return;
+  }
+  if (row >= p.m) return;
+  __nv_bfloat16* dst = p.c + static_cast<int64_t>(row) * p.ldc + col;
+  if (col + 32 <= cols_out && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (col + 2 * i < cols_out) dst[2 * i] = __ushort_as_bfloat16(static_cast<unsigned short>(pk[i] & 0xffffu));
+      if (col + 2 * i + 1 < cols_out) dst[2 * i + 1] = __ushort_as_bfloat16(static_cast<unsigned short>(pk[i] >> 16));
+    }
+  }
+}
+
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t x) { return *reinterpret_cast<__nv_bfloat162*>(&x); }
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 x) { return *reinterpret_cast<uint32_t*>(&x); }
+
 __device__ __forceinline__ void sink_load_resid(Sink& o, uint32_t seq, int col) {
   const uint32_t s = seq & 3;
   mbar_expect_tx(&o.bar[s], SLOT_BYTES);
@@ -398,24 +423,29 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
     }
   } else if (p.epilogue == kRope) {
     // q/k heads: rotate-half RoPE on the bf16-rounded projection with the reference's
-    // rounding points, bf16(bf16(a cos) + bf16(-b sin)) (llama.py:43-45); v heads: plain.
-    // A slice holds whole heads (the host keeps width a multiple of the head size).
+    // rounding points, bf16(bf16(a cos) + bf16(-b sin)) (llama.py:43-45), computed on packed
+    // bf16 pairs (a bf16 multiply rounds its exact product once, as the reference's does); v
+    // heads: plain. A slice holds whole heads (the host keeps width a multiple of the head size).
+    // The fp32 form of the same arithmetic (two roundings and four products per element pair in
+    // fp32) had made this epilogue, not the main loop, set the e4m3 q/k/v tile period.
     const int hd = p.rope_hd, half = hd / 2, base = sub * width;
     const int trow = row < p.m ? row : 0;
     // Every head of the tile rotates by the same per-row angles: each 32-column slice of this
-    // row's cos / sin is loaded once and used for all the tile's heads.
+    // row's cos / sin is loaded once, packed into bf16 pairs, and used for all the tile's heads.
     const bool any_rot = tn * BN + base + hd <= p.rope_cols;
 #pragma unroll 1
     for (int c = 0; c < half; c += 32) {
-      float ct[32], st[32];
+      uint32_t cp[16], sp[16];  // cos and sin as bf16 pairs (the tables hold bf16-rounded values)
       if (any_rot) {  // 32 consecutive cos / sin of this row: 8 + 8 16-byte loads
         const float4* c4 = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(trow) * half + c);
         const float4* s4 = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(trow) * half + c);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float4 cv = c4[i], sv = s4[i];
-          ct[4 * i] = cv.x, ct[4 * i + 1] = cv.y, ct[4 * i + 2] = cv.z, ct[4 * i + 3] = cv.w;
-          st[4 * i] = sv.x, st[4 * i + 1] = sv.y, st[4 * i + 2] = sv.z, st[4 * i + 3] = sv.w;
+          cp[2 * i] = pack_bf16(cv.x, cv.y);
+          cp[2 * i + 1] = pack_bf16(cv.z, cv.w);
+          sp[2 * i] = pack_bf16(sv.x, sv.y);
+          sp[2 * i + 1] = pack_bf16(sv.z, sv.w);
         }
       }
 #pragma unroll 1
@@ -426,34 +456,39 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
         tmem_ld32(taddr + h0 + c, ra);
         tmem_ld32(taddr + h0 + half + c, rb);
         tmem_wait_ld();
-        float va[32], vb[32];
         const bool rot = hc + hd <= p.rope_cols;
         const float wa = FP8 ? pick8(ws, (base + h0 + c) >> 5) : 0.f;
         const float wb = FP8 ? pick8(ws, (base + h0 + half + c) >> 5) : 0.f;
+        uint32_t pa[16], pb[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float a = __uint_as_float(ra[i]), b = __uint_as_float(rb[i]);
+        for (int i = 0; i < 16; ++i) {
+          float a0 = __uint_as_float(ra[2 * i]), a1 = __uint_as_float(ra[2 * i + 1]);
+          float b0 = __uint_as_float(rb[2 * i]), b1 = __uint_as_float(rb[2 * i + 1]);
           if (FP8) {  // scales by shuffle from the tile's prefetched scales
-            a *= as * __shfl_sync(0xffffffffu, wa, i);
-            b *= as * __shfl_sync(0xffffffffu, wb, i);
+            a0 *= as * __shfl_sync(0xffffffffu, wa, 2 * i);
+            a1 *= as * __shfl_sync(0xffffffffu, wa, 2 * i + 1);
+            b0 *= as * __shfl_sync(0xffffffffu, wb, 2 * i);
+            b1 *= as * __shfl_sync(0xffffffffu, wb, 2 * i + 1);
           }
           if (p.bias) {
-            a += __bfloat162float(p.bias[hc + c + i]);
-            b += __bfloat162float(p.bias[hc + half + c + i]);
+            a0 += __bfloat162float(p.bias[hc + c + 2 * i]);
+            a1 += __bfloat162float(p.bias[hc + c + 2 * i + 1]);
+            b0 += __bfloat162float(p.bias[hc + half + c + 2 * i]);
+            b1 += __bfloat162float(p.bias[hc + half + c + 2 * i + 1]);
           }
+          const uint32_t a2 = pack_bf16(a0, a1), b2 = pack_bf16(b0, b1);  // the rounded projection
           if (rot) {
-            a = bf16_round(a);
-            b = bf16_round(b);
-            const float cs = ct[i], sn = st[i];
-            va[i] = bf16_round(a * cs) + bf16_round(-b * sn);
-            vb[i] = bf16_round(b * cs) + bf16_round(a * sn);
+            // bf16(a cos) - bf16(b sin) == bf16(a cos) + bf16(-b sin): negation is exact
+            // (the _rn forms: no contraction of a product and a sum into one rounding)
+            pa[i] = as_u32(__hsub2_rn(__hmul2_rn(as_bf2(a2), as_bf2(cp[i])), __hmul2_rn(as_bf2(b2), as_bf2(sp[i]))));
+            pb[i] = as_u32(__hadd2_rn(__hmul2_rn(as_bf2(b2), as_bf2(cp[i])), __hmul2_rn(as_bf2(a2), as_bf2(sp[i]))));
           } else {
-            va[i] = a;
-            vb[i] = b;
+            pa[i] = a2;
+            pb[i] = b2;
           }
         }
-        emit<FP8>(o, p, row, hc + c, cols_out, va);
-        emit<FP8>(o, p, row, hc + half + c, cols_out, vb);
+        emit_packed(o, p, row, hc + c, cols_out, pa);
+        emit_packed(o, p, row, hc + half + c, cols_out, pb);
       }
     }
   } else {
