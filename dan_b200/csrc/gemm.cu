@@ -180,6 +180,9 @@ __device__ __forceinline__ float pick8(const float (&w)[8], int k) {
 
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t x) { return *reinterpret_cast<__nv_bfloat162*>(&x); }
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 x) { return *reinterpret_cast<uint32_t*>(&x); }
+
 template <bool FP8>
 __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, int cols_out, const float* v) {
   // v: 32 consecutive output values of ``row`` starting at ``col``.
@@ -193,12 +196,10 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, i
       uint4 rv[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) rv[i] = reinterpret_cast<const uint4*>(r)[i];
-      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(rv);
+      const uint32_t* r2 = reinterpret_cast<const uint32_t*>(rv);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 rf = __bfloat1622float2(r2[i]);
-        packed[i] = pack_bf16(rf.x + bf16_round(v[2 * i]), rf.y + bf16_round(v[2 * i + 1]));
-      }
+      for (int i = 0; i < 16; ++i)
+        packed[i] = as_u32(__hadd2_rn(as_bf2(r2[i]), as_bf2(pack_bf16(v[2 * i], v[2 * i + 1]))));
     } else {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -305,9 +306,6 @@ __device__ __forceinline__ void emit_packed(Sink& o, const Params& p, int row, i
   }
 }
 
-__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t x) { return *reinterpret_cast<__nv_bfloat162*>(&x); }
-__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 x) { return *reinterpret_cast<uint32_t*>(&x); }
-
 __device__ __forceinline__ void sink_load_resid(Sink& o, uint32_t seq, int col) {
   const uint32_t s = seq & 3;
   mbar_expect_tx(&o.bar[s], SLOT_BYTES);
@@ -355,9 +353,9 @@ __device__ __forceinline__ void residual_tma(Sink& o, const Params& p, uint32_t 
           x0 += col + c < p.n ? __bfloat162float(p.bias[col + c]) : 0.f;
           x1 += col + c + 1 < p.n ? __bfloat162float(p.bias[col + c + 1]) : 0.f;
         }
-        const uint32_t rw = (&q.x)[j];
-        const float2 rf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw));
-        pk[j] = pack_bf16(rf.x + bf16_round(x0), rf.y + bf16_round(x1));
+        // bf16(R + bf16(acc)) as one rounded bf16 add (the sum of two bf16 values rounds the
+        // same whether or not it passes through fp32 first)
+        pk[j] = as_u32(__hadd2_rn(as_bf2((&q.x)[j]), as_bf2(pack_bf16(x0, x1))));
       }
       slot[g] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
