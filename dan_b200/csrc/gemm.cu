@@ -400,24 +400,28 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, Sink& o, uint32_t
       tmem_ld32(taddr + c, g);
       tmem_ld32(taddr + half + c, u);
       tmem_wait_ld();
-      float v[32];
       const int gcol = tn * BN + off + c, ucol = tn * BN + BN / 2 + off + c;
       if (FP8) {
         scale_chunk(p, gcol, as, g);
         scale_chunk(p, ucol, as, u);
       }
+      // The reference's rounding points (fused.py:59-61 on bf16 projections): gate and up
+      // rounded to bf16, silu(gate) rounded to bf16, then one rounded bf16 product.
+      uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+      for (int i = 0; i < 16; ++i) {
+        float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+        float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
         if (p.bias) {
-          gv += gcol + i < p.n ? __bfloat162float(p.bias[gcol + i]) : 0.f;
-          uv += ucol + i < p.n ? __bfloat162float(p.bias[ucol + i]) : 0.f;
+          g0 += gcol + 2 * i < p.n ? __bfloat162float(p.bias[gcol + 2 * i]) : 0.f;
+          g1 += gcol + 2 * i + 1 < p.n ? __bfloat162float(p.bias[gcol + 2 * i + 1]) : 0.f;
+          u0 += ucol + 2 * i < p.n ? __bfloat162float(p.bias[ucol + 2 * i]) : 0.f;
+          u1 += ucol + 2 * i + 1 < p.n ? __bfloat162float(p.bias[ucol + 2 * i + 1]) : 0.f;
         }
-        gv = bf16_round(gv);
-        uv = bf16_round(uv);
-        v[i] = silu(gv) * uv;
+        const uint32_t s2 = pack_bf16(silu(bf16_round(g0)), silu(bf16_round(g1)));
+        pk[i] = as_u32(__hmul2_rn(as_bf2(s2), as_bf2(pack_bf16(u0, u1))));
       }
-      emit<FP8>(o, p, row, tn * (BN / 2) + off + c, cols_out, v);
+      emit_packed(o, p, row, tn * (BN / 2) + off + c, cols_out, pk);
     }
   } else if (p.epilogue == kRope) {
     // q/k heads: rotate-half RoPE on the bf16-rounded projection with the reference's
