@@ -401,29 +401,44 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, 
 // heads that share a KV head (GQA): both heads have the same key blocks and masks, so
 // each K/V tile is loaded once for 2 x 128 query rows. One CTA per SM walks the
 // LPT-ordered items (tile-major, so CTAs running at the same time share K/V in L2) with
-// barrier phases carried across items: the next item's Q, K and V loads and its first
-// QK products overlap the current item's softmax tail and epilogue.
-// The two softmax warpgroups ping-pong with the tensor core:
-//   MMA issue order  QK0(0) QK1(0) PV0(0) | QK0(j) PV1(j-1) QK1(j) PV0(j) | ... PV1(last)
-// A commit arrives only after every earlier MMA of the issuing thread completed, so when
-// a softmax warp sees S_h(j) the product PV_h(j-1) is already in O_h and the lazy O
-// rescale needs no further wait. Each row's visible keys within a block are three
-// intervals (past, trunk, own branch), turned into a 128-bit mask once per block.
-// Warps: 0 TMA, 1 MMA, 2-5 softmax head 2p, 6-9 softmax head 2p+1 (320 threads).
-// TMEM: S_0 [0,128), S_1 [128,256), O_0 [256, 256+D), O_1 [256+D, 256+2D).
+// barrier phases carried across items.
+// Each 128-key block is consumed as two 64-key units, and each head has two 64-column S
+// buffers in TMEM (unit k in buffer k & 1), so the tensor core computes S_h(k + 2) while
+// the softmax warps of head h are still on unit k + 1: a head's softmax never waits for
+// its own PV and QK products. MMA issue order per item of n units:
+//   QK0(0) QK1(0) QK0(1) QK1(1) | PV0(k) QK0(k+2) PV1(k) QK1(k+2) | ... PV0(n-1) PV1(n-1)
+// (the next item's first QK products run while the softmax warps store this item's output).
+// QK_h(k+2) overwrites the buffer that held P_h(k) only after PV_h(k), issued before it
+// by the same thread, has read it (tcgen05 MMAs of one thread run in issue order). A
+// commit arrives only after every earlier MMA of the issuing thread completed, so when a
+// softmax warp sees S_h(k) the product PV_h(k - 2) is in O_h; PV_h(k - 1) may still be
+// running, and the lazy O rescale (rare) waits for it first. Each row's visible keys within a
+// block are three intervals (past, trunk, own branch), turned into a 32-bit mask per thread
+// and unit.
+// Warps: 0 TMA, 1 MMA, 2-9 softmax head 2p, 10-17 softmax head 2p+1 (576 threads), each softmax
+// warp 16 rows with two threads per row (the 16x32bx2 TMEM access shape), so each SM
+// sub-partition holds four softmax warps. The softmax warps are latency-bound rather than
+// issue-bound (issue slots 40% busy with two softmax warps per sub-partition, 56% with four;
+// configuration-2 batch: 128-key units with one thread per row 661, 64-key units 673, two
+// threads per row 766 TFLOP/s). Measured and not kept: bf16 packing of P by integer rounding
+// instead of the conversion instruction (-14%), scalar instead of packed f32x2 arithmetic
+// (-4%), every exponential on the MUFU unit (-3%).
+// TMEM: S_0 [0,64) [64,128), S_1 [128,192) [192,256) (P of a unit over the first 32
+// columns of its buffer), O_0 [256, 256+D), O_1 [256+D, 256+2D).
 template <int D>
 struct PairCfg {
   static constexpr int NS = D <= 64 ? 3 : 2;
   static constexpr int CHUNKS = D / 64;
-  static constexpr int Q_BYTES = CHUNKS * CHUNK;
+  static constexpr int Q_BYTES = CHUNKS * CHUNK;  // one head's 128 query rows
   static constexpr int KV_BYTES = CHUNKS * CHUNK;
-  // Output staging: per softmax warp two 2 KB slots (32 rows x 32 bf16 columns each), written
-  // with the 64-byte swizzle and sent by TMA store.
-  static constexpr int SLOT_BYTES = 32 * 64;
-  static constexpr int SINK_BYTES = 8 * 2 * SLOT_BYTES;
+  // Output staging: per softmax warp two 1 KB slots (16 rows x 32 bf16 columns each, one per
+  // column half), written with the 64-byte swizzle and sent by TMA store.
+  static constexpr int SLOT_BYTES = 16 * 64;
+  static constexpr int SINK_BYTES = 16 * 2 * SLOT_BYTES;
+  // 225.5 KB at D = 128: a second Q buffer (64 KB) does not fit.
   static constexpr int SMEM_USED = 2 * Q_BYTES + 2 * NS * KV_BYTES + SINK_BYTES + 1024 + 512;
   static constexpr int SMEM = SMEM_USED < 120 * 1024 ? 120 * 1024 : SMEM_USED;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 576;
 };
 
 // bits [lo, hi) of a 32-bit word (arguments relative to the word's first column)
@@ -555,8 +570,71 @@ __device__ __forceinline__ void chunk_p_u(const uint32_t (&s)[32], uint32_t cls,
   }
 }
 
+// Shared-memory operand descriptors (128-byte swizzle) as two words: the low word holds the start
+// address and the leading-dimension offset, the high word the 1024-byte stride offset, the
+// sm100 version bit and the swizzle mode. The paired kernel's MMA issuer steps through an
+// operand by adding to the low word only (shared addresses stay below 256 KB, so the 14-bit
+// address field never carries), which keeps its instruction stream short: it shares an SM
+// sub-partition with four busy softmax warps.
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo) {
+  return ((saddr & 0x3FFFFu) >> 4) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+
+__device__ __forceinline__ void mma_ss_w(uint32_t d, uint32_t alo, uint32_t blo, uint32_t hi, uint32_t idesc,
+                                         uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\tsetp.ne.b32 p, %4, 0;\n\tmov.b64 da, {%1, %5};\n\t"
+      "mov.b64 db, {%2, %5};\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}\n" ::"r"(d),
+      "r"(alo), "r"(blo), "r"(idesc), "r"(acc), "r"(hi)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_w(uint32_t d, uint32_t a_tmem, uint32_t blo, uint32_t hi, uint32_t idesc,
+                                         uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\tsetp.ne.b32 p, %4, 0;\n\tmov.b64 db, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}\n" ::"r"(d),
+      "r"(a_tmem), "r"(blo), "r"(idesc), "r"(acc), "r"(hi)
+      : "memory");
+}
+
+// TMEM access of 16 lanes by a whole warp, twice (shape 16x32bx2): threads 0-15 take lanes
+// [base, base + 16) from the address's column on, threads 16-31 the same lanes from column
+// + OFF on; N consecutive 32-bit columns per thread.
+template <int OFF>
+__device__ __forceinline__ void tmem_ld16x2_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], %33;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr), "n"(OFF));
+}
+template <int OFF>
+__device__ __forceinline__ void tmem_st16x2_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], %1, {%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17};" ::
+          "r"(taddr),
+      "n"(OFF), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+template <int OFF>
+__device__ __forceinline__ void tmem_st16x2_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x32.b32 [%0], %1, {%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33};" ::"r"(taddr),
+      "n"(OFF), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(576, 1)
     tree_attention_pair_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                                const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tpk,
                                const __grid_constant__ CUtensorMap tpv, const __grid_constant__ CUtensorMap to,
@@ -565,21 +643,21 @@ __global__ void __launch_bounds__(320, 1)
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem;  // [2][Q_BYTES]
+  uint8_t* sq = smem;  // [2 heads][Q_BYTES]
   uint8_t* sk = sq + 2 * C::Q_BYTES;
   uint8_t* sv = sk + NS * C::KV_BYTES;
-  uint8_t* sink = sv + NS * C::KV_BYTES;  // 1024-byte aligned: Q and K/V stages are multiples of 16 KB
+  uint8_t* sink = sv + NS * C::KV_BYTES;  // 1024-byte aligned: Q and K/V stages are multiples of 8 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sink + C::SINK_BYTES);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + 1;
-  uint64_t* k_full = q_empty + 1;
+  uint64_t* k_full = q_empty + 1;   // [NS]
   uint64_t* v_full = k_full + NS;
   uint64_t* k_empty = v_full + NS;
   uint64_t* v_empty = k_empty + NS;
-  uint64_t* s_full = v_empty + NS;  // [2] per head
-  uint64_t* p_full = s_full + 2;    // [2] per head
-  uint64_t* pv_done = p_full + 2;   // [2] per head
-  uint64_t* o_free = pv_done + 2;   // [2] per head: epilogue finished reading O_h
+  uint64_t* s_full = v_empty + NS;  // [head * 2 + buffer]
+  uint64_t* p_full = s_full + 4;    // [head * 2 + buffer]
+  uint64_t* pv_done = p_full + 4;   // [head * 2 + buffer]
+  uint64_t* o_free = pv_done + 4;   // [head]: the epilogue finished reading O_h
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
 
   const int npairs = p.n_heads / 2;
@@ -596,12 +674,12 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int h = 0; h < 2; ++h) {
-      mbar_init(&s_full[h], 1);
-      mbar_init(&p_full[h], 4);
-      mbar_init(&pv_done[h], 1);
-      mbar_init(&o_free[h], 4);
+    for (int b = 0; b < 4; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 8);
+      mbar_init(&pv_done[b], 1);
     }
+    for (int h = 0; h < 2; ++h) mbar_init(&o_free[h], 8);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -619,12 +697,14 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
       uint32_t gb = 0, it = 0;
-      for (int kw = 0;; ++kw, ++it) {
+      bool ok = true;
+      for (int kw = 0; ok; ++kw) {
         const int w = item_at(p, kw, n_items);
         if (w < 0) break;
         const Tile tile = tiles[w / npairs];
         const int head0 = 2 * (w % npairs), kvh = head0 / rep;
         const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+        if (nblk == 0) continue;
         if (!mbar_wait(q_empty, (it & 1) ^ 1)) {
           report(p.status, kTimeoutEmpty);
           break;
@@ -635,7 +715,6 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int c = 0; c < C::CHUNKS; ++c)
             tma_load_3d(sq + h * C::Q_BYTES + c * CHUNK, &tq, q_full, c * 64, head0 + h, tile.row0);
-        bool ok = true;
         for (int j = 0; j < nblk; ++j, ++gb) {
           const int stage = gb % NS;
           const uint32_t ph = (gb / NS) & 1;
@@ -664,90 +743,105 @@ __global__ void __launch_bounds__(320, 1)
           for (int c = 0; c < C::CHUNKS; ++c)
             tma_load_3d(sv + stage * C::KV_BYTES + c * CHUNK, mv, &v_full[stage], c * 64, kvh, row);
         }
-        if (!ok) break;
+        ++it;
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc_qk = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_qk = idesc_bf16(BM, 64, false, false);
       constexpr uint32_t idesc_pv = idesc_bf16(BM, D, false, true);
-      uint32_t gb = 0, it = 0;
-      bool ok = true;
-      auto qk = [&](int h, uint32_t g, bool last) -> bool {
-        const int st = g % NS;
-        if (h == 0 && !mbar_wait(&k_full[st], (g / NS) & 1)) {
+      const uint32_t hi = kDescHi;
+      // S_h(k) = Q_h K[64 keys]^T into buffer k & 1 of head h; k counts the units of the item
+      // whose first key block is this CTA's block g0.
+      auto qk = [&](int h, uint32_t g0, int k, int nu) -> bool {
+        const uint32_t g = g0 + (k >> 1);
+        const int s = k & 1, st = g % NS;
+        if (h == 0 && s == 0 && !mbar_wait(&k_full[st], (g / NS) & 1)) {
           report(p.status, kTimeoutFull);
           return false;
         }
         tc_fence_after();
-        const uint32_t q0 = smem_u32(sq + h * C::Q_BYTES), k0 = smem_u32(sk + st * C::KV_BYTES);
+        const uint32_t qlo = desc_lo(smem_u32(sq + h * C::Q_BYTES), 16);
+        const uint32_t klo = desc_lo(smem_u32(sk + st * C::KV_BYTES) + s * 64 * 128, 16);  // key rows [64 s, +64)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
-          mma_f16_ss(tmem + h * 128, desc_sw128(q0 + off, 16, 1024), desc_sw128(k0 + off, 16, 1024), idesc_qk,
-                     kk > 0);
+          const uint32_t off = ((kk >> 2) * CHUNK + (kk & 3) * 32) >> 4;
+          mma_ss_w(tmem + h * 128 + s * 64, qlo + off, klo + off, hi, idesc_qk, kk > 0);
         }
-        mma_commit(&s_full[h]);
+        mma_commit(&s_full[h * 2 + s]);
         if (h == 1) {
-          mma_commit(&k_empty[st]);
-          if (last) mma_commit(q_empty);
+          if (s == 1) mma_commit(&k_empty[st]);
+          if (k == nu - 1) mma_commit(q_empty);
         }
         return true;
       };
-      auto pv = [&](int h, uint32_t g, bool first) -> bool {
-        const int st = g % NS;
-        if (first && !mbar_wait(&o_free[h], (it & 1) ^ 1)) {
+      // O_h += P_h(k) V[64 keys], P read from the first 32 columns of the unit's buffer.
+      auto pv = [&](int h, uint32_t g0, int k, uint32_t it) -> bool {
+        const uint32_t g = g0 + (k >> 1);
+        const int s = k & 1, st = g % NS;
+        if (k == 0 && !mbar_wait(&o_free[h], (it & 1) ^ 1)) {
           report(p.status, kTimeoutSoftmax);
           return false;
         }
-        if (!mbar_wait(&p_full[h], g & 1)) {
+        if (!mbar_wait(&p_full[h * 2 + s], g & 1)) {
           report(p.status, kTimeoutSoftmax);
           return false;
         }
-        if (h == 0 && !mbar_wait(&v_full[st], (g / NS) & 1)) {
+        if (h == 0 && s == 0 && !mbar_wait(&v_full[st], (g / NS) & 1)) {
           report(p.status, kTimeoutFull);
           return false;
         }
         tc_fence_after();
-        const uint32_t v0 = smem_u32(sv + st * C::KV_BYTES);
+        const uint32_t vlo = desc_lo(smem_u32(sv + st * C::KV_BYTES) + s * 64 * 128, CHUNK);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          mma_f16_ts(tmem + 256 + h * D, tmem + h * 128 + kk * 8, desc_sw128(v0 + kk * 2048, CHUNK, 1024),
-                     idesc_pv, (!first || kk > 0) ? 1u : 0u);
-        mma_commit(&pv_done[h]);
-        if (h == 1) mma_commit(&v_empty[st]);
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ts_w(tmem + 256 + h * D, tmem + h * 128 + s * 64 + kk * 8, vlo + kk * (2048 >> 4), hi, idesc_pv,
+                   (k > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&pv_done[h * 2 + s]);
+        if (h == 1 && s == 1) mma_commit(&v_empty[st]);
         return true;
       };
-      for (int kw = 0; ok; ++kw, ++it) {
+      uint32_t gb = 0, it = 0;
+      bool ok = true;
+      for (int kw = 0; ok; ++kw) {
         const int w = item_at(p, kw, n_items);
         if (w < 0) break;
         const Tile tile = tiles[w / npairs];
-        const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+        const int nu = 2 * (tile.nblk_a + (tile.blk_b1 - tile.blk_b0));
+        if (nu == 0) continue;
         if (!mbar_wait(q_full, it & 1)) {
           report(p.status, kTimeoutFull);
           break;
         }
-        for (int j = 0; j < nblk; ++j) {
-          const uint32_t g = gb + j;
-          if (!(ok = qk(0, g, false))) break;
-          if (j > 0 && !(ok = pv(1, g - 1, j == 1))) break;
-          if (!(ok = qk(1, g, j == nblk - 1))) break;
-          if (!(ok = pv(0, g, j == 0))) break;
+        ok = qk(0, gb, 0, nu) && qk(1, gb, 0, nu) && qk(0, gb, 1, nu) && qk(1, gb, 1, nu);
+        for (int k = 0; ok && k < nu; ++k) {
+          if (!(ok = pv(0, gb, k, it))) break;
+          if (k + 2 < nu && !(ok = qk(0, gb, k + 2, nu))) break;
+          if (!(ok = pv(1, gb, k, it))) break;
+          if (k + 2 < nu && !(ok = qk(1, gb, k + 2, nu))) break;
         }
-        if (ok && nblk > 0) ok = pv(1, gb + nblk - 1, nblk == 1);
-        gb += nblk;
+        gb += nu / 2;
+        ++it;
       }
     }
   } else {
-    const int hsel = (warp - 2) >> 2;  // 0: head 2p, 1: head 2p+1
-    const int sub = warp & 3;
-    const int r_in = sub * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
+    // Warp w covers 16 rows of its TMEM lane quarter (w % 4) with two threads per row: thread
+    // t < 16 takes row t and the first 32 keys of each unit (the first half of the O columns),
+    // thread t + 16 the same row and the last 32 keys (the second half of O). The two halves of
+    // a row share their maximum by one shuffle.
+    const int sidx = warp - 2;        // 0..15
+    const int hsel = sidx >> 3;       // 0: head 2p, 1: head 2p+1
+    const int sub = warp & 3;         // TMEM lane quarter
+    const int lh = (sidx >> 2) & 1;   // which 16 lanes of the quarter
+    const int half = lane >> 4;       // key half of a unit, column half of O
+    const int r0 = sub * 32 + lh * 16;  // first tile row of this warp
+    const int r_in = r0 + (lane & 15);
+    const uint32_t lane_base = static_cast<uint32_t>(r0) << 16;
     const uint32_t s_addr = tmem + lane_base + hsel * 128;
     const uint32_t o_addr = tmem + lane_base + 256 + hsel * D;
     const float sl2 = p.scale_log2;
-    uint8_t* slots = sink + (warp - 2) * 2 * C::SLOT_BYTES;
-    uint32_t sent = 0;  // output chunks this warp has sent by TMA store (slot = sent & 1)
+    uint8_t* wslots = sink + sidx * 2 * C::SLOT_BYTES;  // per key half: 16 rows x 32 columns
+    uint8_t* slot = wslots + half * C::SLOT_BYTES;
     uint32_t gb = 0;
     bool ok = true;
     for (int kw = 0; ok; ++kw) {
@@ -756,165 +850,137 @@ __global__ void __launch_bounds__(320, 1)
       const Tile tile = tiles[w / npairs];
       const int head = 2 * (w % npairs) + hsel;
       const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+      if (nblk == 0) continue;
       const int row = tile.row0 + r_in;
       const bool valid = r_in < tile.nrows;
       const int qv = tile.q0v + r_in;
       const int own = valid ? tile.ppad + (p.row_own[row] - tile.seg_start) : tile.ppad;
       const int e_past = min(tile.past, qv + 1), e_trunk = min(tile.split, qv + 1);
-      float m = -INFINITY, l = 0.f;  // m in log2 units (scaled)
-      for (int j = 0; j < nblk; ++j) {
+      float m = -INFINITY, l = 0.f;  // m in log2 units (scaled); l over this thread's keys
+      for (int j = 0; j < nblk && ok; ++j) {
         const uint32_t g = gb + j;
         const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
         const int kb = b * BN;
         const bool full = (kb + BN <= tile.past) ||
                           (kb >= tile.ppad && kb + BN <= tile.split && kb + BN - 1 <= tile.q0v);
-        uint32_t mw[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int base = kb + 32 * c;
-          mw[c] = full ? 0xffffffffu
-                       : (span_bits(-base, e_past - base) | span_bits(tile.ppad - base, e_trunk - base) |
-                          span_bits(own - base, qv + 1 - base));
-        }
-        if (!mbar_wait(&s_full[hsel], g & 1)) {
-          report(p.status, kTimeoutMma);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // S is read in 32-column chunks, two loads in flight per wait (tcgen05.wait::ld waits for
-        // every outstanding load): pass 1 takes chunks 3, 2 then 1, 0 for the row max and keeps
-        // chunks 1 and 0; pass 2 writes P0 and P1 from them (P chunk c covers S columns
-        // [16c, 16c + 16), already consumed), then reloads chunks 2 and 3 for P2 and P3.
-        // Each chunk takes one of three warp-uniform paths: no lane sees any of its keys (P = 0),
-        // every lane sees every key (no mask; some exponentials on the FMA pipe), or mixed (scores
-        // masked to -inf per lane, MUFU exponentials); branching on each row's own mask word had
-        // serialised up to three paths per chunk within a warp (+1.3% on a configuration-2 batch).
-        // Measured and not kept: the whole row in registers with one TMEM round trip (twelve
-        // warps, setmaxnreg moving registers to the softmax warpgroups): no change; each row split
-        // over two warps (sixteen softmax warps of 64 key columns, the row max exchanged through
-        // shared memory per block, 96 registers): 12% slower. Skipping the exponentials of half
-        // the columns (a timing probe, wrong results) made the kernel 22% faster: the softmax
-        // warps' instruction stream, not one warp's latency, sets the block period.
-        uint32_t cls = 0;  // 2 bits per chunk: 0 none visible, 1 mixed, 2 all visible
-        if (full) {
-          cls = 0xaau;
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const bool all = __all_sync(0xffffffffu, mw[c] == 0xffffffffu);
-            const bool any = __any_sync(0xffffffffu, mw[c] != 0u);
-            cls |= (all ? 2u : (any ? 1u : 0u)) << (2 * c);
+        for (int s = 0; s < 2; ++s) {
+          // this thread's 32 keys of unit s: block columns [64 s + 32 half, + 32)
+          const int base = kb + 64 * s + 32 * half;
+          const uint32_t mw = full ? 0xffffffffu
+                                   : (span_bits(-base, e_past - base) | span_bits(tile.ppad - base, e_trunk - base) |
+                                      span_bits(own - base, qv + 1 - base));
+          // warp-uniform path over both halves: 0 no key visible, 1 mixed, 2 every key visible
+          const uint32_t cls = full ? 2u
+                                    : (__all_sync(0xffffffffu, mw == 0xffffffffu)
+                                           ? 2u
+                                           : (__any_sync(0xffffffffu, mw != 0u) ? 1u : 0u));
+          const uint32_t sb = s_addr + s * 64;
+          if (!mbar_wait(&s_full[hsel * 2 + s], g & 1)) {
+            report(p.status, kTimeoutMma);
+            ok = false;
+            break;
           }
-        }
-        uint32_t x[32], y[32];
-        float mx = -INFINITY;
-        tmem_ld32(s_addr + 96, x);
-        tmem_ld32(s_addr + 64, y);
-        tmem_wait_ld();
-        chunk_prep_u(x, mw[3], (cls >> 6) & 3u, mx);
-        chunk_prep_u(y, mw[2], (cls >> 4) & 3u, mx);
-        tmem_ld32(s_addr + 32, x);
-        tmem_ld32(s_addr + 0, y);
-        tmem_wait_ld();
-        chunk_prep_u(x, mw[1], (cls >> 2) & 3u, mx);
-        chunk_prep_u(y, mw[0], cls & 3u, mx);
-        const float m_new = fmaxf(m, mx * sl2);
-        bool rescale = false;
-        float alpha = 1.f;
-        if (m_new != -INFINITY) {
-          if (m == -INFINITY) {
-            m = m_new;
-          } else if (m_new > m + 8.f) {
-            alpha = fast_exp2(m - m_new);
-            m = m_new;
-            rescale = true;
+          tc_fence_after();
+          uint32_t x[32];
+          tmem_ld16x2_x32<32>(sb, x);
+          tmem_wait_ld_regs(x);
+          float mx = -INFINITY;
+          chunk_prep_u(x, mw, cls, mx);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float m_new = fmaxf(m, mx * sl2);
+          bool rescale = false;
+          float alpha = 1.f;
+          if (m_new != -INFINITY) {
+            if (m == -INFINITY) {
+              m = m_new;
+            } else if (m_new > m + 8.f) {
+              alpha = fast_exp2(m - m_new);
+              m = m_new;
+              rescale = true;
+            }
           }
-        }
-        const float mu = m == -INFINITY ? 0.f : m;
-        float sum0 = 0.f, sum1 = 0.f;
-        {
-          uint32_t pk[16];
-          chunk_p_u(y, cls & 3u, sl2, mu, sum0, pk);
-          tmem_st16(s_addr + 0, pk);
-          chunk_p_u(x, (cls >> 2) & 3u, sl2, mu, sum1, pk);
-          tmem_st16(s_addr + 16, pk);
-        }
-        tmem_ld32(s_addr + 64, x);
-        tmem_ld32(s_addr + 96, y);
-        tmem_wait_ld();
-        {
-          uint32_t pk[16];
-          if (((cls >> 4) & 3u) == 1u) mask_chunk(x, mw[2]);
-          chunk_p_u(x, (cls >> 4) & 3u, sl2, mu, sum0, pk);
-          tmem_st16(s_addr + 32, pk);
-          if (((cls >> 6) & 3u) == 1u) mask_chunk(y, mw[3]);
-          chunk_p_u(y, (cls >> 6) & 3u, sl2, mu, sum1, pk);
-          tmem_st16(s_addr + 48, pk);
-        }
-        l = l * alpha + (sum0 + sum1);
-        if (__any_sync(0xffffffffu, rescale)) {
+          const float mu = m == -INFINITY ? 0.f : m;
+          float sum = 0.f;
+          {
+            uint32_t pk[16];
+            chunk_p_u(x, cls, sl2, mu, sum, pk);
+            tmem_st16x2_x16<16>(sb, pk);  // P keys [0, 32) -> columns [0, 16), keys [32, 64) -> [16, 32)
+          }
+          l = l * alpha + sum;
+          if (__any_sync(0xffffffffu, rescale)) {
+            // O_h must hold the previous unit's product before it is scaled: PV_h of the
+            // previous unit may still be running (the one before it has completed).
+            const bool waited = s == 1 ? mbar_wait(&pv_done[hsel * 2], g & 1)
+                                       : mbar_wait(&pv_done[hsel * 2 + 1], (g - 1) & 1);
+            if (!waited) {
+              report(p.status, kTimeoutMma);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(o_addr + c, o);
-            tmem_wait_ld();
+            for (int c = 0; c < D / 2; c += 32) {
+              uint32_t o[32];
+              tmem_ld16x2_x32<D / 2>(o_addr + c, o);
+              tmem_wait_ld_regs(o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(o_addr + c, o);
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st16x2_x32<D / 2>(o_addr + c, o);
+            }
           }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[hsel * 2 + s]);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[hsel]);
       }
       if (!ok) break;
-      if (nblk > 0) {
-        const uint32_t last = gb + nblk - 1;
-        if (!mbar_wait(&pv_done[hsel], last & 1)) {
-          report(p.status, kTimeoutMma);
-          break;
-        }
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        // A warp whose 32 rows all belong to the tile sends each 32-column chunk through a
-        // shared-memory slot by TMA store (whole lines, no per-row stores); the warp holding a
-        // segment's ragged last rows stores its valid rows directly.
-        const bool slab = (sub + 1) * 32 <= tile.nrows;
-        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
+      const uint32_t last = gb + nblk - 1;
+      if (!mbar_wait(&pv_done[hsel * 2 + 1], last & 1)) {
+        report(p.status, kTimeoutMma);
+        break;
+      }
+      tc_fence_after();
+      const float lt = l + __shfl_xor_sync(0xffffffffu, l, 16);
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      // A warp whose 16 rows all belong to the tile sends each 16 x 32 piece through its
+      // shared-memory slot by TMA store (whole lines, no per-row stores); the warp holding a
+      // segment's ragged last rows stores its valid rows directly.
+      const bool slab = r0 + 16 <= tile.nrows;
+      __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c, o);
-          tmem_wait_ld();
-          uint32_t pkd[16];
+      for (int c = 0; c < D / 2; c += 32) {
+        uint32_t o[32];
+        tmem_ld16x2_x32<D / 2>(o_addr + c, o);
+        tmem_wait_ld_regs(o);
+        uint32_t pkd[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-          if (slab) {
-            uint8_t* slot = slots + (sent & 1) * C::SLOT_BYTES;
-            if (lane == 0) bulk_wait_read<1>();  // the store sent from this slot two chunks ago has read it
-            __syncwarp();
-            // 64-byte swizzle: 16-byte unit u of row r sits at unit u ^ ((r >> 1) & 3)
-            uint4* d4 = reinterpret_cast<uint4*>(slot + lane * 64);
-            const int sw = (lane >> 1) & 3;
+        for (int i = 0; i < 16; ++i)
+          pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+        const int col = half * (D / 2) + c;
+        if (slab) {
+          if (lane == 0) bulk_wait_read<0>();  // the previous stores from these slots have read them
+          __syncwarp();
+          // 64-byte swizzle: 16-byte unit u of row r sits at unit u ^ ((r >> 1) & 3)
+          const int r = lane & 15;
+          uint4* d4 = reinterpret_cast<uint4*>(slot + r * 64);
+          const int sw = (r >> 1) & 3;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i ^ sw] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_3d(&to, slot, c, head, tile.row0 + sub * 32);
-              bulk_commit();
-            }
-            __syncwarp();
-            ++sent;
-          } else if (valid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+          for (int i = 0; i < 4; ++i)
+            d4[i ^ sw] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&to, wslots, c, head, tile.row0 + r0);
+            tma_store_3d(&to, wslots + C::SLOT_BYTES, D / 2 + c, head, tile.row0 + r0);
+            bulk_commit();
           }
+          __syncwarp();
+        } else if (valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + col);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
         }
       }
       tc_fence_before();
@@ -954,12 +1020,13 @@ static int rows_map(CUtensorMap* m, const void* base, int64_t row_stride, int64_
   return make_tmap(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// Output of the paired-head kernel: 32 columns x 1 head x 32 rows per store, 64-byte swizzle.
+// Output tiles: 32 columns x 1 head x ``box_rows`` rows per store (32 for the single-head kernel,
+// 16 for the paired one), 64-byte swizzle.
 static int out_map(CUtensorMap* m, const void* base, int64_t row_stride, int64_t head_stride, int heads, int rows,
-                   int d) {
+                   int d, int box_rows) {
   uint64_t dims[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(heads), static_cast<uint64_t>(rows)};
   uint64_t strides[2] = {static_cast<uint64_t>(head_stride) * 2, static_cast<uint64_t>(row_stride) * 2};
-  uint32_t box[3] = {32, 1, 32};
+  uint32_t box[3] = {32, 1, static_cast<uint32_t>(box_rows)};
   return make_tmap(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
@@ -1013,7 +1080,7 @@ DAN_API int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, con
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool paired = (n_heads / n_kv_heads) % 2 == 0 && head_dim <= 128;
   CUtensorMap to;
-  if ((rc = attn::out_map(&to, out, out_row, out_head, n_heads, n_rows, head_dim))) return rc;
+  if ((rc = attn::out_map(&to, out, out_row, out_head, n_heads, n_rows, head_dim, paired ? 16 : 32))) return rc;
   if (paired)
     return head_dim == 64 ? attn::launch_pair<64>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s)
                           : attn::launch_pair<128>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s);
