@@ -501,9 +501,13 @@ __device__ __forceinline__ void exp2_pair_fma(uint64_t x2, float& ra, float& rb)
   rb = __int_as_float(__float_as_int(qb) + (__float_as_int(tb) << 23));
 }
 
-// One score pair in EXP_EMU_EVERY of a fully visible chunk takes exp2_pair_fma (measured on
-// configuration-2 batches: none 535, 1 in 4 551, 1 in 3 547, 1 in 2 532 TFLOP/s).
-constexpr int EXP_EMU_EVERY = 4;
+// One score pair in EXP_EMU_EVERY of a fully visible chunk takes exp2_pair_fma. With four
+// softmax warps per SM sub-partition the MUFU unit is rarely the limit and the emulation's
+// extra instructions cost more than they free (configuration-2 batch, TFLOP/s: 1 in 2 730,
+// 1 in 4 775, 1 in 8 783, 1 in 16 792, none 782-790; with one softmax thread per row it had
+// been none 535, 1 in 4 551, 1 in 2 532). Writing an item's output after the next item's
+// first unit instead of before it measured 1% slower.
+constexpr int EXP_EMU_EVERY = 16;
 
 // Masked scores become -inf in place (partially visible chunks then take the packed path:
 // exp2(-inf) = 0 and -inf never wins a max).
