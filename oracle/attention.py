@@ -37,11 +37,14 @@ def segment_mask(branch_ids, past_len):
     return m
 
 
-def attend(q, k, v, segments, scale=None):
+def attend(q, k, v, segments, scale=None, p_bf16=False):
     """q: [H, N, D]; k, v: [Hkv, N, D] -> [H, N, D] (fp32).
 
     ``segments``: list of dicts ``{"start", "end", "branch": [ids per new token],
-    "past": None or (pk, pv) each [Hkv, past, D]}``."""
+    "past": None or (pk, pv) each [Hkv, past, D]}``. ``p_bf16``: the unnormalised
+    probabilities exp(s - rowmax) rounded to bf16 before they multiply V (normalised by their
+    unrounded sum), as a tensor-core attention kernel feeds them to its PV product; used to
+    measure how far that rounding alone moves a model's answers."""
     h, n, d = q.shape
     rep = h // k.shape[0]
     scale = d ** -0.5 if scale is None else scale
@@ -59,7 +62,11 @@ def attend(q, k, v, segments, scale=None):
         vs = vs.repeat_interleave(rep, 0)
         sc = (q[:, a:b].double() @ ks.transpose(1, 2)) * scale
         sc = sc.masked_fill(~mask[None], float("-inf"))
-        out[:, a:b] = (torch.softmax(sc, -1) @ vs).float()
+        if p_bf16:
+            e = torch.exp(sc - sc.amax(-1, keepdim=True))
+            out[:, a:b] = ((e.float().bfloat16().double() @ vs) / e.sum(-1, keepdim=True)).float()
+        else:
+            out[:, a:b] = (torch.softmax(sc, -1) @ vs).float()
     return out
 
 

@@ -107,7 +107,7 @@ def rotate_rounded(x, cos, sin, bf16):
     return rd(rd(x * cos) + rd(torch.cat((-b, a), dim=-1) * sin))
 
 
-def hidden(state, config, ids, positions, segments, fp8=False, bf16=False):
+def hidden(state, config, ids, positions, segments, fp8=False, bf16=False, p_bf16=False):
     """Final-normed hidden states [N, hidden] of a packed batch.
 
     ``segments``: list of dicts ``{"start", "end", "branch", "past": {layer: (k, v)} or None,
@@ -117,7 +117,9 @@ def hidden(state, config, ids, positions, segments, fp8=False, bf16=False):
     ``bf16``: the reference's bf16 path (``Runner(dtype=torch.bfloat16)``, the dtype its GPU
     path and its FP8 linears run in): weights, cos / sin and every activation rounded to bf16
     where the reference's modules return them (embedding, norms, each linear, RoPE products and
-    sums, attention output, SiLU and its product, residual sums); matmuls accumulate in fp32."""
+    sums, attention output, SiLU and its product, residual sums); matmuls accumulate in fp32.
+    ``p_bf16``: attention probabilities rounded to bf16 before the PV product
+    (``attention.attend``)."""
     c = config
     eps = c["rms_norm_eps"]
     rd = rounding(bf16)
@@ -149,7 +151,7 @@ def hidden(state, config, ids, positions, segments, fp8=False, bf16=False):
                 a = s["start"]
                 s["saved"][i] = (k[:, a:a + s["save"]].clone(), v[:, a:a + s["save"]].clone())
             segs.append({"start": s["start"], "end": s["end"], "branch": s["branch"], "past": past})
-        o = rd(attention.attend(q, k, v, segs))
+        o = rd(attention.attend(q, k, v, segs, p_bf16=p_bf16))
         o = o.transpose(0, 1).reshape(n, nh * d)
         x = rd(x + _linear(state, p + "self_attn.o_proj.weight", o, fp8, bf16))
         h = norm(x, state[p + "post_attention_layernorm.weight"], eps, bf16)

@@ -91,10 +91,11 @@ def pack(plans, cache=None, use_cache=True):
     return ids, pos, segs, reads, stores
 
 
-def read_many(state, config, plans, cache=None, fp8=False, bf16=False):
+def read_many(state, config, plans, cache=None, fp8=False, bf16=False, p_bf16=False):
     """Per plan, per branch: fp32 label logits (runner.py:66-82); ``fp8``: decoder linears
     through the FP8 restatement (Llama family only); ``bf16``: the reference's bf16 path
-    (``Runner(dtype=torch.bfloat16)``, the dtype of its GPU and FP8 paths)."""
+    (``Runner(dtype=torch.bfloat16)``, the dtype of its GPU and FP8 paths); ``p_bf16``:
+    attention probabilities rounded to bf16 before the PV product (Llama family only)."""
     arch = qwen3_5 if config["model_type"].startswith("qwen3_5") else llama
     ids, pos, segs, reads, stores = pack(plans, cache)
     flat = []
@@ -102,6 +103,8 @@ def read_many(state, config, plans, cache=None, fp8=False, bf16=False):
         kw = {"bf16": True} if bf16 else {}
         if fp8:
             kw["fp8"] = True
+        if p_bf16:
+            kw["p_bf16"] = True
         h = arch.hidden(state, config, ids, pos, segs, **kw)
         flat = [arch.label_logits(state, h[r], labels, bf16=bf16) for r, labels in reads]
         for static, seg in stores:

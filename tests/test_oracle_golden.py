@@ -39,6 +39,23 @@ def test_attention_edges_golden():
     torch.testing.assert_close(out, g["out"], atol=2e-5, rtol=1e-5)
 
 
+def test_attention_bf16_probabilities_within_rounding():
+    """``p_bf16`` (probabilities rounded to bf16 before the PV product) moves each output by at
+    most bf16 rounding of the weights: relative 2^-8 of sum |p v|."""
+    from make_golden import attention_inputs
+
+    g = golden("attention_edges.pt")
+    q, k, v, pasts = attention_inputs(g["h"], g["hkv"], g["d"], g["seed"], g["shapes"])
+    segs, start = [], 0
+    for (trunk, lens, past), pkv in zip(g["shapes"], pasts):
+        branch = [0] * trunk + [j for j, n in enumerate(lens, 1) for _ in range(n)]
+        segs.append({"start": start, "end": start + len(branch), "branch": branch, "past": pkv})
+        start += len(branch)
+    exact, rounded = OA.attend(q, k, v, segs), OA.attend(q, k, v, segs, p_bf16=True)
+    bound = 2.0 ** -8 * v.abs().max().item()
+    assert 0 < (exact - rounded).abs().max().item() <= bound
+
+
 def test_pack_golden():
     cache = OR.PrefixCache(1 << 30)
     for rec in golden("pack.json"):
