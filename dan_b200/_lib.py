@@ -119,7 +119,10 @@ def status_word(device):
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     s = _status.get(idx)
     if s is None:
-        s = _status[idx] = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+        # a normal tensor even when the first caller runs under torch.inference_mode (as
+        # Runner.read_many does): check_status clears it in place from any mode
+        with torch.inference_mode(False):
+            s = _status[idx] = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
     return s
 
 

@@ -191,14 +191,15 @@ constexpr int LDF = CH + 1;  // fp32 row stride of 64 x 64 tiles
 constexpr int LDT = CH + 4;  // fp32 row stride of T: 16-byte rows for the merges' vector loads
 constexpr int LDY = 36;      // fp32 row stride of the merges' 32-wide scratch
 
-// Scratch records, rows padded exactly as in shared memory so a chunk loads with a few bulk
-// copies: per (chunk, value head) -W [64][LDW], T'V as two 64-column halves [64][LDN], P
-// [64][LDN] (bf16) and γ_t, e^{Γ_C-Γ_t}, e^{Γ_C} (fp32 x 64 each); per (chunk, key head) q̂ and
-// k̂ [64][LDW] bf16.
-constexpr int64_t TILE_W = CH * LDW * 2, TILE_N = CH * LDN * 2;  // 17408, 9216 B
-constexpr int64_t REC_W = 0, REC_UT = TILE_W, REC_P = REC_UT + 2 * TILE_N, REC_SC = REC_P + TILE_N;
-constexpr int64_t REC_V = REC_SC + 3 * CH * 4;  // 45824 B
-constexpr int64_t REC_K = 2 * TILE_W;           // 34816 B
+// Scratch records, laid out exactly as the chain kernel's shared memory so a chunk loads with
+// a few bulk copies: per (chunk, value head) -W and diag(γ) q̂ [64 rows t][128] and P [64][64]
+// in the 128-byte swizzled row layout of tcgen05 operands (64-column chunks of 8 KB), T'V
+// [64][LDW] bf16, and γ_t, e^{Γ_C-Γ_t}, e^{Γ_C} (fp32 x 64 each); per (chunk, key head) k̂
+// [64 rows][128], swizzled the same way.
+constexpr int64_t REC_W = 0, REC_QG = 16384, REC_P = 32768, REC_TV = 40960;
+constexpr int64_t REC_SC = REC_TV + CH * LDW * 2;  // 58368
+constexpr int64_t REC_V = REC_SC + 3 * CH * 4;     // 59136 B
+constexpr int64_t REC_K = 16384;
 
 __device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -248,10 +249,15 @@ struct PrepSmem {
   float gam[CH], eg[CH], beta[CH], graw[CH];
 };
 
-// Copy ``bytes`` of shared memory (a padded tile) to global memory, 16 bytes per thread step.
-__device__ __forceinline__ void copy_out(uint8_t* dst, const void* src, int bytes) {
-  for (int e = threadIdx.x; e < bytes / 16; e += blockDim.x)
-    reinterpret_cast<uint4*>(dst)[e] = reinterpret_cast<const uint4*>(src)[e];
+// A padded [64 rows][ld] bf16 tile of shared memory (``chunks`` x 64 columns) to global memory
+// in the 128-byte swizzled row layout (per 64-column chunk, row r's 16-byte unit u at
+// r * 128 + ((u ^ (r & 7)) * 16)).
+__device__ __forceinline__ void copy_out_sw128(uint8_t* dst, const __nv_bfloat16* src, int ld, int chunks) {
+  for (int e = threadIdx.x; e < CH * 8 * chunks; e += blockDim.x) {
+    const int r = e / (8 * chunks), j = e % (8 * chunks), ch = j >> 3, u = j & 7;
+    *reinterpret_cast<uint4*>(dst + ch * 8192 + r * 128 + ((u ^ (r & 7)) << 4)) =
+        *reinterpret_cast<const uint4*>(src + r * ld + 8 * j);
+  }
 }
 
 __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
@@ -332,10 +338,7 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
   }
   for (int i = tid; i < CH * LDT; i += blockDim.x) sm.tf[i] = 0.f;
   __syncthreads();
-  if (owner) {
-    copy_out(rk, sm.qn, TILE_W);
-    copy_out(rk + TILE_W, sm.kn, TILE_W);
-  }
+  if (owner) copy_out_sw128(rk, sm.kn, LDW, 2);
   if (warp == 0) {  // Γ: inclusive prefix sum of the log decays
     const float v0 = sm.graw[2 * lane], v1 = sm.graw[2 * lane + 1];
     float incl = v0 + v1;
@@ -358,6 +361,20 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
       sc[CH + tid] = __expf(gc - sm.gam[tid]);
       sc[2 * CH + tid] = __expf(gc);
     }
+  }
+  for (int e = tid; e < CH * 16; e += blockDim.x) {  // diag(γ) q̂, swizzled rows
+    const int r = e >> 4, j = e & 15, ch = j >> 3, u = j & 7;
+    const uint4 qv = *reinterpret_cast<const uint4*>(&sm.qn[r * LDW + 8 * j]);
+    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+    const float gr = sm.eg[r];
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[i]));
+      o[i] = pack_bf16(f.x * gr, f.y * gr);
+    }
+    *reinterpret_cast<uint4*>(rv + REC_QG + ch * 8192 + r * 128 + ((u ^ (r & 7)) << 4)) =
+        make_uint4(o[0], o[1], o[2], o[3]);
   }
   // ---- K K^T -> A and Q K^T -> P (warp: rows [16 tm, +16), columns [32 sh, +32))
   {
@@ -402,7 +419,7 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
     }
   }
   __syncthreads();
-  copy_out(rv + REC_P, sm.pb, TILE_N);
+  copy_out_sw128(rv + REC_P, sm.pb, LDN, 1);
   // ---- T = (I + A)^-1: diagonal 16 x 16 blocks by forward substitution (thread: one column)
   if (tid < 64) {
     const int d = tid >> 4, j = tid & 15;
@@ -506,244 +523,366 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
     st_bf2(&sm.qn[(t + 8) * LDW + col], -aw[j][2], -aw[j][3]);
   }
   __syncthreads();
-  copy_out(rv + REC_W, sm.qn, TILE_W);
-  for (int e = tid; e < CH * 16; e += blockDim.x) {  // T'V as two 64-column halves [64][LDN]
-    const int t = e >> 4, c8 = (e & 15) * 8, hf = c8 >> 6;
-    *reinterpret_cast<uint4*>(rv + REC_UT + hf * TILE_N + (t * LDN + (c8 & 63)) * 2) =
-        *reinterpret_cast<const uint4*>(&sm.v[t * LDW + c8]);
-  }
+  copy_out_sw128(rv + REC_W, sm.qn, LDW, 2);
+  for (int e = tid; e < CH * LDW / 8; e += blockDim.x)  // T'V [64][LDW]
+    reinterpret_cast<uint4*>(rv + REC_TV)[e] = reinterpret_cast<const uint4*>(sm.v)[e];
 }
 
-struct StateBuf {  // one chunk's inputs for one 64-column half of the state
-  __nv_bfloat16 w[CH * LDW];   // -W
-  __nv_bfloat16 qn[CH * LDW];  // q̂
-  __nv_bfloat16 kn[CH * LDW];  // k̂
-  __nv_bfloat16 ut[CH * LDN];  // T'V, this half's columns
-  __nv_bfloat16 p[CH * LDN];   // P
+// ---------------------------------------------------------------------------------
+// The chain on the tensor cores (tcgen05, accumulators in TMEM): one CTA per (value head,
+// segment) walks the segment's chunks in order. The state is held transposed, S^T [value
+// column c = TMEM lane][key k] in fp32, so every product of a chunk is an M = 128 MMA over
+// the head's 128 value columns with the A operand in TMEM:
+//   U^T  = S0^T (-W)^T             A = S0^T (bf16), B = -W           (rows t, K = k)
+//   U    = T'V + U^T^T             warps: bf16 U^T and Us^T = U^T diag(e^{Γ_C-Γ_t})
+//   S^T  = γ_C S0^T + Us^T K       warps scale S^T first; B = K as an MN-major operand
+//   O^T  = S0^T (diag(γ) Q)^T + U^T P^T
+// TMEM columns: S^T [0,128), the trunk's final state F [128,256), U^T fp32 [256,320), O^T
+// [320,384), S0^T bf16 [384,448), U^T bf16 [448,480), Us^T bf16 [480,512).
+// Warps 0-3 (thread = value column = TMEM lane) convert between the products and stage O; warp
+// 4 issues the bulk copies (three chunks in flight), the MMAs and O's TMA stores. Per chunk:
+//   warps: S^T -> S0^T bf16 and S^T *= γ_C (after the previous chunk's S product); read the
+//          previous chunk's O^T
+//   MMA:   U^T
+//   warps: U^T + T'V -> U^T, Us^T bf16; stage the previous O, transposed, in its chunk buffer
+//   MMA:   S^T += Us^T K, then O^T; TMA store of the previous O, then the next bulk copies
+// The products take ~900 tensor-core cycles per chunk; the TMEM round trips of the two
+// conversions (load, wait, convert, store, wait) set the period (~3.7k cycles on a
+// configuration-4 batch; eight conversion warps with half the work each measured no faster).
+// The chain this replaces (mma.sync, which runs at a quarter of tcgen05's rate on B200: 2048 vs
+// 8192 bf16 FLOP per clock and SM, with 128 x 64 of the state per CTA in registers) took 161 us
+// on that batch, this one 152 us.
+struct ChainBuf {               // one chunk's inputs; MMA operands 1024-byte aligned
+  __nv_bfloat16 w[CH * DK];     // -W, rows t, 128-byte swizzle (two 64-column chunks)
+  __nv_bfloat16 qg[CH * DK];    // diag(γ) q̂, same layout
+  __nv_bfloat16 kn[CH * DK];    // k̂, same layout
+  __nv_bfloat16 p[CH * CH];     // P, rows t, 128-byte swizzle
+  __nv_bfloat16 tv[CH * LDW];   // T'V, row-major with padded rows
   float eg[CH], ws[CH], ec[CH];
+  uint8_t pad[256];
 };
-struct StateSmem {
-  StateBuf buf[2];
-  __nv_bfloat16 s0[DK * LDN];  // chunk-start state slice, bf16
-  __nv_bfloat16 u[CH * LDN];
-  __nv_bfloat16 us[CH * LDN];  // e^{Γ_C-Γ_t} U
-  uint64_t full[2];            // per buffer: the chunk's bulk copies landed
+static_assert(sizeof(ChainBuf) % 1024 == 0, "chunk buffers keep 1024-byte alignment");
+struct ChainSmem {
+  ChainBuf buf[3];
+  uint64_t full[3];  // per buffer: the chunk's bulk copies landed
+  uint64_t mma_u, mma_s, mma_o, conv_s, conv_u;
+  uint64_t staged;   // the previous chunk's O left its buffer (staged there for coalesced stores)
+  uint32_t tmem_slot;
 };
+constexpr uint32_t CHAIN_TX = 3 * 16384 + 8192 + CH * LDW * 2 + 3 * CH * 4;
+constexpr int CHAIN_SMEM = static_cast<int>(sizeof(ChainSmem)) + 1024;  // + alignment of the base
+static_assert(CHAIN_SMEM <= 232448, "the chain kernel's shared memory exceeds 227 KB");
 
-// One thread: the chunk's six bulk copies into ``b``, completing on ``bar``.
-__device__ __forceinline__ void load_chunk(const ScanParams& p, StateBuf& b, uint64_t* bar, int ci, int h, int kh,
-                                           int half) {
-  const uint8_t* rv = p.scratch + (static_cast<int64_t>(ci) * p.hv + h) * REC_V;
-  const uint8_t* rk =
-      p.scratch + static_cast<int64_t>(p.n_chunks) * p.hv * REC_V + (static_cast<int64_t>(ci) * p.hk + kh) * REC_K;
-  fence_proxy_async();  // this buffer's previous reads (generic proxy) before the async writes
-  mbar_expect_tx(bar, static_cast<uint32_t>(sizeof(StateBuf)));
-  bulk_load(b.w, rv + REC_W, TILE_W, bar);
-  bulk_load(b.qn, rk, TILE_W, bar);
-  bulk_load(b.kn, rk + TILE_W, TILE_W, bar);
-  bulk_load(b.ut, rv + REC_UT + half * TILE_N, TILE_N, bar);
-  bulk_load(b.p, rv + REC_P, TILE_N, bar);
-  bulk_load(b.eg, rv + REC_SC, 3 * CH * 4, bar);
-}
+enum StateSrc { kSrcZero = 0, kSrcPool = 1, kSrcTmemS = 2, kSrcTmemF = 3 };
 
-__device__ __forceinline__ void state_io(float (&S)[8][4], float* st, bool load) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float* r0 = st + (16 * warp + g) * DK + 8 * j + 2 * c;
-    float* r1 = r0 + 8 * DK;
-    if (load) {
-      const float2 x = *reinterpret_cast<const float2*>(r0), y = *reinterpret_cast<const float2*>(r1);
-      S[j][0] = x.x, S[j][1] = x.y, S[j][2] = y.x, S[j][3] = y.y;
-    } else {
-      *reinterpret_cast<float2*>(r0) = make_float2(S[j][0], S[j][1]);
-      *reinterpret_cast<float2*>(r1) = make_float2(S[j][2], S[j][3]);
-    }
-  }
-}
-
-// The state-dependent part of one chunk: U = T'V - W S0, O = diag(γ) Q S0 + P U (to ``out``),
-// S = γ_C S0 + K^T diag(e^{Γ_C-Γ_t}) U, for this CTA's 64 value columns.
-__device__ __forceinline__ void state_chunk(const ScanParams& p, StateSmem& sm, const StateBuf& b, float (&S)[8][4],
-                                            int h, int half, int row0, int nt) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const int tm = warp & 3, tn = warp >> 2;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    st_bf2(&sm.s0[(16 * warp + g) * LDN + 8 * j + 2 * c], S[j][0], S[j][1]);
-    st_bf2(&sm.s0[(16 * warp + g + 8) * LDN + 8 * j + 2 * c], S[j][2], S[j][3]);
-  }
-  __syncthreads();
-  const int t = 16 * tm + g;
-  float acc[4][4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {  // U starts from T'V
-    const int col = 32 * tn + 8 * j + 2 * c;
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.ut[t * LDN + col]));
-    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b.ut[(t + 8) * LDN + col]));
-    acc[j][0] = x.x, acc[j][1] = x.y, acc[j][2] = y.x, acc[j][3] = y.y;
-  }
-  float acc2[4][4] = {};  // odd K steps: two independent accumulation chains per tile
-#pragma unroll
-  for (int kk = 0; kk < DK / 16; ++kk) {
-    float(&d)[4][4] = (kk & 1) ? acc2 : acc;
-    uint32_t a[4];
-    ldsm4(a, a_rows(b.w, LDW, 16 * tm, 16 * kk, lane));
-#pragma unroll
-    for (int np = 0; np < 2; ++np) {
-      uint32_t bb[4];
-      ldsm4t(bb, b_krows(sm.s0, LDN, 16 * kk, 32 * tn + 16 * np, lane));
-      mma16816(d[2 * np], a, bb[0], bb[1]);
-      mma16816(d[2 * np + 1], a, bb[2], bb[3]);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      acc[j][e] += acc2[j][e];
-      acc2[j][e] = 0.f;
-    }
-  {
-    const float w0 = b.ws[t], w1 = b.ws[t + 8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = 32 * tn + 8 * j + 2 * c;
-      st_bf2(&sm.u[t * LDN + col], acc[j][0], acc[j][1]);
-      st_bf2(&sm.u[(t + 8) * LDN + col], acc[j][2], acc[j][3]);
-      st_bf2(&sm.us[t * LDN + col], acc[j][0] * w0, acc[j][1] * w0);
-      st_bf2(&sm.us[(t + 8) * LDN + col], acc[j][2] * w1, acc[j][3] * w1);
-      acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int kk = 0; kk < DK / 16; ++kk) {  // Q S0
-    float(&d)[4][4] = (kk & 1) ? acc2 : acc;
-    uint32_t a[4];
-    ldsm4(a, a_rows(b.qn, LDW, 16 * tm, 16 * kk, lane));
-#pragma unroll
-    for (int np = 0; np < 2; ++np) {
-      uint32_t bb[4];
-      ldsm4t(bb, b_krows(sm.s0, LDN, 16 * kk, 32 * tn + 16 * np, lane));
-      mma16816(d[2 * np], a, bb[0], bb[1]);
-      mma16816(d[2 * np + 1], a, bb[2], bb[3]);
-    }
-  }
-  {
-    const float e0 = b.eg[t], e1 = b.eg[t + 8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      acc[j][0] = (acc[j][0] + acc2[j][0]) * e0;
-      acc[j][1] = (acc[j][1] + acc2[j][1]) * e0;
-      acc[j][2] = (acc[j][2] + acc2[j][2]) * e1;
-      acc[j][3] = (acc[j][3] + acc2[j][3]) * e1;
-    }
-  }
-#pragma unroll
-  for (int kk = 0; kk < CH / 16; ++kk) {  // + P U
-    uint32_t a[4];
-    ldsm4(a, a_rows(b.p, LDN, 16 * tm, 16 * kk, lane));
-#pragma unroll
-    for (int np = 0; np < 2; ++np) {
-      uint32_t bb[4];
-      ldsm4t(bb, b_krows(sm.u, LDN, 16 * kk, 32 * tn + 16 * np, lane));
-      mma16816(acc[2 * np], a, bb[0], bb[1]);
-      mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int col = h * DK + 64 * half + 32 * tn + 8 * j + 2 * c;
-    if (t < nt) st_bf2(p.out + static_cast<int64_t>(row0 + t) * p.ld_out + col, acc[j][0], acc[j][1]);
-    if (t + 8 < nt) st_bf2(p.out + static_cast<int64_t>(row0 + t + 8) * p.ld_out + col, acc[j][2], acc[j][3]);
-  }
-  {  // S = γ_C S0 + K^T Us (warp: rows [16 w, +16) of the slice)
-    const float ec = b.ec[0];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      S[j][0] *= ec;
-      S[j][1] *= ec;
-      S[j][2] *= ec;
-      S[j][3] *= ec;
-    }
-#pragma unroll
-    for (int kk = 0; kk < CH / 16; ++kk) {
-      uint32_t a[4];
-      ldsm4t(a, a_cols(b.kn, LDW, 16 * warp, 16 * kk, lane));
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bb[4];
-        ldsm4t(bb, b_krows(sm.us, LDN, 16 * kk, 16 * np, lane));
-        mma16816(S[2 * np], a, bb[0], bb[1]);
-        mma16816(S[2 * np + 1], a, bb[2], bb[3]);
-      }
-    }
-  }
-  __syncthreads();
-}
-
-// One CTA: (value head blockIdx.x / 2, value columns [64 (blockIdx.x % 2), +64), segment
-// blockIdx.y). Runs in order: trunk up to the save cut, trunk after it, then each branch from
-// the trunk's final state (kept in registers); the segment's chunks are contiguous in that
-// order, the next one loading while the current one is computed.
-__global__ void __launch_bounds__(256, 1) chunk_state_kernel(ScanParams p) {
-  extern __shared__ __align__(16) uint8_t dsm[];
-  StateSmem& sm = *reinterpret_cast<StateSmem*>(dsm);
-  const int h = blockIdx.x >> 1, half = blockIdx.x & 1;
+__global__ void __launch_bounds__(160, 1) chunk_state_kernel(const __grid_constant__ CUtensorMap tout, ScanParams p) {
+  extern __shared__ uint8_t dsm_raw[];
+  ChainSmem& sm = *reinterpret_cast<ChainSmem*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  const int h = blockIdx.x, kh = h / (p.hv / p.hk);
   const Seg sg = p.segs[blockIdx.y];
-  const int kh = h / (p.hv / p.hk);
-  const int64_t head_off = static_cast<int64_t>(h) * DK * DK + 64 * half;
-  float S[8][4], F[8][4];
-  if (sg.init_slot >= 0) {
-    state_io(S, p.state_pool + static_cast<int64_t>(sg.init_slot) * p.slot_stride + head_off, true);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
-  }
+  const int warp = warp_id(), lane = lane_id();
   int total = (sg.cut + CH - 1) / CH + (sg.trunk_len - sg.cut + CH - 1) / CH;
   for (int bi = 0; bi < sg.n_branches; ++bi) total += (p.branches[4 * (sg.branch0 + bi) + 1] + CH - 1) / CH;
   const int c0 = sg.pad;  // first chunk of the segment
-  if (threadIdx.x == 0) {
-    mbar_init(&sm.full[0], 1);
-    mbar_init(&sm.full[1], 1);
-    fence_barrier_init();
-    if (total > 0) load_chunk(p, sm.buf[0], &sm.full[0], c0, h, kh, half);
-  }
-  __syncthreads();
-  int done = 0;
   const int n_runs = 2 + sg.n_branches;
-  for (int ri = 0; ri < n_runs; ++ri) {
-    int len;
-    if (ri == 0) {
-      len = sg.cut;
-    } else if (ri == 1) {
-      len = sg.trunk_len - sg.cut;
-    } else {
-      len = p.branches[4 * (sg.branch0 + ri - 2) + 1];
-      if (ri > 2) {
+  auto run_len = [&](int ri) {
+    return ri == 0 ? sg.cut : (ri == 1 ? sg.trunk_len - sg.cut : p.branches[4 * (sg.branch0 + ri - 2) + 1]);
+  };
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 3; ++b) mbar_init(&sm.full[b], 1);
+    mbar_init(&sm.mma_u, 1);
+    mbar_init(&sm.mma_s, 1);
+    mbar_init(&sm.mma_o, 1);
+    mbar_init(&sm.conv_s, 4);
+    mbar_init(&sm.conv_u, 4);
+    mbar_init(&sm.staged, 4);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_slot;
+
+  if (warp == 4) {
+    if (elect_one()) {
+      auto load = [&](int i) {
+        ChainBuf& b = sm.buf[i % 3];
+        const int ci = c0 + i;
+        const uint8_t* rv = p.scratch + (static_cast<int64_t>(ci) * p.hv + h) * REC_V;
+        const uint8_t* rk = p.scratch + static_cast<int64_t>(p.n_chunks) * p.hv * REC_V +
+                            (static_cast<int64_t>(ci) * p.hk + kh) * REC_K;
+        fence_proxy_async();  // this buffer's previous generic reads before the async writes
+        mbar_expect_tx(&sm.full[i % 3], CHAIN_TX);
+        bulk_load(b.w, rv + REC_W, 16384, &sm.full[i % 3]);
+        bulk_load(b.qg, rv + REC_QG, 16384, &sm.full[i % 3]);
+        bulk_load(b.kn, rk, 16384, &sm.full[i % 3]);
+        bulk_load(b.p, rv + REC_P, 8192, &sm.full[i % 3]);
+        bulk_load(b.tv, rv + REC_TV, CH * LDW * 2, &sm.full[i % 3]);
+        bulk_load(b.eg, rv + REC_SC, 3 * CH * 4, &sm.full[i % 3]);
+      };
+      // chunk j's O, once the converting warps staged it in the chunk's -W slot: whole chunks by
+      // TMA store (the staging read before the buffer is reloaded), partial ones were stored by
+      // the warps themselves
+      auto store_staged = [&](int j) -> bool {
+        if (!mbar_wait(&sm.staged, j & 1)) {
+          report(p.status, kTimeoutSoftmax);
+          return false;
+        }
+        const int ci = c0 + j;
+        if (p.chunks[2 * ci + 1] == CH) {
+          tma_store_3d(&tout, sm.buf[j % 3].w, 0, h, p.chunks[2 * ci]);
+          bulk_commit();
+          bulk_wait_read<0>();
+        }
+        return true;
+      };
+      constexpr uint32_t idesc64 = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idesc_s = idesc_bf16(128, 128, false, true);
+      for (int i = 0; i < total && i < 3; ++i) load(i);
+      for (int i = 0; i < total; ++i) {
+        if (!mbar_wait(&sm.conv_s, i & 1)) {
+          report(p.status, kTimeoutSoftmax);
+          break;
+        }
+        if (!mbar_wait(&sm.full[i % 3], (i / 3) & 1)) {
+          report(p.status, kTimeoutFull);
+          break;
+        }
+        tc_fence_after();
+        const ChainBuf& b = sm.buf[i % 3];
+        const uint32_t w0 = smem_u32(b.w), q0 = smem_u32(b.qg), k0 = smem_u32(b.kn), p0 = smem_u32(b.p);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int kk = 0; kk < DK / 16; ++kk)  // U^T = S0^T (-W)^T
+          mma_f16_ts(tmem + 256, tmem + 384 + kk * 8, desc_sw128(w0 + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                     idesc64, kk > 0);
+        mma_commit(&sm.mma_u);
+        if (!mbar_wait(&sm.conv_u, i & 1)) {
+          report(p.status, kTimeoutSoftmax);
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) S[j][e] = F[j][e];
+        for (int kk = 0; kk < CH / 16; ++kk)  // S^T += Us^T K
+          mma_f16_ts(tmem + 0, tmem + 480 + kk * 8, desc_sw128(k0 + kk * 2048, 8192, 1024), idesc_s, 1u);
+        mma_commit(&sm.mma_s);
+#pragma unroll
+        for (int kk = 0; kk < DK / 16; ++kk)  // O^T = S0^T (diag(γ) Q)^T
+          mma_f16_ts(tmem + 320, tmem + 384 + kk * 8, desc_sw128(q0 + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                     idesc64, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < CH / 16; ++kk)  // O^T += U^T P^T
+          mma_f16_ts(tmem + 320, tmem + 448 + kk * 8, desc_sw128(p0 + kk * 32, 16, 1024), idesc64, 1u);
+        mma_commit(&sm.mma_o);
+        // chunk i-1's O, staged in its buffer, leaves by TMA store (whole chunks); then the
+        // buffer takes chunk i+2
+        if (i >= 1) {
+          if (!store_staged(i - 1)) break;
+          if (i + 2 < total) load(i + 2);
+        }
+      }
+      if (total > 0) store_staged(total - 1);
+      bulk_wait_all();
+    }
+  } else {
+    const int c = threadIdx.x;  // value column = TMEM lane
+    const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t t_s = tmem + lb, t_f = tmem + lb + 128, t_u = tmem + lb + 256, t_o = tmem + lb + 320;
+    const uint32_t t_s0 = tmem + lb + 384, t_ub = tmem + lb + 448, t_us = tmem + lb + 480;
+    const int64_t head_off = static_cast<int64_t>(h) * DK * DK;
+    const float* init_head =
+        sg.init_slot >= 0 ? p.state_pool + static_cast<int64_t>(sg.init_slot) * p.slot_stride + head_off : nullptr;
+    bool ok = true;
+    // 32 consecutive keys [32 j, 32 j + 32) of row c of the state S^T, from ``src``
+    auto state_piece = [&](uint32_t (&x)[32], int src, int j) {
+      if (src == kSrcTmemS || src == kSrcTmemF) {
+        tmem_ld32((src == kSrcTmemS ? t_s : t_f) + 32 * j, x);
+        tmem_wait_ld_regs(x);
+      } else if (src == kSrcPool) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[e] = __float_as_uint(init_head[(32 * j + e) * DK + c]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[e] = 0u;
+      }
+    };
+    // O of chunk i (this thread's column c, read from TMEM) -> the chunk's -W slot (its data is
+    // dead), transposed to rows [64 t][128 c]: a whole chunk then leaves by one TMA store from
+    // the MMA warp, a partial one by 16-byte row pieces from these warps.
+    auto load_o = [&](uint32_t (&ob)[32]) {  // bf16 pairs (t, t + 1)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t o[32];
+        tmem_ld32(t_o + 32 * half, o);
+        tmem_wait_ld_regs(o);
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          ob[16 * half + e] = pack_bf16(__uint_as_float(o[2 * e]), __uint_as_float(o[2 * e + 1]));
+      }
+    };
+    auto stage_o = [&](int i, const uint32_t (&ob)[32]) {
+      const int ci = c0 + i, row0 = p.chunks[2 * ci], nt = p.chunks[2 * ci + 1];
+      uint16_t* stg = reinterpret_cast<uint16_t*>(sm.buf[i % 3].w);  // [64 t][128 c] bf16
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        stg[(2 * e) * DK + c] = static_cast<uint16_t>(ob[e] & 0xffffu);
+        stg[(2 * e + 1) * DK + c] = static_cast<uint16_t>(ob[e] >> 16);
+      }
+      if (nt < CH) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four converting warps
+        for (int e = c; e < nt * (DK / 8); e += 128) {
+          const int t = e >> 4, u = e & 15;
+          *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row0 + t) * p.ld_out + h * DK + 8 * u) =
+              *reinterpret_cast<const uint4*>(stg + static_cast<int>(t * DK + 8 * u));
+        }
+      } else {
+        fence_proxy_async();  // these writes before the TMA store reads them
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.staged);
+    };
+    // the state (from ``src``) -> pool slot ``slot`` (layout [k][c] per head)
+    auto save = [&](int src, int slot) {
+      float* dst = p.state_pool + static_cast<int64_t>(slot) * p.slot_stride + head_off;
+      for (int j = 0; j < 4; ++j) {
+        uint32_t x[32];
+        state_piece(x, src, j);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) dst[(32 * j + e) * DK + c] = __uint_as_float(x[e]);
+      }
+    };
+    int i = 0, cur = init_head ? kSrcPool : kSrcZero;
+    for (int ri = 0; ri < n_runs && ok; ++ri) {
+      const int nch = (run_len(ri) + CH - 1) / CH;
+      const int run_src = ri >= 2 ? kSrcTmemF : cur;
+      for (int t = 0; t < nch; ++t, ++i) {
+        const int src = t == 0 ? run_src : kSrcTmemS;
+        if (i > 0 && !mbar_wait(&sm.mma_s, (i - 1) & 1)) {
+          report(p.status, kTimeoutMma);
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&sm.full[i % 3], (i / 3) & 1)) {
+          report(p.status, kTimeoutFull);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const ChainBuf& b = sm.buf[i % 3];
+        // the chunk's start state: bf16 copy for the products, S^T scaled by γ_C for the update
+        const float ec = b.ec[0];
+        uint32_t s0[64];
+        {
+          uint32_t x[4][32];
+          if (src == kSrcTmemS || src == kSrcTmemF) {  // four loads in flight, one wait
+            const uint32_t from = src == kSrcTmemS ? t_s : t_f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tmem_ld32(from + 32 * j, x[j]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tmem_wait_ld_regs(x[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) state_piece(x[j], src, j);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              s0[16 * j + e] = pack_bf16(__uint_as_float(x[j][2 * e]), __uint_as_float(x[j][2 * e + 1]));
+#pragma unroll
+            for (int e = 0; e < 32; ++e) x[j][e] = __float_as_uint(__uint_as_float(x[j][e]) * ec);
+            tmem_st32(t_s + 32 * j, x[j]);
+          }
+        }
+        if (i > 0 && !mbar_wait(&sm.mma_o, (i - 1) & 1)) {  // the previous O^T no longer reads S0^T
+          report(p.status, kTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tmem_st16(t_s0 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(s0 + 16 * j));
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.conv_s);
+        uint32_t ov[32];  // the previous chunk's O (complete: its mma_o was waited for above)
+        if (i > 0) load_o(ov);
+        if (!mbar_wait(&sm.mma_u, i & 1)) {
+          report(p.status, kTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {  // U = T'V + U^T, bf16; Us = e^{Γ_C-Γ_t} U, bf16
+          uint32_t u[32], ub[16], us[16];
+          tmem_ld32(t_u + 32 * half, u);
+          tmem_wait_ld_regs(u);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int t = 32 * half + 4 * q;
+            const float4 w4 = *reinterpret_cast<const float4*>(&b.ws[t]);
+            const float a0 = __bfloat162float(b.tv[t * LDW + c]) + __uint_as_float(u[4 * q]);
+            const float a1 = __bfloat162float(b.tv[(t + 1) * LDW + c]) + __uint_as_float(u[4 * q + 1]);
+            const float a2 = __bfloat162float(b.tv[(t + 2) * LDW + c]) + __uint_as_float(u[4 * q + 2]);
+            const float a3 = __bfloat162float(b.tv[(t + 3) * LDW + c]) + __uint_as_float(u[4 * q + 3]);
+            ub[2 * q] = pack_bf16(a0, a1);
+            ub[2 * q + 1] = pack_bf16(a2, a3);
+            us[2 * q] = pack_bf16(a0 * w4.x, a1 * w4.y);
+            us[2 * q + 1] = pack_bf16(a2 * w4.z, a3 * w4.w);
+          }
+          tmem_st16(t_ub + 16 * half, ub);
+          tmem_st16(t_us + 16 * half, us);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.conv_u);
+        if (i > 0) stage_o(i - 1, ov);
+        cur = kSrcTmemS;
+      }
+      if (!ok) break;
+      const bool fork = ri == 1 && sg.n_branches > 0;
+      if ((ri == 0 && sg.save_slot >= 0) || fork) {
+        if (cur == kSrcTmemS && !mbar_wait(&sm.mma_s, (i - 1) & 1)) {  // the run's last state update
+          report(p.status, kTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (ri == 0) save(cur, sg.save_slot);  // state after the cached prefix -> the pool slot
+        if (fork) {                            // the trunk's final state, every branch's start
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+            uint32_t x[32];
+            state_piece(x, cur, j);
+            tmem_st32(t_f + 32 * j, x);
+          }
+          tmem_wait_st();
+        }
       }
     }
-    for (int t0 = 0; t0 < len; t0 += CH) {
-      const int ci = c0 + done;
-      if (threadIdx.x == 0 && done + 1 < total)  // the other buffer's last reader finished (barrier below)
-        load_chunk(p, sm.buf[(done + 1) & 1], &sm.full[(done + 1) & 1], ci + 1, h, kh, half);
-      if (!mbar_wait(&sm.full[done & 1], (done >> 1) & 1)) report(p.status, kTimeoutFull);
-      state_chunk(p, sm, sm.buf[done & 1], S, h, half, p.chunks[2 * ci], p.chunks[2 * ci + 1]);
-      ++done;
+    if (ok && i > 0) {
+      if (mbar_wait(&sm.mma_o, (i - 1) & 1)) {
+        tc_fence_after();
+        uint32_t ov[32];
+        load_o(ov);
+        stage_o(i - 1, ov);
+      } else {
+        report(p.status, kTimeoutMma);
+      }
     }
-    if (ri == 0 && sg.save_slot >= 0)  // state after the cached prefix -> the pool slot
-      state_io(S, p.state_pool + static_cast<int64_t>(sg.save_slot) * p.slot_stride + head_off, false);
-    if (ri == 1 && sg.n_branches > 1) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) F[j][e] = S[j][e];
-    }
+    tc_fence_before();
+  }
+  __syncwarp();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -877,11 +1016,22 @@ static int scan_launch(const delta::ScanParams& p, int n_segs, int dk, int dv, i
   if (!n_segs || !p.n_chunks) return 0;
   static std::atomic<uint64_t> prep_conf{0}, state_conf{0};
   DAN_CUDA(smem_limit_once(delta::chunk_prep_kernel, static_cast<int>(sizeof(delta::PrepSmem)), prep_conf));
-  DAN_CUDA(smem_limit_once(delta::chunk_state_kernel, static_cast<int>(sizeof(delta::StateSmem)), state_conf));
+  DAN_CUDA(smem_limit_once(delta::chunk_state_kernel, delta::CHAIN_SMEM, state_conf));
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   delta::chunk_prep_kernel<<<dim3(p.n_chunks, p.hv), 256, sizeof(delta::PrepSmem), st>>>(p);
   DAN_CUDA(cudaGetLastError());
-  delta::chunk_state_kernel<<<dim3(2 * p.hv, n_segs), 256, sizeof(delta::StateSmem), st>>>(p);
+  // O of whole chunks by TMA store: [rows][hv][128] bf16, box one head x 64 rows, no swizzle (the
+  // rows the kernel stores always exist; the row extent only bounds the map)
+  CUtensorMap tout;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(delta::DK), static_cast<uint64_t>(p.hv), uint64_t{1} << 24};
+    const uint64_t strides[2] = {static_cast<uint64_t>(delta::DK) * 2, static_cast<uint64_t>(p.ld_out) * 2};
+    const uint32_t box[3] = {static_cast<uint32_t>(delta::DK), 1, static_cast<uint32_t>(delta::CH)};
+    int rc = make_tmap(&tout, p.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  delta::chunk_state_kernel<<<dim3(p.hv, n_segs), 160, delta::CHAIN_SMEM, st>>>(tout, p);
   DAN_CUDA(cudaGetLastError());
   return 0;
 }
