@@ -422,7 +422,9 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, 
 // configuration-2 batch: 128-key units with one thread per row 661, 64-key units 673, two
 // threads per row 766 TFLOP/s). Measured and not kept: bf16 packing of P by integer rounding
 // instead of the conversion instruction (-14%), scalar instead of packed f32x2 arithmetic
-// (-4%), every exponential on the MUFU unit (-3%).
+// (-4%), every exponential on the MUFU unit (-3%), S of a whole 128-key block per QK group
+// (N = 128, which the tensor core reads its shared-memory operands for at full rate where
+// N = 64 runs at two thirds) at the cost of the per-unit prefetch (-4.5%).
 // TMEM: S_0 [0,64) [64,128), S_1 [128,192) [192,256) (P of a unit over the first 32
 // columns of its buffer), O_0 [256, 256+D), O_1 [256+D, 256+2D).
 template <int D>
