@@ -79,12 +79,14 @@ def _linear(state, name, x, fp8, bf16=False):
     nn.Linear / torch._scaled_mm(out_dtype=bf16) return it (fp32 accumulation)."""
     rd = rounding(bf16)
     w = rd(state[name].float())
+    bias = state.get(name[:-len("weight")] + "bias")  # qwen2's q/k/v, attention_bias (llama.py:62-66)
+    b = 0.0 if bias is None else rd(bias.float())    # added in the fp32 accumulation, one rounding
     if not fp8:
-        return rd(x @ w.T)
+        return rd(x @ w.T + b)
     from . import fp8 as F8
 
     wq, ws = F8.quantize_rows(w)
-    return rd(F8.linear(x, wq, ws.flatten()))
+    return rd(F8.linear(x, wq, ws.flatten()) + b)
 
 
 def norm(x, w, eps, bf16):

@@ -14,10 +14,15 @@ import os
 import torch
 
 
+ARCHITECTURES = {"llama": "LlamaForCausalLM", "mistral": "MistralForCausalLM", "qwen2": "Qwen2ForCausalLM",
+                 "qwen3": "Qwen3ForCausalLM"}
+
+
 def llama_config(vocab=49152, hidden=576, inter=1536, layers=30, heads=9, kv_heads=3, head_dim=64,
                  theta=10000.0, tie=True, rope_scaling=None, model_type="llama", eps=1e-5):
-    """A Llama-architecture config dict in transformers' LlamaConfig field names."""
-    c = {"model_type": model_type, "architectures": ["LlamaForCausalLM"], "vocab_size": vocab,
+    """A Llama-family config dict in transformers' field names (``model_type`` llama, mistral,
+    qwen2: q/k/v projections with bias, or qwen3: per-head q/k RMSNorm)."""
+    c = {"model_type": model_type, "architectures": [ARCHITECTURES[model_type]], "vocab_size": vocab,
          "hidden_size": hidden, "intermediate_size": inter, "num_hidden_layers": layers,
          "num_attention_heads": heads, "num_key_value_heads": kv_heads, "head_dim": head_dim,
          "rope_theta": theta, "rms_norm_eps": eps, "tie_word_embeddings": tie, "max_position_embeddings": 131072,
@@ -59,6 +64,12 @@ def _shapes_llama(c):
                 (p + "mlp.down_proj.weight", (h, c["intermediate_size"]), "w")]
         if c["model_type"] == "qwen3":
             out += [(p + "self_attn.q_norm.weight", (d,), "n1"), (p + "self_attn.k_norm.weight", (d,), "n1")]
+        if c["model_type"] == "qwen2" or c.get("attention_bias"):  # q/k/v bias (llama.py:62-65)
+            out += [(p + "self_attn.q_proj.bias", (c["num_attention_heads"] * d,), "n0"),
+                    (p + "self_attn.k_proj.bias", (c["num_key_value_heads"] * d,), "n0"),
+                    (p + "self_attn.v_proj.bias", (c["num_key_value_heads"] * d,), "n0")]
+        if c.get("attention_bias"):
+            out.append((p + "self_attn.o_proj.bias", (h,), "n0"))
     out.append(("model.norm.weight", (h,), "n1"))
     if not c.get("tie_word_embeddings"):
         out.append(("lm_head.weight", (c["vocab_size"], h), "w"))

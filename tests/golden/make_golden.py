@@ -18,6 +18,8 @@ Fixtures:
 - ``tiny_llama.json``: per-branch label logits from ``Runner.read_many`` (dense
   masked path, fp32) and from ``HFReference`` (reference.py:16-23) for the
   configuration-1 model, plus a cold/warm/mixed prefix-cache sequence.
+- ``tiny_qwen2.json`` / ``tiny_qwen3.json``: the same for small Qwen2 (q/k/v bias) and Qwen3
+  (per-head q/k RMSNorm) models;
 - ``tiny_hybrid.json``: the same for a small Qwen3.5 hybrid (3 DeltaNet + 1
   gated attention layer) whose trunks exceed one 64-token delta-rule chunk.
 - ``tree_mask.json``: ``tree_mask`` / ``branch_rows_mask`` rows
@@ -216,11 +218,15 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DAN_REFERENCE"), required=False,
                     help="path of the reference source tree (the directory holding the dan package)")
+    ap.add_argument("--only", choices=["families"], help="regenerate only these fixtures")
     args = ap.parse_args()
     if not args.reference:
         ap.error("--reference (or DAN_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     import dan.prompt  # noqa: F401
+    if args.only == "families":
+        dump_families(dan)
+        return
     from dan.attention import branch_rows_mask, tree_mask
 
     torch.manual_seed(0)
@@ -248,7 +254,21 @@ def main():
     hp = small_plans(rng, cfgh["vocab_size"], 3, trunk=(70, 150), nb=(1, 3), blen=(3, 9), static=(20, 60))
     hx = small_plans(rng, cfgh["vocab_size"], 1, trunk=(70, 150), nb=(1, 3), blen=(3, 9), static=(20, 60))
     run_model(dan, cfgh, 0, [("cold", hp), ("warm", hp), ("mixed", [hp[2], hx[0], hp[0]])], "tiny_hybrid.json")
+    dump_families(dan)
     dump_fullsize(dan)
+
+
+def dump_families(dan):
+    """``tiny_qwen2.json`` / ``tiny_qwen3.json``: the other Llama-family variants dan runs
+    (llama.py:62-85, 129-135): Qwen2's q/k/v bias and Qwen3's per-head q/k RMSNorm."""
+    for mt, seed in (("qwen2", 5), ("qwen3", 6)):
+        cfg = weights.llama_config(vocab=512, hidden=256, inter=512, layers=2, heads=4, kv_heads=2, head_dim=64,
+                                   model_type=mt, tie=False, theta=1000000.0, eps=1e-6)
+        rng = random.Random(seed)
+        plans = small_plans(rng, cfg["vocab_size"], 3, trunk=(60, 140), nb=(1, 3), blen=(3, 9), static=(20, 50))
+        extra = small_plans(rng, cfg["vocab_size"], 1, trunk=(60, 140), nb=(1, 3), blen=(3, 9), static=(20, 50))
+        run_model(dan, cfg, seed, [("cold", plans), ("warm", plans), ("mixed", [plans[1], extra[0], plans[0]])],
+                  f"tiny_{mt}.json")
 
 
 if __name__ == "__main__":

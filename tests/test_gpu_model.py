@@ -40,6 +40,23 @@ def test_tiny_llama_matches_reference(cuda, tiny_dir):
     assert worst_l < 5e-2, worst_l
 
 
+@pytest.mark.parametrize("name", ["tiny_qwen2.json", "tiny_qwen3.json"])
+def test_llama_family_variants_match_reference(cuda, tmp_path, name):
+    """Qwen2 (q/k/v bias in the q/k/v GEMM's epilogue, before RoPE) and Qwen3 (per-head q/k
+    RMSNorm before RoPE) end to end against dan's own fp32 runner, cold -> warm -> mixed."""
+    g = golden(name)
+    weights.save_checkpoint(str(tmp_path), g["config"], weights.random_state(g["config"], g["seed"]))
+    runner = Runner(str(tmp_path), cuda)
+    worst_p = 0.0
+    for b in g["batches"]:
+        _, probs = runner.read_many(plans_from_json(b["plans"]), probabilities=True)
+        for pp, want in zip(probs, b["runner"]):
+            for p, w in zip(pp, want):
+                worst_p = max(worst_p, (p - torch.softmax(torch.tensor(w).double(), 0).float()).abs().max().item())
+        assert runner.cache.hits == b["hits"], b["name"]
+    assert worst_p < 5e-3, worst_p
+
+
 def test_without_cache_same_answers(cuda, tiny_dir):
     path, g = tiny_dir
     runner = Runner(path, cuda, cache_bytes=0)

@@ -4,6 +4,7 @@ The fixtures come from running the reference (tests/golden/make_golden.py);
 these tests prove the oracle restates its algorithm before the oracle is used
 to check the CUDA path.
 """
+import pytest
 import torch
 from conftest import golden, plans_from_json
 
@@ -95,6 +96,12 @@ def test_tiny_hybrid_golden():
     _model_golden("tiny_hybrid.json", OQ)
 
 
+@pytest.mark.parametrize("name", ["tiny_qwen2.json", "tiny_qwen3.json"])
+def test_llama_family_variants_golden(name):
+    """Qwen2 (q/k/v bias) and Qwen3 (per-head q/k RMSNorm) through the oracle's Llama path."""
+    _model_golden(name, OL)
+
+
 def test_useful_pairs_matches_mask_count():
     segs = [{"start": 0, "end": 10, "branch": [0] * 4 + [1] * 3 + [2] * 3,
              "past": (torch.zeros(1, 5, 2), torch.zeros(1, 5, 2))}]
@@ -130,3 +137,8 @@ def test_tiny_llama_bf16_mode_golden():
 
 def test_tiny_hybrid_bf16_mode_golden():
     _bf16_golden("tiny_hybrid.json")
+
+
+@pytest.mark.parametrize("name", ["tiny_qwen2.json", "tiny_qwen3.json"])
+def test_llama_family_variants_bf16_mode_golden(name):
+    _bf16_golden(name)
