@@ -18,6 +18,7 @@ Fixtures:
 - ``tiny_llama.json``: per-branch label logits from ``Runner.read_many`` (dense
   masked path, fp32) and from ``HFReference`` (reference.py:16-23) for the
   configuration-1 model, plus a cold/warm/mixed prefix-cache sequence.
+- ``rope_frequencies.json``: RoPE inverse frequencies (default, linear, llama3 scaling);
 - ``tiny_qwen2.json`` / ``tiny_qwen3.json``: the same for small Qwen2 (q/k/v bias) and Qwen3
   (per-head q/k RMSNorm) models;
 - ``tiny_hybrid.json``: the same for a small Qwen3.5 hybrid (3 DeltaNet + 1
@@ -218,7 +219,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DAN_REFERENCE"), required=False,
                     help="path of the reference source tree (the directory holding the dan package)")
-    ap.add_argument("--only", choices=["families"], help="regenerate only these fixtures")
+    ap.add_argument("--only", choices=["families", "rope"], help="regenerate only these fixtures")
     args = ap.parse_args()
     if not args.reference:
         ap.error("--reference (or DAN_REFERENCE) is required")
@@ -226,6 +227,9 @@ def main():
     import dan.prompt  # noqa: F401
     if args.only == "families":
         dump_families(dan)
+        return
+    if args.only == "rope":
+        dump_rope(dan)
         return
     from dan.attention import branch_rows_mask, tree_mask
 
@@ -255,7 +259,34 @@ def main():
     hx = small_plans(rng, cfgh["vocab_size"], 1, trunk=(70, 150), nb=(1, 3), blen=(3, 9), static=(20, 60))
     run_model(dan, cfgh, 0, [("cold", hp), ("warm", hp), ("mixed", [hp[2], hx[0], hp[0]])], "tiny_hybrid.json")
     dump_families(dan)
+    dump_rope(dan)
     dump_fullsize(dan)
+
+
+ROPE_CASES = [
+    ("default", {"rope_theta": 500000.0}),
+    ("linear", {"rope_theta": 10000.0, "rope_scaling": {"rope_type": "linear", "factor": 4.0}}),
+    ("llama3", {"rope_theta": 500000.0, "rope_scaling": {
+        "rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+        "original_max_position_embeddings": 8192}}),
+    ("params", {"rope_parameters": {"rope_theta": 1000000.0, "rope_type": "default"}}),
+]
+
+
+def dump_rope(dan):
+    """``rope_frequencies.json``: the reference's RoPE inverse frequencies (llama.py:18-40) for
+    default, linear and llama3 scaling at head dims 64 / 128 / 256."""
+    from types import SimpleNamespace
+
+    from dan.models.llama import inv_frequencies
+
+    out = []
+    for name, fields in ROPE_CASES:
+        for d in (64, 128, 256):
+            inv = inv_frequencies(SimpleNamespace(**fields), d)
+            out.append({"name": name, "config": fields, "head_dim": d, "inv": inv.tolist()})
+    with open(os.path.join(HERE, "rope_frequencies.json"), "w") as f:
+        json.dump(out, f)
 
 
 def dump_families(dan):

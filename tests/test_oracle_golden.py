@@ -142,3 +142,15 @@ def test_tiny_hybrid_bf16_mode_golden():
 @pytest.mark.parametrize("name", ["tiny_qwen2.json", "tiny_qwen3.json"])
 def test_llama_family_variants_bf16_mode_golden(name):
     _bf16_golden(name)
+
+
+def test_rope_frequencies_golden():
+    """RoPE inverse frequencies (default, linear, llama3 scaling; llama.py:18-40), bit for bit in
+    both the oracle and the model's table builder."""
+    from dan_b200.llama import inv_frequencies
+
+    for case in golden("rope_frequencies.json"):
+        want = torch.tensor(case["inv"], dtype=torch.float32)
+        assert torch.equal(OL.inv_frequencies(case["config"], case["head_dim"]), want), case["name"]
+        assert torch.equal(inv_frequencies(case["config"], case["head_dim"]), want), case["name"]
+
