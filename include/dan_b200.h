@@ -169,15 +169,17 @@ int dan_gather_rows(const void* src, int64_t ld_src, const void* hist, int64_t l
  * [n_chunks, 2] {first row, rows <= 64}, each segment's runs (trunk to the cut, rest of the
  * trunk, each branch) cut into chunks listed contiguously in that order; state_pool: fp32
  * [slots, hv, 128, 128] of this layer (init / save slots, -1 = none). dk = dv = 128.
- * scratch: caller-owned device buffer of dan_gated_delta_scratch_bytes(n_chunks, hk, hv) bytes
- * (16-byte aligned) for the per-chunk intermediates; it is fully rewritten by each call. */
+ * out: [rows, hv * 128] bf16, 16-byte aligned, ld_out a multiple of 8 (whole chunks of it are
+ * written by TMA store). scratch: caller-owned device buffer of
+ * dan_gated_delta_scratch_bytes(n_chunks, hk, hv) bytes (16-byte aligned) for the per-chunk
+ * intermediates; it is fully rewritten by each call. */
 int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* b, const void* a,
                          int64_t ld_ba, const float* a_log, const float* dt_bias, const int* segs, int n_segs,
                          const int* branches, const int* chunks, int n_chunks, float* state_pool,
                          int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv, int dk, int dv,
                          float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream);
-/* Bytes of scratch dan_gated_delta_scan needs for n_chunks chunks (45824 per chunk and value head
- * plus 34816 per chunk and key head). */
+/* Bytes of scratch dan_gated_delta_scan needs for n_chunks chunks (59136 per chunk and value head
+ * plus 16384 per chunk and key head). */
 int64_t dan_gated_delta_scratch_bytes(int n_chunks, int hk, int hv);
 /* dan_gated_delta_scan with the gates given instead of computed: beta [rows, hv] bf16 (row stride
  * ld_beta) and the log decay g [rows, hv] fp32 (row stride ld_g); q and k still l2-normalised
