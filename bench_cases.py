@@ -11,6 +11,7 @@ are larger than L2 where the configuration's are.
   (M = 7089 tokens): q/k/v + RoPE epilogue, o + residual, gate/up + SwiGLU,
   down + residual.
 - attention: tree attention of one configuration-2 batch (32/8 heads x 128).
+- attention256: the same kernel family at 16/4 heads x 256 on a configuration-4 batch.
 - deltanet: causal conv + gated delta scan of one configuration-4 batch
   (Qwen3.5-4B-style: 16 key / 32 value heads x 128).
 - norm: RMSNorm of [7089, 4096].
@@ -81,6 +82,22 @@ def attention(iters):
     ms = _time(lambda: tree_attention(q, k, v, lay), iters)
     return {"tokens": n, "useful_pairs": lay.pairs, "tiles": lay.n_tiles, "ms": ms,
             "tflops": 4 * 32 * 128 * lay.pairs / ms / 1e9}
+
+
+def attention256(iters):
+    """Tree attention at the Qwen3.5-4B gated-attention heads (16 / 4 x 256, the single-head
+    kernel) on one configuration-4 batch."""
+    dev = torch.device("cuda")
+    ids, pos, segs, reads, _ = _pack(4, 0)
+    n = len(ids)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(n, 16, 256, device=dev, generator=g).bfloat16()
+    k = torch.randn(n, 4, 256, device=dev, generator=g).bfloat16()
+    v = torch.randn(n, 4, 256, device=dev, generator=g).bfloat16()
+    lay = TreeLayout.build(segs, n, dev)
+    ms = _time(lambda: tree_attention(q, k, v, lay), iters)
+    return {"tokens": n, "useful_pairs": lay.pairs, "tiles": lay.n_tiles, "ms": ms,
+            "tflops": 4 * 16 * 256 * lay.pairs / ms / 1e9}
 
 
 def deltanet(iters):
@@ -333,7 +350,7 @@ def kvstore(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "gemm8", "attention", "deltanet", "conv", "gnorm", "norm", "quant", "readout",
+    ap.add_argument("case", choices=["gemm", "gemm8", "attention", "attention256", "deltanet", "conv", "gnorm", "norm", "quant", "readout",
                                      "gate", "kvstore", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()

@@ -20,16 +20,19 @@
 // every other block is fully masked and skipped. A block that is fully
 // visible to every row of the tile skips the mask arithmetic.
 //
-// Pipeline (warp-specialised, 192 threads):
+// Pipeline of the single-head kernel (warp-specialised, 320 threads):
 //   warp 0   TMA producer: Q once, then K_j / V_j into an NS-deep ring
 //            (packed rows of the current batch, or pool pages for past keys);
 //   warp 1   MMA issuer: S_j = Q K_j^T into TMEM buffer j&1 (SS MMA); after the
 //            softmax has written P_j (bf16) over S_j, O += P_j V_j with P read
 //            from TMEM (TS MMA) and V as an MN-major shared-memory operand;
-//   warps 2-5 softmax (one thread per query row): online softmax in the log2
-//            domain; O is rescaled lazily, only when a row max grows by more
-//            than 2^8 (exact: the same stale max is used for P and for l);
-//            then the epilogue O / l -> bf16.
+//   warps 2-9 softmax, 16 rows each with two threads per row (16x32bx2 TMEM
+//            shape: one thread per 64 keys of a block and half of O's columns):
+//            online softmax in the log2 domain; O is rescaled lazily, only when a
+//            row max grows by more than 2^8 (exact: the same stale max is used for
+//            P and for l); then the epilogue O / l -> bf16. With one thread per row
+//            (four softmax warps) it ran 686 TFLOP/s at 16 / 4 heads x 256 on a
+//            configuration-4 batch, with two 825.
 // TMEM: S0 [0,128), S1 [128,256), O [256, 256 + D).
 #include "common.cuh"
 
@@ -37,7 +40,7 @@ namespace dan {
 namespace attn {
 
 constexpr int BM = 128, BN = 128;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // single-head kernel: TMA warp, MMA warp, 8 softmax warps
 constexpr int CHUNK = 128 * 128;  // bytes of one 64-column x 128-row bf16 box
 
 struct Tile {
@@ -74,10 +77,10 @@ struct Cfg {
   static constexpr int CHUNKS = D / 64;
   static constexpr int Q_BYTES = CHUNKS * CHUNK;
   static constexpr int KV_BYTES = CHUNKS * CHUNK;
-  // Output staging: per softmax warp two 2 KB slots (32 rows x 32 bf16 columns, 64-byte
-  // swizzle) sent by TMA store.
-  static constexpr int SLOT_BYTES = 32 * 64;
-  static constexpr int SINK_BYTES = 4 * 2 * SLOT_BYTES;
+  // Output staging: per softmax warp two 1 KB slots (16 rows x 32 bf16 columns, one per
+  // column half, 64-byte swizzle) sent by TMA store.
+  static constexpr int SLOT_BYTES = 16 * 64;
+  static constexpr int SINK_BYTES = 8 * 2 * SLOT_BYTES;
   // At least 120 KB so two CTAs never share an SM: each allocates all 512 TMEM columns.
   static constexpr int SMEM_USED = Q_BYTES + 2 * NS * KV_BYTES + SINK_BYTES + 1024 + 512;
   static constexpr int SMEM = SMEM_USED < 120 * 1024 ? 120 * 1024 : SMEM_USED;
@@ -88,360 +91,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-
-template <int D>
-__global__ void __launch_bounds__(THREADS, 1)
-    tree_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tpk,
-                          const __grid_constant__ CUtensorMap tpv, const __grid_constant__ CUtensorMap to,
-                          Params p) {
-  using C = Cfg<D>;
-  constexpr int NS = C::NS;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem;
-  uint8_t* sk = sq + C::Q_BYTES;
-  uint8_t* sv = sk + NS * C::KV_BYTES;
-  uint8_t* sink = sv + NS * C::KV_BYTES;  // 1024-byte aligned: Q and K/V stages are multiples of 16 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sink + C::SINK_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
-  uint64_t* v_full = k_full + NS;
-  uint64_t* k_empty = v_full + NS;
-  uint64_t* v_empty = k_empty + NS;
-  uint64_t* s_full = v_empty + NS;   // [2]
-  uint64_t* p_full = s_full + 2;     // [2]
-  uint64_t* pv_done = p_full + 2;    // [2] indexed by block parity
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
-
-  const int head = blockIdx.x;
-  const int kvh = head / (p.n_heads / p.n_kv_heads);
-  const Tile tile = reinterpret_cast<const Tile*>(p.tiles)[blockIdx.y];
-  const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
-  const int warp = warp_id(), lane = lane_id();
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 4);
-      mbar_init(&pv_done[b], 1);
-    }
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;
-
-  if (warp == 0) {
-    if (elect_one()) {
-      tma_prefetch_desc(&tq);
-      tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
-      mbar_expect_tx(q_full, C::Q_BYTES);
-#pragma unroll
-      for (int c = 0; c < C::CHUNKS; ++c) tma_load_3d(sq + c * CHUNK, &tq, q_full, c * 64, head, tile.row0);
-      for (int j = 0; j < nblk; ++j) {
-        const int stage = j % NS;
-        const uint32_t ph = (j / NS) & 1;
-        const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
-        const int kb = b * BN;
-        const bool pool = kb < tile.ppad;
-        const int row = pool ? p.pages[tile.page0 + b] * BN : tile.seg_start + (kb - tile.ppad);
-        const CUtensorMap* mk = pool ? &tpk : &tk;
-        const CUtensorMap* mv = pool ? &tpv : &tv;
-        if (!mbar_wait(&k_empty[stage], ph ^ 1)) {
-          report(p.status, kTimeoutEmpty);
-          break;
-        }
-        mbar_expect_tx(&k_full[stage], C::KV_BYTES);
-#pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_3d(sk + stage * C::KV_BYTES + c * CHUNK, mk, &k_full[stage], c * 64, kvh, row);
-        if (!mbar_wait(&v_empty[stage], ph ^ 1)) {
-          report(p.status, kTimeoutEmpty);
-          break;
-        }
-        mbar_expect_tx(&v_full[stage], C::KV_BYTES);
-#pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_3d(sv + stage * C::KV_BYTES + c * CHUNK, mv, &v_full[stage], c * 64, kvh, row);
-      }
-    }
-  } else if (warp == 1) {
-    if (elect_one()) {
-      constexpr uint32_t idesc_qk = idesc_bf16(BM, BN, false, false);
-      constexpr uint32_t idesc_pv = idesc_bf16(BM, D, false, true);
-      bool ok = mbar_wait(q_full, 0);
-      if (!ok) report(p.status, kTimeoutFull);
-      tc_fence_after();
-      const uint32_t q0 = smem_u32(sq);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % NS;
-        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1)) {
-          report(p.status, kTimeoutSoftmax);
-          return false;
-        }
-        if (!mbar_wait(&v_full[st], (i / NS) & 1)) {
-          report(p.status, kTimeoutFull);
-          return false;
-        }
-        tc_fence_after();
-        const uint32_t v0 = smem_u32(sv + st * C::KV_BYTES);
-        const uint32_t pa = tmem + (i & 1) * 128;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t db = desc_sw128(v0 + kk * 2048, CHUNK, 1024);
-          mma_f16_ts(tmem_o, pa + kk * 8, db, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&v_empty[st]);
-        mma_commit(&pv_done[i & 1]);
-        return true;
-      };
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int stage = j % NS;
-        if (j >= 2 && !mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1)) {
-          report(p.status, kTimeoutMma);
-          break;
-        }
-        if (!mbar_wait(&k_full[stage], (j / NS) & 1)) {
-          report(p.status, kTimeoutFull);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t k0 = smem_u32(sk + stage * C::KV_BYTES);
-        const uint32_t sd = tmem + (j & 1) * 128;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
-          mma_f16_ss(sd, desc_sw128(q0 + off, 16, 1024), desc_sw128(k0 + off, 16, 1024), idesc_qk, kk > 0);
-        }
-        mma_commit(&s_full[j & 1]);
-        mma_commit(&k_empty[stage]);
-        if (j >= 1 && !issue_pv(j - 1)) break;
-        if (j == nblk - 1) issue_pv(j);
-      }
-    }
-  } else {
-    // softmax + epilogue: thread <-> query row
-    const int sub = warp & 3;
-    const int r_in = sub * 32 + lane;
-    const int row = tile.row0 + r_in;
-    const bool valid = r_in < tile.nrows;
-    const int qv = tile.q0v + r_in;
-    const int own = valid ? tile.ppad + (p.row_own[row] - tile.seg_start) : 0;
-    const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
-      const int kb = b * BN;
-      const bool full = (kb + BN <= tile.past) ||
-                        (kb >= tile.ppad && kb + BN <= tile.split && kb + BN - 1 <= tile.q0v);
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
-        report(p.status, kTimeoutMma);
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t sa = tmem + lane_base + (j & 1) * 128;
-      uint32_t s[128];
-      tmem_ld32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tmem_ld32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-      tmem_ld32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
-      tmem_ld32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
-      tmem_wait_ld();
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const float x = __uint_as_float(s[c]) * p.scale_log2;
-          s[c] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const int v = kb + c;
-          const bool vis = v <= qv && (v < tile.split || v >= own) && (v < tile.past || v >= tile.ppad);
-          const float x = vis ? __uint_as_float(s[c]) * p.scale_log2 : -INFINITY;
-          s[c] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
-      }
-      const float m_new = fmaxf(m, mx);
-      bool rescale = false;
-      float alpha = 1.f;
-      if (m_new != -INFINITY) {
-        if (m == -INFINITY) {
-          m = m_new;  // nothing accumulated yet for this row: O row and l are zero
-        } else if (m_new > m + 8.f) {
-          alpha = fast_exp2(m - m_new);
-          m = m_new;
-          rescale = true;
-        }
-      }
-      const float mu = m == -INFINITY ? 0.f : m;
-      float sum = 0.f;
-      uint32_t pk[64];
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = fast_exp2(__uint_as_float(s[2 * c]) - mu);
-        const float p1 = fast_exp2(__uint_as_float(s[2 * c + 1]) - mu);
-        sum += p0 + p1;
-        pk[c] = pack_bf16(p0, p1);
-      }
-      l = l * alpha + sum;
-      tmem_st32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-      if (__any_sync(0xffffffffu, rescale) && j > 0) {
-        // O holds sum_{i<j} P_i V_i once PV_{j-1} completes; scale this warp's rows.
-        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
-          report(p.status, kTimeoutMma);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(tmem_o + lane_base + c, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tmem_o + lane_base + c, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[j & 1]);
-    }
-    if (ok && nblk > 0) {
-      const int last = nblk - 1;
-      if (!mbar_wait(&pv_done[last & 1], (last >> 1) & 1)) {
-        report(p.status, kTimeoutMma);
-      } else {
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        // Whole 32-row slabs leave through two shared-memory slots by TMA store (as in the
-        // paired kernel); a segment's ragged last rows are stored per row.
-        const bool slab = (sub + 1) * 32 <= tile.nrows;
-        uint8_t* slots = sink + (warp - 2) * 2 * C::SLOT_BYTES;
-        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
-#pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(tmem_o + lane_base + c, o);
-          tmem_wait_ld();
-          uint32_t pkd[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-          if (slab) {
-            uint8_t* slot = slots + ((c >> 5) & 1) * C::SLOT_BYTES;
-            if (lane == 0) bulk_wait_read<1>();  // the store sent from this slot two chunks ago has read it
-            __syncwarp();
-            uint4* d4 = reinterpret_cast<uint4*>(slot + lane * 64);
-            const int sw = (lane >> 1) & 3;  // 64-byte swizzle: unit u of row r at u ^ ((r >> 1) & 3)
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i ^ sw] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_3d(&to, slot, c, head, tile.row0 + sub * 32);
-              bulk_commit();
-            }
-            __syncwarp();
-          } else if (valid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
-          }
-        }
-      }
-    }
-    if (lane == 0) bulk_wait_all();  // output stores done before the CTA's shared memory goes away
-    tc_fence_before();
-  }
-  __syncwarp();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-template <int D>
-int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tpk,
-           const CUtensorMap& tpv, const CUtensorMap& to, const Params& p, int n_tiles, cudaStream_t stream) {
-  static std::atomic<uint64_t> configured{0};
-  DAN_CUDA(smem_limit_once(tree_attention_kernel<D>, Cfg<D>::SMEM, configured));
-  dim3 grid(p.n_heads, n_tiles);
-  tree_attention_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, to, p);
-  DAN_CUDA(cudaGetLastError());
-  return 0;
-}
-
-// ---------------------------------------------------------------------------------
-// Paired-head persistent variant. A work item is one 128-row query tile x two query
-// heads that share a KV head (GQA): both heads have the same key blocks and masks, so
-// each K/V tile is loaded once for 2 x 128 query rows. One CTA per SM walks the
-// LPT-ordered items (tile-major, so CTAs running at the same time share K/V in L2) with
-// barrier phases carried across items.
-// Each 128-key block is consumed as two 64-key units, and each head has two 64-column S
-// buffers in TMEM (unit k in buffer k & 1), so the tensor core computes S_h(k + 2) while
-// the softmax warps of head h are still on unit k + 1: a head's softmax never waits for
-// its own PV and QK products. MMA issue order per item of n units:
-//   QK0(0) QK1(0) QK0(1) QK1(1) | PV0(k) QK0(k+2) PV1(k) QK1(k+2) | ... PV0(n-1) PV1(n-1)
-// (the next item's first QK products run while the softmax warps store this item's output).
-// QK_h(k+2) overwrites the buffer that held P_h(k) only after PV_h(k), issued before it
-// by the same thread, has read it (tcgen05 MMAs of one thread run in issue order). A
-// commit arrives only after every earlier MMA of the issuing thread completed, so when a
-// softmax warp sees S_h(k) the product PV_h(k - 2) is in O_h; PV_h(k - 1) may still be
-// running, and the lazy O rescale (rare) waits for it first. Each row's visible keys within a
-// block are three intervals (past, trunk, own branch), turned into a 32-bit mask per thread
-// and unit.
-// Warps: 0 TMA, 1 MMA, 2-9 softmax head 2p, 10-17 softmax head 2p+1 (576 threads), each softmax
-// warp 16 rows with two threads per row (the 16x32bx2 TMEM access shape), so each SM
-// sub-partition holds four softmax warps. The softmax warps are latency-bound rather than
-// issue-bound (issue slots 40% busy with two softmax warps per sub-partition, 56% with four;
-// configuration-2 batch: 128-key units with one thread per row 661, 64-key units 673, two
-// threads per row 766 TFLOP/s). Measured and not kept: bf16 packing of P by integer rounding
-// instead of the conversion instruction (-14%), scalar instead of packed f32x2 arithmetic
-// (-4%), every exponential on the MUFU unit (-3%), S of a whole 128-key block per QK group
-// (N = 128, which the tensor core reads its shared-memory operands for at full rate where
-// N = 64 runs at two thirds) at the cost of the per-unit prefetch (-4.5%).
-// TMEM: S_0 [0,64) [64,128), S_1 [128,192) [192,256) (P of a unit over the first 32
-// columns of its buffer), O_0 [256, 256+D), O_1 [256+D, 256+2D).
-template <int D>
-struct PairCfg {
-  static constexpr int NS = D <= 64 ? 3 : 2;
-  static constexpr int CHUNKS = D / 64;
-  static constexpr int Q_BYTES = CHUNKS * CHUNK;  // one head's 128 query rows
-  static constexpr int KV_BYTES = CHUNKS * CHUNK;
-  // Output staging: per softmax warp two 1 KB slots (16 rows x 32 bf16 columns each, one per
-  // column half), written with the 64-byte swizzle and sent by TMA store.
-  static constexpr int SLOT_BYTES = 16 * 64;
-  static constexpr int SINK_BYTES = 16 * 2 * SLOT_BYTES;
-  // 225.5 KB at D = 128: a second Q buffer (64 KB) does not fit.
-  static constexpr int SMEM_USED = 2 * Q_BYTES + 2 * NS * KV_BYTES + SINK_BYTES + 1024 + 512;
-  static constexpr int SMEM = SMEM_USED < 120 * 1024 ? 120 * 1024 : SMEM_USED;
-  static constexpr int THREADS = 576;
-};
 
 // bits [lo, hi) of a 32-bit word (arguments relative to the word's first column)
 __device__ __forceinline__ uint32_t span_bits(int lo, int hi) {
@@ -575,6 +224,366 @@ __device__ __forceinline__ void chunk_p_u(const uint32_t (&s)[32], uint32_t cls,
     chunk_exp<false>(s, sl2, mu, sum, pk);
   }
 }
+
+template <int D>
+__global__ void __launch_bounds__(THREADS, 1)
+    tree_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tpk,
+                          const __grid_constant__ CUtensorMap tpv, const __grid_constant__ CUtensorMap to,
+                          Params p) {
+  using C = Cfg<D>;
+  constexpr int NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* sk = sq + C::Q_BYTES;
+  uint8_t* sv = sk + NS * C::KV_BYTES;
+  uint8_t* sink = sv + NS * C::KV_BYTES;  // 1024-byte aligned: Q and K/V stages are multiples of 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sink + C::SINK_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* v_full = k_full + NS;
+  uint64_t* k_empty = v_full + NS;
+  uint64_t* v_empty = k_empty + NS;
+  uint64_t* s_full = v_empty + NS;   // [2]
+  uint64_t* p_full = s_full + 2;     // [2]
+  uint64_t* pv_done = p_full + 2;    // [2] indexed by block parity
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+
+  const int head = blockIdx.x;
+  const int kvh = head / (p.n_heads / p.n_kv_heads);
+  const Tile tile = reinterpret_cast<const Tile*>(p.tiles)[blockIdx.y];
+  const int nblk = tile.nblk_a + (tile.blk_b1 - tile.blk_b0);
+  const int warp = warp_id(), lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 8);
+      mbar_init(&pv_done[b], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem + 256;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < C::CHUNKS; ++c) tma_load_3d(sq + c * CHUNK, &tq, q_full, c * 64, head, tile.row0);
+      for (int j = 0; j < nblk; ++j) {
+        const int stage = j % NS;
+        const uint32_t ph = (j / NS) & 1;
+        const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
+        const int kb = b * BN;
+        const bool pool = kb < tile.ppad;
+        const int row = pool ? p.pages[tile.page0 + b] * BN : tile.seg_start + (kb - tile.ppad);
+        const CUtensorMap* mk = pool ? &tpk : &tk;
+        const CUtensorMap* mv = pool ? &tpv : &tv;
+        if (!mbar_wait(&k_empty[stage], ph ^ 1)) {
+          report(p.status, kTimeoutEmpty);
+          break;
+        }
+        mbar_expect_tx(&k_full[stage], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_3d(sk + stage * C::KV_BYTES + c * CHUNK, mk, &k_full[stage], c * 64, kvh, row);
+        if (!mbar_wait(&v_empty[stage], ph ^ 1)) {
+          report(p.status, kTimeoutEmpty);
+          break;
+        }
+        mbar_expect_tx(&v_full[stage], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_3d(sv + stage * C::KV_BYTES + c * CHUNK, mv, &v_full[stage], c * 64, kvh, row);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16(BM, D, false, true);
+      bool ok = mbar_wait(q_full, 0);
+      if (!ok) report(p.status, kTimeoutFull);
+      tc_fence_after();
+      const uint32_t q0 = smem_u32(sq);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i % NS;
+        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1)) {
+          report(p.status, kTimeoutSoftmax);
+          return false;
+        }
+        if (!mbar_wait(&v_full[st], (i / NS) & 1)) {
+          report(p.status, kTimeoutFull);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t v0 = smem_u32(sv + st * C::KV_BYTES);
+        const uint32_t pa = tmem + (i & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t db = desc_sw128(v0 + kk * 2048, CHUNK, 1024);
+          mma_f16_ts(tmem_o, pa + kk * 8, db, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&v_empty[st]);
+        mma_commit(&pv_done[i & 1]);
+        return true;
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int stage = j % NS;
+        if (j >= 2 && !mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1)) {
+          report(p.status, kTimeoutMma);
+          break;
+        }
+        if (!mbar_wait(&k_full[stage], (j / NS) & 1)) {
+          report(p.status, kTimeoutFull);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sk + stage * C::KV_BYTES);
+        const uint32_t sd = tmem + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_f16_ss(sd, desc_sw128(q0 + off, 16, 1024), desc_sw128(k0 + off, 16, 1024), idesc_qk, kk > 0);
+        }
+        mma_commit(&s_full[j & 1]);
+        mma_commit(&k_empty[stage]);
+        if (j >= 1 && !issue_pv(j - 1)) break;
+        if (j == nblk - 1) issue_pv(j);
+      }
+    }
+  } else {
+    // softmax + epilogue: warp w (2..9) covers 16 rows of its TMEM lane quarter (w % 4), two
+    // threads per row (the 16x32bx2 access shape): thread t < 16 takes row t and keys [0, 64)
+    // of each block (the first half of O's columns), thread t + 16 keys [64, 128) (the second
+    // half); the halves of a row share their maximum by one shuffle.
+    const int sidx = warp - 2;       // 0..7
+    const int sub = warp & 3;        // TMEM lane quarter
+    const int half = lane >> 4;
+    const int r0 = sub * 32 + (sidx >> 2) * 16;  // first tile row of this warp
+    const int r_in = r0 + (lane & 15);
+    const int row = tile.row0 + r_in;
+    const bool valid = r_in < tile.nrows;
+    const int qv = tile.q0v + r_in;
+    const int own = valid ? tile.ppad + (p.row_own[row] - tile.seg_start) : tile.ppad;
+    const int e_past = min(tile.past, qv + 1), e_trunk = min(tile.split, qv + 1);
+    const uint32_t lane_base = static_cast<uint32_t>(r0) << 16;
+    const uint32_t o_addr = tmem_o + lane_base;
+    const float sl2 = p.scale_log2;
+    uint8_t* wslots = sink + sidx * 2 * C::SLOT_BYTES;  // per key half: 16 rows x 32 columns
+    uint8_t* slot = wslots + half * C::SLOT_BYTES;
+    float m = -INFINITY, l = 0.f;  // m in log2 units (scaled); l over this thread's keys
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j < tile.nblk_a ? j : tile.blk_b0 + (j - tile.nblk_a);
+      const int kb = b * BN;
+      const bool full = (kb + BN <= tile.past) ||
+                        (kb >= tile.ppad && kb + BN <= tile.split && kb + BN - 1 <= tile.q0v);
+      uint32_t mw[2], cls[2];  // this thread's two 32-key chunks: [kb + 64 half + 32 c, + 32)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int base = kb + 64 * half + 32 * c;
+        mw[c] = full ? 0xffffffffu
+                     : (span_bits(-base, e_past - base) | span_bits(tile.ppad - base, e_trunk - base) |
+                        span_bits(own - base, qv + 1 - base));
+        cls[c] = full ? 2u
+                      : (__all_sync(0xffffffffu, mw[c] == 0xffffffffu)
+                             ? 2u
+                             : (__any_sync(0xffffffffu, mw[c] != 0u) ? 1u : 0u));
+      }
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
+        report(p.status, kTimeoutMma);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = tmem + lane_base + (j & 1) * 128;
+      uint32_t x[32], y[32];
+      tmem_ld16x2_x32<64>(sa, x);
+      tmem_ld16x2_x32<64>(sa + 32, y);
+      tmem_wait_ld_regs(x);
+      tmem_wait_ld_regs(y);
+      float mx = -INFINITY;
+      chunk_prep_u(x, mw[0], cls[0], mx);
+      chunk_prep_u(y, mw[1], cls[1], mx);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float m_new = fmaxf(m, mx * sl2);
+      bool rescale = false;
+      float alpha = 1.f;
+      if (m_new != -INFINITY) {
+        if (m == -INFINITY) {
+          m = m_new;  // nothing accumulated yet for this row: O row and l are zero
+        } else if (m_new > m + 8.f) {
+          alpha = fast_exp2(m - m_new);
+          m = m_new;
+          rescale = true;
+        }
+      }
+      const float mu = m == -INFINITY ? 0.f : m;
+      float sum = 0.f;
+      {
+        uint32_t pk[16];
+        chunk_p_u(x, cls[0], sl2, mu, sum, pk);
+        tmem_st16x2_x16<32>(sa, pk);  // keys [64 half, +32) -> P columns [32 half, +16)
+        chunk_p_u(y, cls[1], sl2, mu, sum, pk);
+        tmem_st16x2_x16<32>(sa + 16, pk);
+      }
+      l = l * alpha + sum;
+      if (__any_sync(0xffffffffu, rescale) && j > 0) {
+        // O holds sum_{i<j} P_i V_i once PV_{j-1} completes; scale this thread's half of it.
+        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          report(p.status, kTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 2; c += 32) {
+          uint32_t o[32];
+          tmem_ld16x2_x32<D / 2>(o_addr + c, o);
+          tmem_wait_ld_regs(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16x2_x32<D / 2>(o_addr + c, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+    }
+    if (ok && nblk > 0) {
+      const int last = nblk - 1;
+      if (!mbar_wait(&pv_done[last & 1], (last >> 1) & 1)) {
+        report(p.status, kTimeoutMma);
+      } else {
+        tc_fence_after();
+        const float lt = l + __shfl_xor_sync(0xffffffffu, l, 16);
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        // Whole 16-row slabs leave through the warp's shared-memory slots by TMA store (as in the
+        // paired kernel); a segment's ragged last rows are stored per row.
+        const bool slab = r0 + 16 <= tile.nrows;
+        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row) * p.out_row + static_cast<int64_t>(head) * p.out_head;
+#pragma unroll 1
+        for (int c = 0; c < D / 2; c += 32) {
+          uint32_t o[32];
+          tmem_ld16x2_x32<D / 2>(o_addr + c, o);
+          tmem_wait_ld_regs(o);
+          uint32_t pkd[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pkd[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          if (slab) {
+            if (lane == 0) bulk_wait_read<0>();  // the previous stores from these slots have read them
+            __syncwarp();
+            const int r = lane & 15;  // 64-byte swizzle: unit u of row r at u ^ ((r >> 1) & 3)
+            uint4* d4 = reinterpret_cast<uint4*>(slot + r * 64);
+            const int sw = (r >> 1) & 3;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i ^ sw] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&to, wslots, c, head, tile.row0 + r0);
+              tma_store_3d(&to, wslots + C::SLOT_BYTES, D / 2 + c, head, tile.row0 + r0);
+              bulk_commit();
+            }
+            __syncwarp();
+          } else if (valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + half * (D / 2) + c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pkd[4 * i], pkd[4 * i + 1], pkd[4 * i + 2], pkd[4 * i + 3]);
+          }
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all();  // output stores done before the CTA's shared memory goes away
+    tc_fence_before();
+  }
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tpk,
+           const CUtensorMap& tpv, const CUtensorMap& to, const Params& p, int n_tiles, cudaStream_t stream) {
+  static std::atomic<uint64_t> configured{0};
+  DAN_CUDA(smem_limit_once(tree_attention_kernel<D>, Cfg<D>::SMEM, configured));
+  dim3 grid(p.n_heads, n_tiles);
+  tree_attention_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, tpk, tpv, to, p);
+  DAN_CUDA(cudaGetLastError());
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------
+// Paired-head persistent variant. A work item is one 128-row query tile x two query
+// heads that share a KV head (GQA): both heads have the same key blocks and masks, so
+// each K/V tile is loaded once for 2 x 128 query rows. One CTA per SM walks the
+// LPT-ordered items (tile-major, so CTAs running at the same time share K/V in L2) with
+// barrier phases carried across items.
+// Each 128-key block is consumed as two 64-key units, and each head has two 64-column S
+// buffers in TMEM (unit k in buffer k & 1), so the tensor core computes S_h(k + 2) while
+// the softmax warps of head h are still on unit k + 1: a head's softmax never waits for
+// its own PV and QK products. MMA issue order per item of n units:
+//   QK0(0) QK1(0) QK0(1) QK1(1) | PV0(k) QK0(k+2) PV1(k) QK1(k+2) | ... PV0(n-1) PV1(n-1)
+// (the next item's first QK products run while the softmax warps store this item's output).
+// QK_h(k+2) overwrites the buffer that held P_h(k) only after PV_h(k), issued before it
+// by the same thread, has read it (tcgen05 MMAs of one thread run in issue order). A
+// commit arrives only after every earlier MMA of the issuing thread completed, so when a
+// softmax warp sees S_h(k) the product PV_h(k - 2) is in O_h; PV_h(k - 1) may still be
+// running, and the lazy O rescale (rare) waits for it first. Each row's visible keys within a
+// block are three intervals (past, trunk, own branch), turned into a 32-bit mask per thread
+// and unit.
+// Warps: 0 TMA, 1 MMA, 2-9 softmax head 2p, 10-17 softmax head 2p+1 (576 threads), each softmax
+// warp 16 rows with two threads per row (the 16x32bx2 TMEM access shape), so each SM
+// sub-partition holds four softmax warps. The softmax warps are latency-bound rather than
+// issue-bound (issue slots 40% busy with two softmax warps per sub-partition, 56% with four;
+// configuration-2 batch: 128-key units with one thread per row 661, 64-key units 673, two
+// threads per row 766 TFLOP/s). Measured and not kept: bf16 packing of P by integer rounding
+// instead of the conversion instruction (-14%), scalar instead of packed f32x2 arithmetic
+// (-4%), every exponential on the MUFU unit (-3%), S of a whole 128-key block per QK group
+// (N = 128, which the tensor core reads its shared-memory operands for at full rate where
+// N = 64 runs at two thirds) at the cost of the per-unit prefetch (-4.5%).
+// TMEM: S_0 [0,64) [64,128), S_1 [128,192) [192,256) (P of a unit over the first 32
+// columns of its buffer), O_0 [256, 256+D), O_1 [256+D, 256+2D).
+template <int D>
+struct PairCfg {
+  static constexpr int NS = D <= 64 ? 3 : 2;
+  static constexpr int CHUNKS = D / 64;
+  static constexpr int Q_BYTES = CHUNKS * CHUNK;  // one head's 128 query rows
+  static constexpr int KV_BYTES = CHUNKS * CHUNK;
+  // Output staging: per softmax warp two 1 KB slots (16 rows x 32 bf16 columns each, one per
+  // column half), written with the 64-byte swizzle and sent by TMA store.
+  static constexpr int SLOT_BYTES = 16 * 64;
+  static constexpr int SINK_BYTES = 16 * 2 * SLOT_BYTES;
+  // 225.5 KB at D = 128: a second Q buffer (64 KB) does not fit.
+  static constexpr int SMEM_USED = 2 * Q_BYTES + 2 * NS * KV_BYTES + SINK_BYTES + 1024 + 512;
+  static constexpr int SMEM = SMEM_USED < 120 * 1024 ? 120 * 1024 : SMEM_USED;
+  static constexpr int THREADS = 576;
+};
 
 // Shared-memory operand descriptors (128-byte swizzle) as two words: the low word holds the start
 // address and the leading-dimension offset, the high word the 1024-byte stride offset, the
@@ -991,8 +1000,8 @@ static int rows_map(CUtensorMap* m, const void* base, int64_t row_stride, int64_
   return make_tmap(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// Output tiles: 32 columns x 1 head x ``box_rows`` rows per store (32 for the single-head kernel,
-// 16 for the paired one), 64-byte swizzle.
+// Output tiles: 32 columns x 1 head x ``box_rows`` rows per store (16 for both kernels), 64-byte
+// swizzle.
 static int out_map(CUtensorMap* m, const void* base, int64_t row_stride, int64_t head_stride, int heads, int rows,
                    int d, int box_rows) {
   uint64_t dims[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(heads), static_cast<uint64_t>(rows)};
@@ -1051,7 +1060,7 @@ DAN_API int dan_tree_attention(const void* q, int64_t q_row, int64_t q_head, con
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool paired = (n_heads / n_kv_heads) % 2 == 0 && head_dim <= 128;
   CUtensorMap to;
-  if ((rc = attn::out_map(&to, out, out_row, out_head, n_heads, n_rows, head_dim, paired ? 16 : 32))) return rc;
+  if ((rc = attn::out_map(&to, out, out_row, out_head, n_heads, n_rows, head_dim, 16))) return rc;
   if (paired)
     return head_dim == 64 ? attn::launch_pair<64>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s)
                           : attn::launch_pair<128>(tq, tk, tv, tpk, tpv, to, p, n_tiles, s);
