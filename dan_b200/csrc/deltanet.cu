@@ -315,9 +315,8 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {  // l2 norms in place (q also scaled), one row per step per warp
-    const int t = warp * 8 + i;
-    if (t >= nt) break;
+  for (int i = 0; i < 8; ++i) {  // l2 norms in place (q also scaled), a warp's 8 rows interleaved
+    const int t = warp * 8 + i;      // (rows past the chunk are zero and stay zero)
     uint2* qp = reinterpret_cast<uint2*>(&sm.qn[t * LDW + lane * 4]);
     uint2* kp = reinterpret_cast<uint2*>(&sm.kn[t * LDW + lane * 4]);
     const uint2 qw = *qp, kw = *kp;
