@@ -462,6 +462,7 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
   {  // level 2: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32]
     const int r = tid >> 3, cq = (tid & 7) * 4;
     float y[4] = {};
+#pragma unroll 8
     for (int k = 0; k < 32; ++k) {
       const float av = sm.a[(32 + r) * LDF + k];
       const float4 t4 = *reinterpret_cast<const float4*>(&sm.tf[k * LDT + cq]);
@@ -473,6 +474,7 @@ __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
     *reinterpret_cast<float4*>(&ysc[r * LDY + cq]) = make_float4(y[0], y[1], y[2], y[3]);
     __syncthreads();
     float x[4] = {};
+#pragma unroll 8
     for (int k = 0; k < 32; ++k) {
       const float tv = sm.tf[(32 + r) * LDT + 32 + k];
       const float4 y4 = *reinterpret_cast<const float4*>(&ysc[k * LDY + cq]);
