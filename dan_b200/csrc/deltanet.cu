@@ -168,8 +168,8 @@ struct ScanParams {
 constexpr int DK = 128;
 
 // ---------------------------------------------------------------------------------
-// Chunked gated delta rule on the tensor cores (mma.sync m16n8k16, bf16 operands, fp32
-// accumulation). Runs are cut into chunks of CH = 64 tokens. With Γ_t the cumulative log
+// Chunked gated delta rule on the tensor cores (bf16 operands, fp32 accumulation: mma.sync
+// m16n8k16 in the pre-pass, tcgen05 in the chain). Runs are cut into chunks of CH = 64 tokens. With Γ_t the cumulative log
 // decay inside a chunk (γ_t = e^Γ_t), the token recurrence S_t = d_t S_{t-1} + k_t u_t^T,
 // u_t = β_t (v_t - k_t^T d_t S_{t-1}), o_t = q_t^T S_t unrolls over a chunk that starts from
 // state S0 to (the WY form; every decay factor is e^{difference} <= 1)
@@ -179,11 +179,10 @@ constexpr int DK = 128;
 //   S  = γ_C S0 + K^T diag(e^{Γ_C-Γ_t}) U
 // chunk_prep_kernel computes everything that does not depend on S0 for all chunks at once
 // (one CTA per chunk and value head): normalised q and k, gates, P, T (fp32, 16 x 16
-// diagonal blocks by substitution then two merge levels), -W and T'V, into a scratch
-// buffer. chunk_state_kernel then walks each segment's chunks in order (one CTA per value
-// head, 64-column half of the state and segment) doing only U, O and the state update, the
-// next chunk's inputs arriving by cp.async while this one is computed; the 128 x 64 fp32
-// state slice stays in registers for the whole segment.
+// diagonal blocks by substitution then two merge levels), -W, diag(γ) q̂ and T'V, into a
+// scratch buffer. chunk_state_kernel then walks each segment's chunks in order (one CTA per
+// value head and segment) doing only U, O and the state update, with the fp32 state in TMEM
+// for the whole segment (see the chain's own comment below).
 constexpr int CH = 64;
 constexpr int LDW = DK + 8;  // bf16 row stride of 128-wide tiles: 272 B, ldmatrix rows on distinct banks
 constexpr int LDN = CH + 8;  // bf16 row stride of 64-wide tiles
