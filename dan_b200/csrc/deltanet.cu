@@ -8,16 +8,17 @@
 // Tree runs: a segment's trunk runs from its initial state (zeros, or the
 // prefix pool's state slot) after k-1 history rows (zeros, or the pool's conv
 // tail); every branch runs from the trunk's final state, with the trunk's last
-// k-1 rows as conv history. The scan kernel keeps one head's 128 x 128 state
-// in registers (fp32) across the whole segment: it walks the trunk in chunks
-// of 64 tokens, writes the state at the prefix-save cut to the pool, keeps the
-// trunk's final state as a second register copy and forks each branch from it:
-// the state never round-trips to HBM.
+// k-1 rows as conv history. The chain kernel keeps one head's 128 x 128 state
+// in TMEM (fp32) across the whole segment: it walks the trunk in chunks of 64
+// tokens, writes the state at the prefix-save cut to the pool, keeps the
+// trunk's final state as a second TMEM copy and forks each branch from it: the
+// state never round-trips to HBM.
 //
 // Recurrence per token (delta_rule_torch, qwen3_5.py:103-133):
 //   a = exp(g);  S <- a S;  u = beta (v - S^T k);  S <- S + k u^T;  o = S^T q
 // with k, q l2-normalised (eps 1e-6) and q scaled by Dk^-0.5; evaluated per
-// chunk in the WY form on the tensor cores (see chunk_scan_kernel).
+// chunk in the WY form on the tensor cores (chunk_prep_kernel, then
+// chunk_state_kernel, below).
 #include "common.cuh"
 
 #include <type_traits>
