@@ -4,7 +4,8 @@ weights; the oracle runs on the host CPU in fp32 / fp64).
 - configuration 2: one <= 8192-token batch of tree attention at Llama-3-8B heads (32 / 8 x
   128, trunks up to 2048, up to 16 branches) through ``dan_tree_attention`` against the dense
   masked oracle; the bar is BASELINE's "max relative error 2e-2" (max |got - want| over max
-  |want|) and the reference's own assert_close(2e-2, 2e-2) (tests/test_runner.py:55-68);
+  |want|) and the reference's own assert_close(2e-2, 2e-2) (tests/test_runner.py:55-68); and
+  its secondary form, 16 requests in one uncapped batch (~25k tokens), to the same bars;
 - configuration 3: a 2-layer Llama-3-8B-shaped slice (hidden 4096, 32 / 8 x 128 heads, MLP
   14336, vocabulary 128,256) on one batch, against the reference's own outputs
   (``fullsize.json``, made by running dan's Runner in fp32 and in bf16);
@@ -33,16 +34,28 @@ from oracle import weights as OW
 pytestmark = pytest.mark.gpu
 
 
-def _packed(cfg_id, seed, vocab):
+def _packed(cfg_id, seed, vocab, **kw):
     r = Runner.__new__(Runner)
     r.device, r.cache = torch.device("cuda"), None
-    return r.pack(synthetic.batch(cfg_id, seed=seed, vocab=vocab), use_cache=False)
+    return r.pack(synthetic.batch(cfg_id, seed=seed, vocab=vocab, **kw), use_cache=False)
 
 
 def test_cfg2_attention_full_batch(cuda):
     ids, pos, segs, reads, _ = _packed(2, 11, 128256)
+    assert len(ids) > 4096 and max(s.trunk for s in segs) > 512
+    _check_attention_batch(cuda, ids, segs, reads, "cfg2")
+
+
+def test_cfg2b_attention_sixteen_requests_uncapped(cuda):
+    """Configuration 2's secondary form: exactly 16 requests in one batch with no token cap
+    (~25k tokens, ~200 query tiles), the same bars."""
+    ids, pos, segs, reads, _ = _packed(2, 12, 128256, max_tokens=1 << 30, max_requests=16)
+    assert len(segs) == 16 and len(ids) > 16384
+    _check_attention_batch(cuda, ids, segs, reads, "cfg2b")
+
+
+def _check_attention_batch(cuda, ids, segs, reads, name):
     n, h, hkv, d = len(ids), 32, 8, 128
-    assert n > 4096 and max(s.trunk for s in segs) > 512
     g = torch.Generator().manual_seed(2)
     q = torch.randn(n, h, d, generator=g).bfloat16()
     k = torch.randn(n, hkv, d, generator=g).bfloat16()
@@ -58,7 +71,7 @@ def test_cfg2_attention_full_batch(cuda):
                                                     vt[grp:grp + 1], oracle_segs)
     want = want.transpose(0, 1)
     rel = ((got - want).abs().max() / want.abs().max()).item()
-    print(f"cfg2: {n} tokens, {len(segs)} segments, {len(reads)} branches, max relative error {rel:.3e}")
+    print(f"{name}: {n} tokens, {len(segs)} segments, {len(reads)} branches, max relative error {rel:.3e}")
     assert rel <= 2e-2, rel
     torch.testing.assert_close(got, want, atol=2e-2, rtol=2e-2)
 
