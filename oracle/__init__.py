@@ -13,6 +13,9 @@ this package and fails loudly when its CUDA library is missing.
 
 Pinning: the attention, Llama, Qwen3.5 and packing restatements are checked
 against golden vectors produced by running the reference itself
-(``tests/golden/make_golden.py``). The FP8 restatement is parity-unpinned:
-the reference's FP8 path needs a CUDA GPU and has no test of its own.
+(``tests/golden/make_golden.py``). The reference's FP8 path needs a CUDA GPU
+and has no test of its own, so no fixture pins the FP8 restatement here; on
+the GPU box, ``tests/test_gpu_model.py`` runs the reference's own FP8 path
+(its offline install) and checks this restatement against it (3e-2 on
+probabilities).
 """

@@ -9,8 +9,10 @@ Follows the reference's FP8 path:
 - ``y = (xq @ Wq^T) * scale_x[:, None] * scale_w[None, :]`` (+ bias) in fp32, cast to
   the model dtype (``torch._scaled_mm`` with row-wise scales, dan/quant.py:37-42).
 
-PARITY UNPINNED: the reference's FP8 path needs a CUDA GPU and its tests hold
-no FP8 case, so this restatement is checked only by its own definition.
+Pinning: the reference's FP8 path needs a CUDA GPU and its tests hold no FP8
+case, so no CPU fixture exists; on the GPU box ``tests/test_gpu_model.py`` runs
+the reference's own FP8 path (its offline install) and checks this restatement
+against it at the 3e-2 probability bound.
 """
 import torch
 

@@ -69,7 +69,8 @@ def test_without_cache_same_answers(cuda, tiny_dir):
 
 def test_tiny_llama_fp8_matches_fp8_oracle(cuda, tiny_dir):
     """FP8 e4m3 decoder linears (configuration 5's quantisation) vs the FP8 restatement of the
-    reference (oracle.fp8, parity unpinned upstream) at the north-star 3e-2 probability bound."""
+    reference (oracle.fp8, itself checked against the reference's FP8 path in the next test) at
+    the north-star 3e-2 probability bound."""
     from oracle import runner as OR
 
     path, g = tiny_dir
@@ -83,6 +84,41 @@ def test_tiny_llama_fp8_matches_fp8_oracle(cuda, tiny_dir):
         for p, w in zip(pp, ww):
             worst = max(worst, (p - torch.softmax(w.double(), 0).float()).abs().max().item())
     assert worst < 3e-2, worst
+
+
+def test_tiny_llama_fp8_matches_reference_fp8_on_gpu(cuda, tiny_dir, monkeypatch):
+    """FP8 pinned to the reference itself: dan's own Runner(quantization="fp8") from its
+    offline install (torch._scaled_mm with row-wise scales, its varlen attention, eager
+    activation quantisation: quant.py:23-42, fused.py:85-91) on the same GPU, same checkpoint
+    and plans; probabilities within the north-star FP8 bound 3e-2, cold and warm cache."""
+    dan_runner = pytest.importorskip("dan.runner")
+    import dan.fused
+
+    monkeypatch.setattr(dan.fused, "ENABLED", False)  # dan's eager rounding (its CPU / < 512-row path)
+    from oracle import runner as OR
+
+    path, g = tiny_dir
+    ref = dan_runner.Runner(path, "cuda", torch.bfloat16, cache_bytes=2 << 30, quantization="fp8")
+    ours = Runner(path, cuda, quantization="fp8")
+    worst, first = 0.0, None
+    for b in g["batches"]:
+        plans = plans_from_json(b["plans"])
+        want = ref.read_many(plans)
+        first = want if first is None else first
+        _, probs = ours.read_many(plans, probabilities=True)
+        for pp, ww in zip(probs, want):
+            assert len(pp) == len(ww)
+            for p, w in zip(pp, ww):
+                worst = max(worst, (p - torch.softmax(w.double(), 0).float()).abs().max().item())
+        assert ours.cache.hits == ref.cache.hits, b["name"]
+    # the FP8 restatement (oracle.fp8, CPU) against the same reference run, cold batch
+    orc = OR.read_many(weights.random_state(g["config"], g["seed"]), g["config"],
+                       plans_from_json(g["batches"][0]["plans"]), fp8=True)
+    worst_o = max((torch.softmax(a.double(), 0) - torch.softmax(torch.as_tensor(w).double(), 0)).abs().max().item()
+                  for pa, pw in zip(orc, first) for a, w in zip(pa, pw))
+    print(f"fp8 vs dan's own fp8 path on this GPU: max |dp| {worst:.2e}; oracle.fp8 vs it: {worst_o:.2e}")
+    assert worst < 3e-2, worst
+    assert worst_o < 3e-2, worst_o
 
 
 def test_read_stream_matches_read_many(cuda, tiny_dir):
