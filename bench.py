@@ -22,7 +22,9 @@ collective on the data path).
 All ranks draw one seeded stream of batches and deal them so each rank times
 ``steps`` batches with near-equal token totals; ``per_rank`` lists every
 rank's tokens and device time. ``attention_cfg2`` times the tree-attention
-kernel alone on a configuration-2 batch; ``cpu_baseline`` is dan's own CPU
+kernel alone on a configuration-2 batch, before the warm-up steps (at the
+unthrottled clock, as the burst peak is measured; the SM clock read before
+and after it is reported); ``cpu_baseline`` is dan's own CPU
 path on one of the timed batches (configuration 3, one GPU).
 
 ``--impl reference`` runs dan itself: its unmodified ``Runner`` (fp32, all
@@ -327,6 +329,20 @@ def flush_l2(buf):
     buf.add_(1)  # writes 256 MB: more than the 126 MB L2
 
 
+def sm_clock_mhz(index):
+    """The GPU's current SM clock by one NVML query (a read; nothing is set), or None."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            return pynvml.nvmlDeviceGetClockInfo(pynvml.nvmlDeviceGetHandleByIndex(index), pynvml.NVML_CLOCK_SM)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:  # no NVML on this host
+        return None
+
+
 def attention_cfg2(device, hbm_peak, burst_peak, iters=10, seed=0):
     """dan_tree_attention alone on one configuration-2 batch (<= 8192 tokens, Llama-3-8B heads
     32 / 8 x 128, q / k / v ~ N(0, 1) bf16), timed per launch with CUDA events around the launch
@@ -348,12 +364,15 @@ def attention_cfg2(device, hbm_peak, burst_peak, iters=10, seed=0):
     lay = TreeLayout.build(segs, n, device)
     buf = torch.empty(64 << 20, dtype=torch.float32, device=device)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters + 3)]
+    torch.cuda.synchronize()
+    mhz_before = sm_clock_mhz(device.index or 0)
     for s, e in ev:
         flush_l2(buf)
         s.record()
         tree_attention(q, k, v, lay, out=out)
         e.record()
     torch.cuda.synchronize()
+    mhz_after = sm_clock_mhz(device.index or 0)
     ms = [s.elapsed_time(e) for s, e in ev[3:]]
     med = statistics.median(ms)
     tflops = 4 * h * d * lay.pairs / (med * 1e-3) / 1e12
@@ -363,7 +382,9 @@ def attention_cfg2(device, hbm_peak, burst_peak, iters=10, seed=0):
             "achieved": tflops, "peak": burst_peak, "unit": "TFLOP/s", "frac": tflops / burst_peak,
             "peak_kind": "measured burst", "ms_median": med, "ms_min": min(ms), "launches": len(ms),
             "useful_pairs": lay.pairs, "computed_pairs": computed, "useful_frac_of_computed": lay.pairs / computed,
-            "l2": "flushed (256 MB write) before every launch"}
+            "l2": "flushed (256 MB write) before every launch", "sm_mhz_before": mhz_before,
+            "sm_mhz_after": mhz_after,
+            "when": "before the warm-up steps, so at the unthrottled clock the burst peak is measured at"}
 
 
 def fp8_library_peak(device, iters=5):
@@ -419,6 +440,11 @@ def run_dan(args, world, rank, local):
     drawn = synthetic.batches(cid, 1 + args.warmup + world * args.steps, seed=1000, vocab=cfg["vocab_size"])
     if cid == 5:  # the shared 1024-token prefix enters the prefix pool once, as in serving
         runner.read_many(drawn[0][:1])
+    # the configuration-2 attention case runs first, before any step has heated the GPU: the
+    # burst peak it is set against was measured the same way (a kernel alone, unthrottled)
+    attn_case = None
+    if rank == 0 and not args.no_attention_case:
+        attn_case = attention_cfg2(device, *peaks()[:2])
     warm_plans = drawn[1:1 + args.warmup]
     timed_plans = deal(drawn[1 + args.warmup:], world, args.steps)[rank]
     use_cache = cid == 5
@@ -542,8 +568,8 @@ def run_dan(args, world, rank, local):
                                  "unit": "GB/s", "frac": gbs / hbm if hbm else None, "peak_kind": "measured",
                                  "tflops": flops / (sc["ms_total"] * 1e-3) / 1e12,
                                  "share_of_step": sc["ms_total"] / ms}
-    if not args.no_attention_case:
-        line["attention_cfg2"] = attention_cfg2(device, hbm, pk_burst)
+    if attn_case is not None:
+        line["attention_cfg2"] = attn_case
     if world == 1 and not args.no_cpu and cid == 3:
         line["cpu_baseline"] = cpu_baseline_sample(timed_plans[0])
     print(json.dumps(line), flush=True)
