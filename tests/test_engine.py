@@ -12,9 +12,12 @@ import threading
 import pytest
 import torch
 
-from dan.readout import answers
-from dan_b200.engine import AsyncEngine, Overloaded
-from dan_b200.plan import Branch, ReadPlan
+pytest.importorskip("dan.readout")  # dan's own answer formatting, installed beside this package
+
+from dan.readout import answers  # noqa: E402
+
+from dan_b200.engine import AsyncEngine, Overloaded  # noqa: E402
+from dan_b200.plan import Branch, ReadPlan  # noqa: E402
 
 
 class Spec:
