@@ -13,7 +13,8 @@ are larger than L2 where the configuration's are.
 - attention: tree attention of one configuration-2 batch (32/8 heads x 128).
 - attention256: the same kernel family at 16/4 heads x 256 on a configuration-4 batch.
 - deltanet: causal conv + gated delta scan of one configuration-4 batch
-  (Qwen3.5-4B-style: 16 key / 32 value heads x 128).
+  (Qwen3.5-4B-style: 16 key / 32 value heads x 128); deltanet_whole: the same with the scan
+  launched unsplit.
 - norm: RMSNorm of [7089, 4096].
 - gemm8: the four projections in e4m3 at M = 3400 (configuration 5).
 - readout, gate, gnorm, conv, quant, kvstore: the HBM-bound kernels at benchmark sizes.
@@ -100,7 +101,7 @@ def attention256(iters):
             "tflops": 4 * 16 * 256 * lay.pairs / ms / 1e9}
 
 
-def deltanet(iters):
+def deltanet(iters, split=True):
     from dan_b200.qwen3_5 import RecurrentLayout
 
     dev = torch.device("cuda")
@@ -115,6 +116,7 @@ def deltanet(iters):
     a_log = torch.log(1 + 15 * torch.rand(hv, device=dev, generator=g))
     dt = 0.5 + 0.5 * torch.rand(hv, device=dev, generator=g)
     rl = RecurrentLayout.build(segs, n, 3, dev)
+    lead = rl.choose_lead(hv) if split else (0, 0)
     conv = torch.empty(n, C, dtype=torch.bfloat16, device=dev)
     out = torch.empty(n, hv * dv, dtype=torch.bfloat16, device=dev)
     kd = hk * dk
@@ -127,10 +129,16 @@ def deltanet(iters):
                   _lib.ptr(conv[:, 2 * kd:]), C, _lib.ptr(ba[:, :hv]), _lib.ptr(ba[:, hv:]), 2 * hv,
                   _lib.ptr(a_log), _lib.ptr(dt), _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches),
                   _lib.ptr(rl.chunks), rl.n_chunks, None, 0, _lib.ptr(out), hv * dv, hk, hv, dk, dv,
-                  float(dk ** -0.5), _lib.ptr(scratch), scratch.numel(), _lib.ptr(_lib.status_word(dev)), _lib.stream())
+                  float(dk ** -0.5), _lib.ptr(scratch), scratch.numel(), *lead, _lib.ptr(_lib.status_word(dev)),
+                  _lib.stream())
 
     ms = _time(run, iters)
-    return {"tokens": n, "segments": rl.n_segs, "chunks": rl.n_chunks, "ms": ms}
+    return {"tokens": n, "segments": rl.n_segs, "chunks": rl.n_chunks, "lead": list(lead), "ms": ms}
+
+
+def deltanet_whole(iters):
+    """The deltanet case with the scan launched unsplit (both kernels over everything)."""
+    return deltanet(iters, split=False)
 
 
 def fp8peak(iters):
@@ -350,7 +358,7 @@ def kvstore(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "gemm8", "attention", "attention256", "deltanet", "conv", "gnorm", "norm", "quant", "readout",
+    ap.add_argument("case", choices=["gemm", "gemm8", "attention", "attention256", "deltanet", "deltanet_whole", "conv", "gnorm", "norm", "quant", "readout",
                                      "gate", "kvstore", "fp8peak"])
     ap.add_argument("--iters", type=int, default=4)
     a = ap.parse_args()

@@ -41,7 +41,7 @@ SIGNATURES = {
     "dan_causal_conv": ([P, I64, P, I64, P, P, P, I64, I32, I32, P], I32),
     "dan_gather_rows": ([P, I64, P, I64, P, I32, P, I64, I32, P], I32),
     "dan_gated_delta_scan": ([P, P, P, I64, P, P, I64, P, P, P, I32, P, P, I32, P, I64, P, I64, I32, I32, I32, I32,
-                              F32, P, I64, P, P], I32),
+                              F32, P, I64, I32, I32, P, P], I32),
     "dan_gated_delta_scratch_bytes": ([I32, I32, I32], I64),
     "dan_gated_rms_norm": ([P, I64, P, I64, P, F32, P, I64, I32, I32, I32, P], I32),
     "dan_delta_rule_scan": ([P, P, P, I64, P, I64, P, I64, P, I32, P, P, I32, P, I64, P, I64, I32, I32, I32, I32, F32,

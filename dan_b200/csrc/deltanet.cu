@@ -21,6 +21,7 @@
 // chunk_state_kernel, below).
 #include "common.cuh"
 
+#include <mutex>
 #include <type_traits>
 
 namespace dan {
@@ -164,6 +165,10 @@ struct ScanParams {
   int n_chunks;
   uint8_t* scratch;   // chunk records (REC_V per chunk and value head, REC_K per chunk and key head)
   int32_t* status;
+  // Launch subsets (zero for a launch over everything): the pre-pass's chunk of block x is
+  // chunk_base + x, then moved past [skip_at, skip_at + skip_len); the chain's segment of
+  // block y is seg_base + y.
+  int chunk_base, skip_at, skip_len, seg_base;
 };
 
 constexpr int DK = 128;
@@ -263,7 +268,9 @@ __device__ __forceinline__ void copy_out_sw128(uint8_t* dst, const __nv_bfloat16
 __global__ void __launch_bounds__(256, 2) chunk_prep_kernel(ScanParams p) {
   extern __shared__ __align__(16) uint8_t dsm[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(dsm);
-  const int ci = blockIdx.x, h = blockIdx.y;
+  const int h = blockIdx.y;
+  int ci = p.chunk_base + static_cast<int>(blockIdx.x);
+  if (ci >= p.skip_at) ci += p.skip_len;
   const int row0 = p.chunks[2 * ci], nt = p.chunks[2 * ci + 1];
   const int per = p.hv / p.hk, kh = h / per;
   const bool owner = h % per == 0;  // writes this key head's q̂ and k̂
@@ -580,7 +587,7 @@ __global__ void __launch_bounds__(160, 1) chunk_state_kernel(const __grid_consta
   extern __shared__ uint8_t dsm_raw[];
   ChainSmem& sm = *reinterpret_cast<ChainSmem*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   const int h = blockIdx.x, kh = h / (p.hv / p.hk);
-  const Seg sg = p.segs[blockIdx.y];
+  const Seg sg = p.segs[p.seg_base + static_cast<int>(blockIdx.y)];
   const int warp = warp_id(), lane = lane_id();
   int total = (sg.cut + CH - 1) / CH + (sg.trunk_len - sg.cut + CH - 1) / CH;
   for (int bi = 0; bi < sg.n_branches; ++bi) total += (p.branches[4 * (sg.branch0 + bi) + 1] + CH - 1) / CH;
@@ -998,9 +1005,40 @@ DAN_API int64_t dan_gated_delta_scratch_bytes(int n_chunks, int hk, int hv) {
   return static_cast<int64_t>(n_chunks) * (hv * delta::REC_V + hk * delta::REC_K);
 }
 
-// Checks and launches of the two scan kernels (prep over all chunks, then the chains).
-static int scan_launch(const delta::ScanParams& p, int n_segs, int dk, int dv, int64_t scratch_bytes,
-                       void* stream) {
+// A second stream per device for the split launch below, created on first use and kept for
+// the life of the process.
+static cudaError_t side_stream(cudaStream_t* out) {
+  static std::mutex mu;
+  static cudaStream_t streams[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!streams[dev]) {
+    e = cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking);
+    if (e != cudaSuccess) return e;
+  }
+  *out = streams[dev];
+  return cudaSuccess;
+}
+
+// Checks and launches of the two scan kernels: the pre-pass over the chunks, then the chains.
+// With ``lead_chunks`` > 0 (the caller's estimate that the leading segment's chain outlasts the
+// rest of the pre-pass; its chunks are [lead_chunk0, lead_chunk0 + lead_chunks)), the launch is
+// split so that chain starts as soon as its own chunks are prepared, while the pre-pass of the
+// other segments runs beside it on a second stream:
+//   stream: prep(lead chunks) -> event A -> chain(segment 0) ---------------------> wait S
+//   side:                        wait A -> prep(the other chunks) -> chains(other segments) -> event S
+// The leading chain follows its pre-pass in stream order, so its CTAs (one SM each: their shared
+// memory fills it) are placed on the SMs the pre-pass leaves empty before the other pre-pass
+// CTAs, which wait for the event, fill the rest. Every kernel sees exactly the data it would in
+// the unsplit order (a chain reads only its own segment's chunk records, and the records of
+// different chunks are disjoint), so results are bit-identical; work queued on ``stream`` after
+// the call waits for both streams' kernels.
+static int scan_launch(const delta::ScanParams& p0, int n_segs, int dk, int dv, int64_t scratch_bytes,
+                       int lead_chunk0, int lead_chunks, void* stream) {
+  delta::ScanParams p = p0;
   DAN_REQUIRE(dk == delta::DK && dv == delta::DK, "gated_delta_scan: needs dk = dv = 128 (got %d, %d)", dk, dv);
   DAN_REQUIRE(p.ld_qkv % 8 == 0 && p.ld_out % 8 == 0, "gated_delta_scan: strides must be multiples of 8");
   DAN_REQUIRE(reinterpret_cast<uintptr_t>(p.q) % 16 == 0 && reinterpret_cast<uintptr_t>(p.k) % 16 == 0 &&
@@ -1014,13 +1052,14 @@ static int scan_launch(const delta::ScanParams& p, int n_segs, int dk, int dv, i
               "gated_delta_scan: scratch needs %lld bytes, 16-byte aligned (got %lld)",
               static_cast<long long>(dan_gated_delta_scratch_bytes(p.n_chunks, p.hk, p.hv)),
               static_cast<long long>(scratch_bytes));
+  DAN_REQUIRE(lead_chunks == 0 || (lead_chunk0 >= 0 && lead_chunks > 0 && lead_chunk0 + lead_chunks <= p.n_chunks),
+              "gated_delta_scan: lead chunks [%d, %d) outside the %d chunks", lead_chunk0, lead_chunk0 + lead_chunks,
+              p.n_chunks);
   if (!n_segs || !p.n_chunks) return 0;
   static std::atomic<uint64_t> prep_conf{0}, state_conf{0};
   DAN_CUDA(smem_limit_once(delta::chunk_prep_kernel, static_cast<int>(sizeof(delta::PrepSmem)), prep_conf));
   DAN_CUDA(smem_limit_once(delta::chunk_state_kernel, delta::CHAIN_SMEM, state_conf));
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  delta::chunk_prep_kernel<<<dim3(p.n_chunks, p.hv), 256, sizeof(delta::PrepSmem), st>>>(p);
-  DAN_CUDA(cudaGetLastError());
   // O of whole chunks by TMA store: [rows][hv][128] bf16, box one head x 64 rows, no swizzle (the
   // rows the kernel stores always exist; the row extent only bounds the map)
   CUtensorMap tout;
@@ -1032,8 +1071,48 @@ static int scan_launch(const delta::ScanParams& p, int n_segs, int dk, int dv, i
                        CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
-  delta::chunk_state_kernel<<<dim3(p.hv, n_segs), 160, delta::CHAIN_SMEM, st>>>(tout, p);
-  DAN_CUDA(cudaGetLastError());
+  const size_t prep_smem = sizeof(delta::PrepSmem);
+  if (lead_chunks == 0 || lead_chunks == p.n_chunks || n_segs < 2) {
+    delta::chunk_prep_kernel<<<dim3(p.n_chunks, p.hv), 256, prep_smem, st>>>(p);
+    DAN_CUDA(cudaGetLastError());
+    delta::chunk_state_kernel<<<dim3(p.hv, n_segs), 160, delta::CHAIN_SMEM, st>>>(tout, p);
+    DAN_CUDA(cudaGetLastError());
+    return 0;
+  }
+  cudaStream_t side = nullptr;
+  DAN_CUDA(side_stream(&side));
+  cudaEvent_t ev_a = nullptr, ev_s = nullptr;
+  DAN_CUDA(cudaEventCreateWithFlags(&ev_a, cudaEventDisableTiming));
+  cudaError_t e = cudaEventCreateWithFlags(&ev_s, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    cudaEventDestroy(ev_a);
+    return ::dan::fail(-5, "cudaEventCreateWithFlags failed: %s", cudaGetErrorString(e));
+  }
+  delta::ScanParams pa = p, pb = p, ps = p;
+  pa.chunk_base = lead_chunk0;                                // the leading segment's chunks
+  pb.skip_at = lead_chunk0, pb.skip_len = lead_chunks;        // every other chunk
+  ps.seg_base = 1;                                            // segments 1 .. n_segs - 1
+  delta::chunk_prep_kernel<<<dim3(lead_chunks, p.hv), 256, prep_smem, st>>>(pa);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaEventRecord(ev_a, st);
+  if (e == cudaSuccess) {
+    delta::chunk_state_kernel<<<dim3(p.hv, 1), 160, delta::CHAIN_SMEM, st>>>(tout, p);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(side, ev_a, 0);
+  if (e == cudaSuccess) {
+    delta::chunk_prep_kernel<<<dim3(p.n_chunks - lead_chunks, p.hv), 256, prep_smem, side>>>(pb);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    delta::chunk_state_kernel<<<dim3(p.hv, n_segs - 1), 160, delta::CHAIN_SMEM, side>>>(tout, ps);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(ev_s, side);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ev_s, 0);
+  cudaEventDestroy(ev_a);  // released once the work that records or waits on them has run
+  cudaEventDestroy(ev_s);
+  if (e != cudaSuccess) return ::dan::fail(-5, "gated_delta_scan split launch failed: %s", cudaGetErrorString(e));
   return 0;
 }
 
@@ -1066,8 +1145,8 @@ DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, in
                                  const void* a, int64_t ld_ba, const float* a_log, const float* dt_bias,
                                  const int* segs, int n_segs, const int* branches, const int* chunks, int n_chunks,
                                  float* state_pool, int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv,
-                                 int dk, int dv, float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status,
-                                 void* stream) {
+                                 int dk, int dv, float q_scale, void* scratch, int64_t scratch_bytes, int lead_chunk0,
+                                 int lead_chunks, int32_t* status, void* stream) {
   DAN_REQUIRE(a_log != nullptr && dt_bias != nullptr, "gated_delta_scan: A_log and dt_bias are required");
   delta::ScanParams p = scan_params(q, k, v, ld_qkv, segs, branches, chunks, n_chunks, state_pool, slot_stride, out,
                                     ld_out, hk, hv, q_scale, scratch, status);
@@ -1076,7 +1155,7 @@ DAN_API int dan_gated_delta_scan(const void* q, const void* k, const void* v, in
   p.ld_ba = ld_ba;
   p.a_log = a_log;
   p.dt_bias = dt_bias;
-  return scan_launch(p, n_segs, dk, dv, scratch_bytes, stream);
+  return scan_launch(p, n_segs, dk, dv, scratch_bytes, lead_chunk0, lead_chunks, stream);
 }
 
 DAN_API int dan_delta_rule_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* beta,
@@ -1091,7 +1170,7 @@ DAN_API int dan_delta_rule_scan(const void* q, const void* k, const void* v, int
   p.ld_ba = ld_beta;
   p.g_given = g;
   p.ld_g = ld_g;
-  return scan_launch(p, n_segs, dk, dv, scratch_bytes, stream);
+  return scan_launch(p, n_segs, dk, dv, scratch_bytes, 0, 0, stream);
 }
 
 DAN_API int dan_gated_rms_norm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* w, float eps,

@@ -105,6 +105,24 @@ class RecurrentLayout:
     n_rows: int
     n_chunks: int = 0
     n_state_io: int = 0  # fp32 states the scan reads (cached pasts) plus writes (save cuts)
+    lead: tuple = (0, 0)  # (first chunk, chunks) of segment 0 when the scan should split, else (0, 0)
+
+    # The scan's split launch (segment 0's chain beside the other segments' pre-pass) pays when
+    # that chain outlasts the rest of the pre-pass: measured on B200 at 128-wide heads, a chain
+    # takes ~2.3 us per chunk and the pre-pass ~0.054 us per chunk and value head, slowed by
+    # ~30% while it shares the GPU with the chain. So split when the leading segment has at
+    # least MIN_LEAD chunks and leads the next one by more than the share of the rest of the
+    # pre-pass the overlap costs.
+    MIN_LEAD = 8
+
+    @staticmethod
+    def split_lead(counts, hv):
+        """counts: chunks per segment, longest segment first. (index of its first chunk is the
+        caller's) -> whether the scan should split off segment 0."""
+        if len(counts) < 2 or counts[0] < RecurrentLayout.MIN_LEAD:
+            return False
+        rest = sum(counts) - counts[0]
+        return 2.3 * (counts[0] - max(counts[1:])) > 0.3 * 0.054 * hv * rest
 
     @classmethod
     def build(cls, segments, n_rows, k1, device):
@@ -140,8 +158,11 @@ class RecurrentLayout:
             b0 = len(brs)
             for a, b in s.branches:
                 brs.append((a, b - a, cut_runs(a, b - a), 0))
-            segs.append((s.start, s.trunk, cut, slot, save_slot, b0, len(s.branches), chunk0))
+            # the record, then (not uploaded) its chunk count: a segment's chunks are contiguous
+            segs.append((s.start, s.trunk, cut, slot, save_slot, b0, len(s.branches), chunk0, len(chunks) - chunk0))
         segs.sort(key=lambda r: -(r[1] + sum(brs[r[5] + i][1] for i in range(r[6]))))
+        seg_chunks = [(r[7], r[8]) for r in segs]  # (first chunk, chunks), longest segment first
+        segs = [r[:8] for r in segs]
         dev = torch.device(device)
 
         def up(a, shape):
@@ -149,9 +170,17 @@ class RecurrentLayout:
             return t.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else t
 
         io = sum((r[3] >= 0) + (r[4] >= 0) for r in segs)
-        return cls(up(prev[:max(n_rows, 1)], (-1, k1)), up(segs, (-1, 8)), up(brs or [(0, 0, 0, 0)], (-1, 4)),
-                   up(chunks or [(0, 0)], (-1, 2)), up(tail or [0], (-1,)), tail_dst, len(segs), n_rows,
-                   len(chunks), int(io))
+        lay = cls(up(prev[:max(n_rows, 1)], (-1, k1)), up(segs, (-1, 8)), up(brs or [(0, 0, 0, 0)], (-1, 4)),
+                  up(chunks or [(0, 0)], (-1, 2)), up(tail or [0], (-1,)), tail_dst, len(segs), n_rows,
+                  len(chunks), int(io))
+        lay.seg_chunks = seg_chunks
+        return lay
+
+    def choose_lead(self, hv):
+        """Set ``lead`` for a layer with ``hv`` value heads (``split_lead``'s rule)."""
+        counts = [c for _, c in self.seg_chunks]
+        self.lead = self.seg_chunks[0] if self.split_lead(counts, hv) else (0, 0)
+        return self.lead
 
 
 class Qwen35ForReads:
@@ -233,6 +262,7 @@ class Qwen35ForReads:
         lay = getattr(segments, "recurrent", None)
         if lay is None or lay.n_rows != n:
             lay = RecurrentLayout.build(segments, n, self.kconv - 1, self.device)
+            lay.choose_lead(self.hv)
             segments.recurrent = lay
         return lay
 
@@ -286,7 +316,7 @@ class Qwen35ForReads:
                   C, _lib.ptr(b), _lib.ptr(a), P.stride(0), _lib.ptr(L["a_log"]), _lib.ptr(L["dt_bias"]),
                   _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), _lib.ptr(rl.chunks), rl.n_chunks,
                   _lib.ptr(state), state.stride(0) if state is not None else 0, _lib.ptr(out), vd, self.hk, hv,
-                  self.dk, self.dv, float(self.dk ** -0.5), _lib.ptr(scratch), scratch.numel(),
+                  self.dk, self.dv, float(self.dk ** -0.5), _lib.ptr(scratch), scratch.numel(), *rl.lead,
                   _lib.ptr(_lib.status_word(self.device)), _lib.stream(),
                   work=n * (2 * kd + vd) * 2 + n * hv * 2 * 2 + n * vd * 2 + rl.n_state_io * hv * self.dk * self.dv * 4)
         y = torch.empty_like(out)

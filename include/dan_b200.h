@@ -172,12 +172,18 @@ int dan_gather_rows(const void* src, int64_t ld_src, const void* hist, int64_t l
  * out: [rows, hv * 128] bf16, 16-byte aligned, ld_out a multiple of 8 (whole chunks of it are
  * written by TMA store). scratch: caller-owned device buffer of
  * dan_gated_delta_scratch_bytes(n_chunks, hk, hv) bytes (16-byte aligned) for the per-chunk
- * intermediates; it is fully rewritten by each call. */
+ * intermediates; it is fully rewritten by each call.
+ * lead_chunk0 / lead_chunks: 0 / 0, or the chunk range [lead_chunk0, lead_chunk0 + lead_chunks)
+ * of segment 0 (segs[0]), when the caller expects that segment's chain to outlast the pre-pass
+ * of all the others: the call then runs that chain beside the other segments' pre-pass (a second
+ * stream of the library's, forked from and joined back into ``stream`` by events); results are
+ * identical either way. */
 int dan_gated_delta_scan(const void* q, const void* k, const void* v, int64_t ld_qkv, const void* b, const void* a,
                          int64_t ld_ba, const float* a_log, const float* dt_bias, const int* segs, int n_segs,
                          const int* branches, const int* chunks, int n_chunks, float* state_pool,
                          int64_t slot_stride, void* out, int64_t ld_out, int hk, int hv, int dk, int dv,
-                         float q_scale, void* scratch, int64_t scratch_bytes, int32_t* status, void* stream);
+                         float q_scale, void* scratch, int64_t scratch_bytes, int lead_chunk0, int lead_chunks,
+                         int32_t* status, void* stream);
 /* Bytes of scratch dan_gated_delta_scan needs for n_chunks chunks (59136 per chunk and value head
  * plus 16384 per chunk and key head). */
 int64_t dan_gated_delta_scratch_bytes(int n_chunks, int hk, int hv);

@@ -42,8 +42,9 @@ def test_tiny_hybrid_matches_reference(cuda, hybrid_dir):
     assert worst_l < 5e-2, worst_l
 
 
-def _scan_case(cuda, hk, hv, seg_shapes, seed=0):
-    """Conv + scan over a packed batch (no pasts) vs the oracle; q/k/v from random pre-conv rows."""
+def _scan_case(cuda, hk, hv, seg_shapes, seed=0, lead=None, oracle=True):
+    """Conv + scan over a packed batch (no pasts) vs the oracle; q/k/v from random pre-conv rows.
+    ``lead``: the scan's split range (default: the layout's own choice)."""
     from dan_b200.attention import Batch, segment
     from dan_b200.qwen3_5 import RecurrentLayout
 
@@ -62,6 +63,7 @@ def _scan_case(cuda, hk, hv, seg_shapes, seed=0):
     a_log = torch.log(1 + 15 * torch.rand(hv, generator=gen))
     dt_bias = 0.5 + 0.5 * torch.rand(hv, generator=gen)
     rl = RecurrentLayout.build(segs, n, 3, cuda)
+    lead = rl.choose_lead(hv) if lead is None else lead
     # every device buffer is held in a variable until the kernels ran: a temporary passed as
     # ``_lib.ptr(t.to(cuda))`` would be freed (and its memory reused) before the launch
     pre_d, conv = pre.to(cuda), torch.empty(n, C, dtype=torch.bfloat16, device=cuda)
@@ -75,8 +77,10 @@ def _scan_case(cuda, hk, hv, seg_shapes, seed=0):
               C, _lib.ptr(ba_d[:, :hv]), _lib.ptr(ba_d[:, hv:]), 2 * hv, _lib.ptr(a_log_d), _lib.ptr(dt_d),
               _lib.ptr(rl.segs), rl.n_segs, _lib.ptr(rl.branches), _lib.ptr(rl.chunks), rl.n_chunks, None, 0,
               _lib.ptr(out), hv * dv, hk, hv, dk, dv, float(dk ** -0.5), _lib.ptr(scratch), scratch.numel(),
-              _lib.ptr(_lib.status_word(cuda)), _lib.stream())
+              *lead, _lib.ptr(_lib.status_word(cuda)), _lib.stream())
     torch.cuda.synchronize()
+    if not oracle:
+        return out.float().cpu().view(n, hv, dv), None
     # oracle: same tree runs, token by token, from the same bf16 inputs
     w = conv_w[:, None, :].float()
     b, a = ba[:, :hv].float(), ba[:, hv:].float()
@@ -123,6 +127,22 @@ def test_long_chunk_chain_vs_oracle(cuda):
     recurrence: the chunked form must not drift over a long chain."""
     got, want = _scan_case(cuda, 1, 2, [(1500, [40, 64]), (64, [1])], seed=3)
     err = (got - want).abs().max().item() / want.abs().max().item()
+    assert err < 2e-2, err
+
+
+def test_split_scan_matches_unsplit_and_oracle(cuda):
+    """A batch whose first segment's chain dominates (1000-token trunk) beside two short ones, at
+    configuration-4 head counts: the layout splits the scan (that chain beside the other
+    segments' pre-pass, on a second stream), and the outputs are bit-identical to the unsplit
+    launch and within the oracle bar."""
+    from dan_b200.qwen3_5 import RecurrentLayout
+
+    shapes = [(1000, [40, 50]), (200, [30]), (100, [20])]
+    assert RecurrentLayout.split_lead([18, 5, 3], 32) and not RecurrentLayout.split_lead([6, 5], 32)
+    split, want = _scan_case(cuda, 16, 32, shapes, seed=5)
+    whole, _ = _scan_case(cuda, 16, 32, shapes, seed=5, lead=(0, 0), oracle=False)
+    assert torch.equal(split, whole)
+    err = (split - want).abs().max().item() / want.abs().max().item()
     assert err < 2e-2, err
 
 
