@@ -198,6 +198,24 @@ def test_recurrent_layout_chunks_follow_each_segments_runs():
                 c += 1
     assert sorted(seen) == list(range(rl.n_chunks))  # every chunk belongs to exactly one run
     assert recs[[r[1] for r in recs].index(300)][2] == 130
+    # each segment's (first chunk, chunk count), longest first, for the scan's split launch
+    assert [c0 for c0, _ in rl.seg_chunks] == [int(r[7]) for r in recs]
+    assert sum(k for _, k in rl.seg_chunks) == rl.n_chunks
+
+
+def test_scan_split_rule():
+    """The scan splits off segment 0's chain only when it leads the next segment by more than
+    the overlap costs the rest of the pre-pass, and never for one segment or a short lead."""
+    from dan_b200.qwen3_5 import RecurrentLayout
+
+    rule = RecurrentLayout.split_lead
+    assert rule([66, 40, 15], 32) and rule([18, 5, 3], 32)
+    assert not rule([64, 63], 32) and not rule([43, 38, 34, 21], 32)
+    assert not rule([100], 32) and not rule([7, 1], 32)
+    assert rule([61, 50], 2) and not rule([61, 50], 64)  # more value heads: a longer pre-pass to hide
+    segs, n, _ = build_segments([(1000, [40], 0), (100, [20], 0), (70, [], 0)], shuffle_pages=False)
+    rl = RecurrentLayout.build(segs, n, 3, "cpu")
+    assert rl.lead == (0, 0) and rl.choose_lead(32) == rl.seg_chunks[0] and rl.lead[1] == 17
 
 
 def test_prefix_cache_contract():
